@@ -1,0 +1,151 @@
+"""ctypes binding of the C ABI in ``include/cxlsparse.h``.
+
+The shared library is built in-tree by ``cxlsparse_b200/build.py``. There is
+no fallback: if the library is missing or cannot be loaded, every entry point
+raises. Raw device pointers come from torch tensors (``data_ptr()``) and the
+stream from ``torch.cuda.current_stream().cuda_stream``.
+"""
+
+import ctypes
+from pathlib import Path
+
+LIBRARY = Path(__file__).resolve().parent / "libcxlsparse_b200.so"
+
+# Status codes (enum cxs_status).
+OK, ERR_INVALID, ERR_CUDA, ERR_CAPACITY, ERR_REGISTRATION, ERR_UNSUPPORTED = range(6)
+# Device error word bits.
+DEVICE_ERR_READY_TIMEOUT, DEVICE_ERR_COPY_TIMEOUT, DEVICE_ERR_BAD_BLOCK = 1, 2, 4
+ORDER_PHYSICAL, ORDER_DEPTH, ORDER_DEPTH_SHARED = 0, 1, 2
+READ_ORDERS = {
+    "physical": ORDER_PHYSICAL,
+    "consumption_depth": ORDER_DEPTH,
+    "consumption_depth_shared": ORDER_DEPTH_SHARED,
+}
+
+c_i32, c_i64, c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
+
+
+class CxsError(RuntimeError):
+    """A C-ABI call returned a failure status."""
+
+    def __init__(self, status, message):
+        super().__init__(f"cxlsparse_b200 status {status}: {message}")
+        self.status = status
+
+
+class CapacityError(CxsError):
+    """Capacity refusal raised before any device work was enqueued."""
+
+
+class PlanGeometry(ctypes.Structure):
+    _fields_ = [(name, c_i32) for name in (
+        "queries", "heads", "width", "block_size", "map_blocks", "per_head",
+        "sort_extent", "hot", "max_history", "regions", "page_size",
+        "consumer_ctas", "read_order", "private_plan")] + [("pool_tokens", c_i64)]
+
+
+PLAN_BUFFER_FIELDS = (
+    "blocks", "positions", "desc", "bases", "tags", "locs", "host_locs", "hot_data",
+    "mapping", "insert_keys", "active_keys", "active_counts", "required", "frequencies",
+    "stats", "address", "hbm", "valid", "starts", "flags", "slots", "ioids", "ranks",
+    "missing", "all_ids", "all_counts", "row_positions", "region_counts", "row_depth",
+    "first_depth", "near_consumers", "chosen", "private_required",
+    "private_occurrences", "canonical",
+)
+
+
+class PlanBuffers(ctypes.Structure):
+    _fields_ = [(name, c_vp) for name in PLAN_BUFFER_FIELDS]
+
+
+class AttendGeometry(ctypes.Structure):
+    _fields_ = [(name, c_i32) for name in (
+        "queries", "heads", "width", "block_size", "physical", "window", "window_len",
+        "gate")] + [("window_start", c_i64), ("spin_limit", c_i64)]
+
+
+ATTEND_BUFFER_FIELDS = (
+    "query", "kv", "all_ids", "all_counts", "row_positions", "starts", "valid", "flags",
+    "ioids", "missing", "address", "sources", "kinds", "ready", "control", "error",
+    "window_kv", "compressed", "gates", "out",
+)
+
+
+class AttendBuffers(ctypes.Structure):
+    _fields_ = [(name, c_vp) for name in ATTEND_BUFFER_FIELDS]
+
+
+_lib = None
+
+
+def lib():
+    """Load the in-tree library once; raise if it is absent (no CPU fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIBRARY.exists():
+            raise ImportError(
+                f"{LIBRARY.name} is not built; run `python -m cxlsparse_b200.build` "
+                "(the NSA transport has no CPU fallback)")
+        handle = ctypes.CDLL(str(LIBRARY))
+        sigs = {
+            "cxs_abi_version": (c_i32, []),
+            "cxs_last_error": (ctypes.c_char_p, []),
+            "cxs_pool_create": (c_i32, [ctypes.c_size_t, c_i32, c_i32,
+                                        ctypes.POINTER(c_vp), ctypes.POINTER(c_i32)]),
+            "cxs_pool_destroy": (c_i32, [c_vp, ctypes.c_size_t]),
+            "cxs_pool_register": (c_i32, [c_vp, ctypes.c_size_t]),
+            "cxs_pool_unregister": (c_i32, [c_vp]),
+            "cxs_device_numa_node": (c_i32, [c_i32]),
+            "cxs_pool_write": (c_i32, [c_vp, c_vp, c_i64, c_vp, c_i32, c_i32, c_vp]),
+            "cxs_plan_check": (c_i32, [ctypes.POINTER(PlanGeometry)]),
+            "cxs_plan": (c_i32, [ctypes.POINTER(PlanGeometry), ctypes.POINTER(PlanBuffers),
+                                 c_vp]),
+            "cxs_plan_commit_hot": (c_i32, [ctypes.POINTER(PlanGeometry),
+                                            ctypes.POINTER(PlanBuffers), c_vp, c_vp, c_vp,
+                                            c_vp]),
+            "cxs_fetch_attend": (c_i32, [ctypes.POINTER(AttendGeometry),
+                                         ctypes.POINTER(AttendBuffers), c_vp]),
+            "cxs_attend_capacity": (c_i32, [c_i32, ctypes.POINTER(c_i32)]),
+            "cxs_compressed_select": (c_i32, [c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_i32,
+                                              c_i32, c_i64, c_vp, c_vp, c_vp, c_vp]),
+            "cxs_block_summaries": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
+        }
+        for name, (restype, argtypes) in sigs.items():
+            fn = getattr(handle, name)
+            fn.restype, fn.argtypes = restype, argtypes
+        if handle.cxs_abi_version() != 1:
+            raise ImportError("cxlsparse_b200 ABI version mismatch")
+        _lib = handle
+    return _lib
+
+
+def check(status):
+    """Raise the matching exception for a non-zero status."""
+    if status == OK:
+        return
+    message = lib().cxs_last_error().decode(errors="replace")
+    if status == ERR_CAPACITY:
+        raise CapacityError(status, message)
+    if status == ERR_INVALID:
+        raise ValueError(f"cxlsparse_b200: {message}")
+    raise CxsError(status, message)
+
+
+def ptr(tensor):
+    """Device address of a tensor, or None for a missing optional buffer."""
+    return None if tensor is None else tensor.data_ptr()
+
+
+def stream_handle(device=None):
+    import torch
+
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def exported_symbols():
+    """Names the header declares (used by the CPU symbol test)."""
+    return ("cxs_abi_version", "cxs_last_error", "cxs_pool_create", "cxs_pool_destroy",
+            "cxs_pool_register", "cxs_pool_unregister", "cxs_device_numa_node",
+            "cxs_pool_write", "cxs_plan_check", "cxs_plan", "cxs_plan_commit_hot",
+            "cxs_fetch_attend", "cxs_attend_capacity", "cxs_compressed_select",
+            "cxs_block_summaries")

@@ -1,0 +1,836 @@
+// Device-side fetch planner for the NSA GR selected-block path.
+//
+// Deduplicating plan: planning/active.py:21-500, 670-907 (reference).
+// Query-private plan: planning/query_private.py:29-216, 258-457.
+// Occurrence rows: planning/occurrences.py:7-35.
+// Consumption-depth read order: planning/dependencies.py:37-300.
+//
+// Every launch only enqueues work on the caller's stream (graph-capturable),
+// uses fixed-size caller buffers and never downloads data to the host.
+#include <cub/block/block_radix_sort.cuh>
+#include <cub/block/block_reduce.cuh>
+#include <cub/block/block_scan.cuh>
+
+#include "cxs_common.cuh"
+
+using cxs::kInt32Max;
+using cxs::kTokenBytes;
+using cxs_host::set_error;
+
+namespace {
+
+constexpr int kNearWindow = 4;  // planning/dependencies.py:14
+constexpr int kMaxMapBlocks = 1 << 18;  // bitmap compaction limit (32 KiB of shared memory)
+constexpr int kMaxPhysical = 16384;     // single-CTA publish sort limit
+constexpr int kMaxHot = 4096;           // shared-memory hot hash / hot sort limit
+
+struct Geo {
+  int Q, H, W, BS, MAP, CAP, SORT, HOT, MAXH, REGIONS, PAGE, CONSUMERS, ORDER, PRIVATE;
+  int HASH, P, R;
+  long long POOL;
+};
+
+__device__ __forceinline__ bool occurrence_valid(int block, int pos, int total, const Geo& g) {
+  return pos >= 0 && block >= 0 && block < g.MAP && (long long)block * g.BS <= pos &&
+         (long long)block * g.BS < total;
+}
+
+// ------------------------------------------------------------------ reset ---
+// Scratch fills (active.py:21-53) plus clearing the mapping entries named by
+// this request (active.py:56-77). No read-after-write dependency inside.
+__global__ void reset_kernel(Geo g, cxs_plan_buffers b, int max_depth) {
+  long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  long long stride = (long long)gridDim.x * blockDim.x;
+  long long hc = (long long)g.H * g.CAP;
+  long long hs = (long long)g.H * g.SORT;
+  long long rw = (long long)g.R * g.W;
+  for (long long i = tid; i < hc; i += stride) {
+    b.required[i] = 0;
+    b.insert_keys[i] = kInt32Max;
+    if (g.PRIVATE) b.private_required[i] = 0;
+  }
+  for (long long i = tid; i < hs; i += stride) {
+    b.frequencies[i] = 0;
+    if (g.PRIVATE) b.canonical[i] = kInt32Max;
+  }
+  for (long long i = tid; i < rw; i += stride) b.all_ids[i] = -1;
+  for (long long i = tid; i < g.R; i += stride) b.all_counts[i] = 0;
+  for (long long i = tid; i < g.P; i += stride) {
+    b.ioids[i] = -1;
+    b.ranks[i] = -1;
+    b.first_depth[i] = max_depth;
+    b.near_consumers[i] = 0;
+  }
+  for (long long i = tid; i < g.H; i += stride) b.active_counts[i] = 0;
+  for (long long i = tid; i < (long long)g.H * 7; i += stride) b.stats[i] = 0;
+  for (long long i = tid; i < g.REGIONS; i += stride) b.region_counts[i] = 0;
+  if (tid == 0) b.missing[0] = 0;
+  if (!g.PRIVATE) {
+    // Clear mapping entries of every valid selection and set the sentinel.
+    for (long long i = tid; i < (long long)g.Q * g.H * g.W; i += stride) {
+      int q = (int)(i / ((long long)g.H * g.W));
+      int h = (int)((i / g.W) % g.H);
+      int block = b.blocks[i];
+      int pos = b.positions[q];
+      int total = (int)(b.desc[h * 5 + 1] + b.desc[h * 5 + 4]);
+      if (occurrence_valid(block, pos, total, g)) b.mapping[(long long)h * (g.MAP + 1) + block] = -1;
+    }
+    for (long long i = tid; i < g.H; i += stride)
+      b.mapping[i * (g.MAP + 1) + g.MAP] = -2;
+  }
+}
+
+// ------------------------------------------------------------ dedup insert ---
+// First CAS winner of (head, block) claims a compact slot (active.py:80-114).
+__global__ void insert_kernel(Geo g, cxs_plan_buffers b) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  int lane = threadIdx.x % 32;
+  if (warp >= g.Q * g.H) return;
+  int q = warp / g.H, h = warp % g.H;
+  int pos = b.positions[q];
+  int total = (int)(b.desc[h * 5 + 1] + b.desc[h * 5 + 4]);
+  int errors = 0;
+  for (int i0 = 0; i0 < g.W; i0 += 32) {
+    int i = i0 + lane;
+    if (i >= g.W) continue;
+    int block = b.blocks[(long long)warp * g.W + i];
+    bool valid = occurrence_valid(block, pos, total, g);
+    if (valid) {
+      int prev = atomicCAS(&b.mapping[(long long)h * (g.MAP + 1) + block], -1, -2);
+      if (prev == -1) {
+        int compact = atomicAdd(&b.active_counts[h], 1);
+        if (compact < g.CAP) b.insert_keys[(long long)h * g.CAP + compact] = block;
+        else ++errors;
+      }
+    } else if (block >= 0 && pos >= 0) {
+      ++errors;
+    }
+  }
+  errors = cxs::warp_sum(errors);
+  if (lane == 0 && errors) atomicAdd(&b.stats[h * 7 + 6], errors);
+}
+
+// --------------------------------------------------- sorted compaction ---
+// Compact index = rank of the block among the head's active keys, i.e. the
+// sorted-key layout of active.py:117-131, 440-446, built from a bitmap.
+__global__ void compact_kernel(Geo g, cxs_plan_buffers b) {
+  extern __shared__ uint32_t bits[];
+  int h = blockIdx.x;
+  int words = (g.MAP + 31) / 32;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) bits[w] = 0;
+  __syncthreads();
+  int count = min(b.active_counts[h], g.CAP);
+  for (int i = threadIdx.x; i < count; i += blockDim.x) {
+    int block = b.insert_keys[(long long)h * g.CAP + i];
+    atomicOr(&bits[block >> 5], 1u << (block & 31));
+  }
+  __syncthreads();
+  // Each thread owns a contiguous run of words; exclusive scan of popcounts.
+  int per = (words + blockDim.x - 1) / blockDim.x;
+  int begin = threadIdx.x * per, end = min(words, begin + per);
+  int local = 0;
+  for (int w = begin; w < end; ++w) local += __popc(bits[w]);
+  typedef cub::BlockScan<int, 1024> Scan;
+  __shared__ typename Scan::TempStorage scan;
+  int offset;
+  Scan(scan).ExclusiveSum(local, offset);
+  for (int w = begin; w < end; ++w) {
+    uint32_t word = bits[w];
+    while (word) {
+      int bit = __ffs(word) - 1;
+      word &= word - 1;
+      int block = w * 32 + bit;
+      b.active_keys[(long long)h * g.CAP + offset] = block;
+      b.mapping[(long long)h * (g.MAP + 1) + block] = offset;
+      ++offset;
+    }
+  }
+  for (int c = count + threadIdx.x; c < g.CAP; c += blockDim.x)
+    b.active_keys[(long long)h * g.CAP + c] = kInt32Max;
+}
+
+// -------------------------------------------------------------- references ---
+// required = max causal prefix; per-token frequencies of historical tokens;
+// stats[4] old refs / stats[5] local refs (active.py:168-206).
+__global__ void references_kernel(Geo g, cxs_plan_buffers b) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  int lane = threadIdx.x % 32;
+  if (warp >= g.Q * g.H) return;
+  int q = warp / g.H, h = warp % g.H;
+  int pos = b.positions[q];
+  int old = (int)b.desc[h * 5 + 1];
+  int history = (int)b.desc[h * 5 + 2];
+  int total = old + (int)b.desc[h * 5 + 4];
+  int old_refs = 0, local_refs = 0;
+  for (int i = 0; i < g.W; ++i) {
+    int block = b.blocks[(long long)warp * g.W + i];
+    if (!occurrence_valid(block, pos, total, g)) continue;
+    int compact = b.mapping[(long long)h * (g.MAP + 1) + block];
+    if (compact < 0 || compact >= g.CAP) continue;
+    int start = block * g.BS;
+    int req = min(g.BS, min(pos + 1, total) - start);
+    if (lane == 0) {
+      atomicMax(&b.required[(long long)h * g.CAP + compact], req);
+      int olds = min(max(old - start, 0), req);
+      old_refs += olds;
+      local_refs += req - olds;
+    }
+    int historical = min(max(history - start, 0), req);
+    int32_t* freq = b.frequencies + (long long)h * g.SORT + (long long)compact * g.BS;
+    for (int o = lane; o < historical; o += 32) atomicAdd(&freq[o], 1);
+  }
+  if (lane == 0) {
+    if (old_refs) atomicAdd(&b.stats[h * 7 + 4], old_refs);
+    if (local_refs) atomicAdd(&b.stats[h * 7 + 5], local_refs);
+  }
+}
+
+// ------------------------------------------------------ source resolution ---
+// Per compact block: current suffix KV, hot replica or backing-pool slot for
+// each required token (active.py:134-165 hot hash, 209-295 addresses).
+__device__ __forceinline__ uint32_t hash_slot(int token, int mask) {
+  return ((uint32_t)token * 2654435761u) & (uint32_t)mask;
+}
+
+__global__ void addresses_kernel(Geo g, cxs_plan_buffers b) {
+  extern __shared__ int hash_mem[];
+  int* hkeys = hash_mem;
+  int* hvals = hash_mem + g.HASH;
+  int h = blockIdx.y;
+  int row = (int)b.desc[h * 5];
+  int old = (int)b.desc[h * 5 + 1];
+  long long pointer = b.desc[h * 5 + 3];
+  for (int i = threadIdx.x; i < g.HASH; i += blockDim.x) hkeys[i] = -1;
+  __syncthreads();
+  const int32_t* tags = b.tags + (long long)row * (g.HOT + 1);
+  const int32_t* locs = b.locs + (long long)row * (g.HOT + 1);
+  for (int i = threadIdx.x; i < g.HOT; i += blockDim.x) {
+    int token = tags[i];
+    if (token < 0 || token >= old) continue;
+    uint32_t s = hash_slot(token, g.HASH - 1);
+    for (int probe = 0; probe < g.HASH; ++probe) {
+      int prev = atomicCAS(&hkeys[s], -1, token);
+      if (prev == -1) {
+        hvals[s] = locs[i];
+        break;
+      }
+      if (prev == token) break;  // duplicate tag: keep the first location
+      s = (s + 1) & (g.HASH - 1);
+    }
+  }
+  __syncthreads();
+  int warps = blockDim.x / 32;
+  int lane = threadIdx.x % 32;
+  int c = blockIdx.x * warps + threadIdx.x / 32;
+  if (c >= g.CAP) return;
+  long long p = (long long)h * g.CAP + c;
+  bool active = c < b.active_counts[h];
+  int block = active ? b.active_keys[p] : -1;
+  int req = active ? b.required[p] : 0;
+  const char* hot_data = static_cast<const char*>(b.hot_data);
+  int n_valid = 0, n_prev = 0, n_hot = 0, n_ext = 0, n_err = 0;
+  int region_mask_counts[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int o = lane; o < g.BS; o += 32) {
+    long long token = (long long)block * g.BS + o;
+    bool valid = active && o < req;
+    bool previous = valid && token < old;
+    int location = -1;
+    if (previous) {
+      uint32_t s = hash_slot((int)token, g.HASH - 1);
+      for (int probe = 0; probe < g.HASH; ++probe) {
+        int key = hkeys[s];
+        if (key == (int)token) {
+          location = hvals[s];
+          break;
+        }
+        if (key == -1) break;
+        s = (s + 1) & (g.HASH - 1);
+      }
+    }
+    bool external = previous && location < 0;
+    long long source = -1;
+    if (external && token >= 0 && token < g.MAXH) source = b.host_locs[(long long)row * g.MAXH + token];
+    bool error = external && (source < 0 || source >= g.POOL);
+    bool safe = external && !error;
+    long long hbm = 0;
+    if (valid && !external)
+      hbm = previous ? (long long)(hot_data + (long long)location * kTokenBytes) - 0
+                     : pointer + (token - old) * kTokenBytes;
+    long long address = hbm;
+    if (safe) {
+      long long page = source / g.PAGE;
+      int region = (int)(page % g.REGIONS);
+      long long local = (page / g.REGIONS) * g.PAGE + source % g.PAGE;
+      address = b.bases[region] + local * kTokenBytes;
+      if (region < 8) region_mask_counts[region] += 1;
+      else atomicAdd(&b.region_counts[region], 1);
+    }
+    long long idx = p * g.BS + o;
+    b.address[idx] = address;
+    b.hbm[idx] = hbm;
+    b.slots[idx] = safe ? source : -1;
+    n_valid += valid;
+    n_prev += previous;
+    n_hot += previous && !external;
+    n_ext += external;
+    n_err += error;
+  }
+  n_valid = cxs::warp_sum(n_valid);
+  n_prev = cxs::warp_sum(n_prev);
+  n_hot = cxs::warp_sum(n_hot);
+  n_ext = cxs::warp_sum(n_ext);
+  n_err = cxs::warp_sum(n_err);
+  int regions8 = min(g.REGIONS, 8);
+  for (int r = 0; r < regions8; ++r) {
+    int cnt = cxs::warp_sum(region_mask_counts[r]);
+    if (lane == 0 && cnt) atomicAdd(&b.region_counts[r], cnt);
+  }
+  if (lane == 0) {
+    b.valid[p] = (active && n_err == 0) ? req : 0;
+    b.starts[p] = active ? block * g.BS : 0;
+    b.flags[p] = n_ext > 0;
+    if (n_valid) atomicAdd(&b.stats[h * 7 + 0], n_valid);
+    if (n_prev) atomicAdd(&b.stats[h * 7 + 1], n_prev);
+    if (n_hot) atomicAdd(&b.stats[h * 7 + 2], n_hot);
+    if (n_ext) atomicAdd(&b.stats[h * 7 + 3], n_ext);
+    if (n_err) atomicAdd(&b.stats[h * 7 + 6], n_err);
+  }
+}
+
+// ------------------------------------------------------------- occurrences ---
+// Original-order occurrence rows with duplicates kept (occurrences.py:7-35).
+__global__ void occurrences_kernel(Geo g, cxs_plan_buffers b) {
+  int r = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  int lane = threadIdx.x % 32;
+  if (r >= g.R) return;
+  int q = r / g.H, h = r % g.H;
+  int pos = b.positions[q];
+  bool head_ok = b.stats[h * 7 + 6] == 0;
+  int count = 0;
+  for (int i0 = 0; i0 < g.W; i0 += 32) {
+    int i = i0 + lane;
+    bool valid = false;
+    int physical = 0;
+    if (i < g.W && head_ok) {
+      if (!g.PRIVATE) {
+        int block = b.blocks[(long long)r * g.W + i];
+        valid = pos >= 0 && block >= 0 && block < g.MAP && (long long)block * g.BS <= pos;
+        if (valid) {
+          int compact = b.mapping[(long long)h * (g.MAP + 1) + block];
+          valid = compact >= 0 && compact < g.CAP;
+          physical = h * g.CAP + compact;
+        }
+      } else {
+        int origin = b.private_occurrences[(long long)r * g.W + i];
+        valid = origin >= 0;
+        if (valid) {
+          int compact = b.mapping[(long long)h * g.CAP + origin];
+          valid = compact >= 0;
+          physical = h * g.CAP + compact;
+        }
+      }
+    }
+    unsigned mask = __ballot_sync(0xffffffffu, valid);
+    if (valid) b.all_ids[(long long)r * g.W + count + __popc(mask & ((1u << lane) - 1))] = physical;
+    count += __popc(mask);
+  }
+  if (lane == 0) {
+    b.all_counts[r] = count;
+    b.row_positions[r] = pos;
+  }
+}
+
+// ------------------------------------------------------ consumption depth ---
+// Depth of each row along its consumer's serial row stream, counting resident
+// steps; first depth at which each missing block is consumed
+// (dependencies.py:47-75).
+__global__ void depth_kernel(Geo g, cxs_plan_buffers b) {
+  int r = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  int lane = threadIdx.x % 32;
+  if (r >= g.R) return;
+  int consumers = g.CONSUMERS;
+  int depth = 0;
+  for (int prev = r % consumers + lane * consumers; prev < r; prev += 32 * consumers)
+    if (b.row_positions[prev] >= 0) depth += b.all_counts[prev];
+  depth = cxs::warp_sum(depth);
+  if (lane == 0) b.row_depth[r] = depth;
+  if (b.row_positions[r] < 0) return;
+  int count = min(g.W, b.all_counts[r]);
+  for (int col = lane; col < count; col += 32) {
+    int block = b.all_ids[(long long)r * g.W + col];
+    if (block >= 0 && block < g.P && b.flags[block]) atomicMin(&b.first_depth[block], depth + col);
+  }
+}
+
+// Distinct rows consuming a block within NEAR_WINDOW steps of its first depth
+// (dependencies.py:78-112).
+__global__ void near_kernel(Geo g, cxs_plan_buffers b) {
+  int r = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  int lane = threadIdx.x % 32;
+  if (r >= g.R || b.row_positions[r] < 0) return;
+  int count = min(g.W, b.all_counts[r]);
+  int depth0 = b.row_depth[r];
+  const int32_t* ids = b.all_ids + (long long)r * g.W;
+  for (int col = lane; col < count; col += 32) {
+    int block = ids[col];
+    if (block < 0 || block >= g.P || !b.flags[block]) continue;
+    int first = b.first_depth[block];
+    int depth = depth0 + col;
+    if (depth < first || depth >= first + kNearWindow) continue;
+    bool unique = true;
+    for (int back = 1; back < kNearWindow; ++back)
+      if (col >= back && ids[col - back] == block) unique = false;
+    if (unique) atomicAdd(&b.near_consumers[block], 1);
+  }
+}
+
+// ----------------------------------------------------------------- publish ---
+// Stable IOIDs/Ranks: missing blocks by (first depth, -near, block); physical
+// order is the special case of a zero depth (dependencies.py:115-191,
+// active.py:298-305). One CTA, CUB block radix sort on unique 64-bit keys.
+template <int ITEMS>
+__global__ void __launch_bounds__(1024) publish_kernel(Geo g, cxs_plan_buffers b,
+                                                       unsigned long long bound, int end_bit) {
+  typedef cub::BlockRadixSort<unsigned long long, 1024, ITEMS> Sort;
+  typedef cub::BlockReduce<int, 1024> Reduce;
+  extern __shared__ __align__(16) unsigned char sort_mem[];
+  auto& temp = *reinterpret_cast<typename Sort::TempStorage*>(sort_mem);
+  __shared__ typename Reduce::TempStorage reduce;
+  __shared__ int total_missing;
+  unsigned long long keys[ITEMS];
+  int missing = 0;
+  const unsigned long long P = (unsigned long long)g.P;
+  const unsigned long long rows = (unsigned long long)g.R;
+#pragma unroll
+  for (int k = 0; k < ITEMS; ++k) {
+    int block = threadIdx.x * ITEMS + k;
+    if (block < g.P) {
+      bool miss = b.flags[block] != 0;
+      missing += miss;
+      if (!miss) {
+        keys[k] = bound + (unsigned long long)block;
+      } else if (g.ORDER == CXS_ORDER_PHYSICAL) {
+        keys[k] = (unsigned long long)block;
+      } else {
+        unsigned long long first = (unsigned long long)b.first_depth[block];
+        unsigned long long near =
+            g.ORDER == CXS_ORDER_DEPTH_SHARED ? (unsigned long long)b.near_consumers[block] : 0ull;
+        keys[k] = (first * (rows + 1) + rows - near) * P + (unsigned long long)block;
+      }
+    } else {
+      keys[k] = ~0ull;  // padding sorts last
+    }
+  }
+  int total = Reduce(reduce).Sum(missing);
+  if (threadIdx.x == 0) {
+    total_missing = total;
+    b.missing[0] = total;
+  }
+  Sort(temp).SortBlockedToStriped(keys, 0, end_bit);
+  __syncthreads();
+  int count = total_missing;
+#pragma unroll
+  for (int k = 0; k < ITEMS; ++k) {
+    int rank = k * 1024 + threadIdx.x;  // striped arrangement
+    if (rank < count) {
+      int block = (int)(keys[k] % P);
+      b.ioids[rank] = block;
+      b.ranks[block] = rank;
+    }
+  }
+}
+
+// --------------------------------------------------------------- hot top-k ---
+// Top-`hot` indices of a head's frequency table by (frequency desc, index asc)
+// (active.py:449-500; stable argsort fallback active.py:884-888): radix-select
+// the threshold frequency, keep every larger one and the lowest-index ties,
+// then sort the `hot` winners.
+template <int ITEMS>
+__global__ void __launch_bounds__(1024) hot_select_kernel(Geo g, cxs_plan_buffers b) {
+  typedef cub::BlockRadixSort<unsigned long long, 1024, ITEMS> Sort;
+  typedef cub::BlockScan<int, 1024> Scan;
+  extern __shared__ __align__(16) unsigned char sort_mem[];
+  auto& temp = *reinterpret_cast<typename Sort::TempStorage*>(sort_mem);
+  __shared__ typename Scan::TempStorage scan;
+  __shared__ int hist[256];
+  __shared__ unsigned int prefix_s, mask_s;
+  __shared__ int remaining_s, chosen_count, eq_taken;
+  __shared__ unsigned long long cand[kMaxHot];
+  int h = blockIdx.x;
+  const int32_t* freq = b.frequencies + (long long)h * g.SORT;
+  int n = g.SORT;
+  if (threadIdx.x == 0) {
+    prefix_s = 0;
+    mask_s = 0;
+    remaining_s = g.HOT;
+    chosen_count = 0;
+    eq_taken = 0;
+  }
+  __syncthreads();
+  // Radix select over the 31-bit frequency, most significant byte first.
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    unsigned int prefix = prefix_s, mask = mask_s;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      unsigned int f = (unsigned int)freq[i];
+      if ((f & mask) == prefix) atomicAdd(&hist[(f >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int remaining = remaining_s;
+      int digit = 255;
+      for (; digit > 0; --digit) {
+        if (hist[digit] >= remaining) break;
+        remaining -= hist[digit];
+      }
+      prefix_s = prefix | ((unsigned int)digit << shift);
+      mask_s = mask | (255u << shift);
+      remaining_s = remaining;
+    }
+    __syncthreads();
+  }
+  unsigned int threshold = prefix_s;
+  int need_eq = remaining_s;  // ties at the threshold, lowest indices first
+  // Gather: every frequency above the threshold, plus the first ties in index order.
+  for (int base = 0; base < n; base += blockDim.x) {
+    int i = base + threadIdx.x;
+    unsigned int f = i < n ? (unsigned int)freq[i] : 0u;
+    bool greater = i < n && f > threshold;
+    bool equal = i < n && f == threshold;
+    if (greater) {
+      int slot = atomicAdd(&chosen_count, 1);
+      cand[slot] = ((unsigned long long)(0x7FFFFFFFu - f) << 32) | (unsigned int)i;
+    }
+    int eq_prefix, eq_total;
+    Scan(scan).ExclusiveSum((int)equal, eq_prefix, eq_total);
+    int taken = eq_taken;
+    if (equal && taken + eq_prefix < need_eq) {
+      int slot = atomicAdd(&chosen_count, 1);
+      cand[slot] = ((unsigned long long)(0x7FFFFFFFu - f) << 32) | (unsigned int)i;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) eq_taken = taken + eq_total;
+    __syncthreads();
+  }
+  unsigned long long keys[ITEMS];
+#pragma unroll
+  for (int k = 0; k < ITEMS; ++k) {
+    int idx = threadIdx.x * ITEMS + k;
+    keys[k] = idx < g.HOT ? cand[idx] : ~0ull;
+  }
+  __syncthreads();
+  Sort(temp).SortBlockedToStriped(keys);
+#pragma unroll
+  for (int k = 0; k < ITEMS; ++k) {
+    int rank = k * 1024 + threadIdx.x;
+    if (rank < g.HOT) b.chosen[(long long)h * g.HOT + rank] = (int)(keys[k] & 0xFFFFFFFFull);
+  }
+}
+
+// ------------------------------------------------------ query-private plan ---
+// Per (query, head): first-occurrence ownership, sorted private keys,
+// occurrence origins, absolute-token frequencies with a canonical source
+// (query_private.py:29-105). Requires W <= 32.
+__global__ void private_references_kernel(Geo g, cxs_plan_buffers b) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  int lane = threadIdx.x % 32;
+  if (warp >= g.Q * g.H) return;
+  int q = warp / g.H, h = warp % g.H;
+  int pos = b.positions[q];
+  int old = (int)b.desc[h * 5 + 1];
+  int history = (int)b.desc[h * 5 + 2];
+  int total = old + (int)b.desc[h * 5 + 4];
+  bool in_row = lane < g.W;
+  int block = in_row ? b.blocks[(long long)warp * g.W + lane] : (-1 - lane) - 64;
+  bool valid = in_row && occurrence_valid(block, pos, total, g);
+  unsigned same = __match_any_sync(0xffffffffu, block);
+  bool own = valid && (__ffs(same) - 1) == lane;
+  unsigned own_mask = __ballot_sync(0xffffffffu, own);
+  int n_own = __popc(own_mask);
+  // local rank = number of owned blocks smaller than this lane's block
+  int local = 0;
+  for (int j = 0; j < 32; ++j) {
+    int other = __shfl_sync(0xffffffffu, block, j);
+    if ((own_mask >> j) & 1u) local += other < block;
+  }
+  long long base = (long long)h * g.CAP + (long long)q * g.W;
+  if (own) {
+    b.insert_keys[base + local] = block;
+    b.private_required[base + local] = min(g.BS, min(pos + 1, total) - block * g.BS);
+  }
+  if (in_row && lane >= n_own) {
+    b.insert_keys[base + lane] = kInt32Max;
+    b.private_required[base + lane] = 0;
+  }
+  if (in_row) b.private_occurrences[(long long)warp * g.W + lane] = valid ? q * g.W + local : -1;
+  int old_refs = 0, local_refs = 0, errors = 0;
+  if (in_row && !valid && block >= 0 && pos >= 0) errors = 1;
+  // Frequencies / canonical sources: each valid occurrence, lanes over tokens.
+  for (int i = 0; i < g.W; ++i) {
+    int bi = __shfl_sync(0xffffffffu, block, i);
+    bool vi = __shfl_sync(0xffffffffu, valid, i);
+    int li = __shfl_sync(0xffffffffu, local, i);
+    if (!vi) continue;
+    int start = bi * g.BS;
+    int req = min(g.BS, min(pos + 1, total) - start);
+    if (lane == 0) {
+      int olds = min(max(old - start, 0), req);
+      old_refs += olds;
+      local_refs += req - olds;
+    }
+    int historical = min(max(history - start, 0), req);
+    int origin = q * g.W + li;
+    for (int o = lane; o < historical; o += 32) {
+      long long t = (long long)h * g.SORT + start + o;
+      atomicAdd(&b.frequencies[t], 1);
+      atomicMin(&b.canonical[t], origin * g.BS + o);
+    }
+  }
+  errors = cxs::warp_sum(errors);
+  if (lane == 0) {
+    if (old_refs) atomicAdd(&b.stats[h * 7 + 4], old_refs);
+    if (local_refs) atomicAdd(&b.stats[h * 7 + 5], local_refs);
+    if (errors) atomicAdd(&b.stats[h * 7 + 6], errors);
+  }
+}
+
+// Ordered compaction of nonempty private slots (query_private.py:108-128).
+__global__ void private_compact_kernel(Geo g, cxs_plan_buffers b) {
+  typedef cub::BlockScan<int, 1024> Scan;
+  __shared__ typename Scan::TempStorage scan;
+  __shared__ int running;
+  int h = blockIdx.x;
+  if (threadIdx.x == 0) running = 0;
+  __syncthreads();
+  for (int base = 0; base < g.CAP; base += blockDim.x) {
+    int i = base + threadIdx.x;
+    long long idx = (long long)h * g.CAP + i;
+    int length = i < g.CAP ? b.private_required[idx] : 0;
+    bool valid = length > 0;
+    int prefix, sum;
+    Scan(scan).ExclusiveSum((int)valid, prefix, sum);
+    int rank = running + prefix;
+    if (valid) {
+      b.active_keys[(long long)h * g.CAP + rank] = b.insert_keys[idx];
+      b.required[(long long)h * g.CAP + rank] = length;
+    }
+    if (i < g.CAP) b.mapping[idx] = valid ? rank : -1;
+    __syncthreads();
+    if (threadIdx.x == 0) running += sum;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) b.active_counts[h] = running;
+}
+
+// ------------------------------------------------------------ hot commit ---
+// One warp per (head, hot slot): tag update and 256-byte payload copy from the
+// staging buffer (active.py:410-437; query_private.py:188-216).
+__global__ void commit_kernel(Geo g, cxs_plan_buffers b, const uint4* __restrict__ kv,
+                              int32_t* tags, uint4* data) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  int lane = threadIdx.x % 32;
+  if (warp >= g.H * g.HOT) return;
+  int h = warp / g.HOT, slot = warp % g.HOT;
+  int row = (int)b.desc[h * 5];
+  int ct = b.chosen[(long long)h * g.HOT + slot];
+  bool selected = ct >= 0 && ct < g.SORT && b.frequencies[(long long)h * g.SORT + ct] > 0;
+  int token = -1;
+  long long source = -1;
+  if (selected) {
+    if (!g.PRIVATE) {
+      int compact = ct / g.BS;
+      if (compact < g.CAP) {
+        token = b.active_keys[(long long)h * g.CAP + compact] * g.BS + ct % g.BS;
+        source = ((long long)h * g.CAP + compact) * g.BS + ct % g.BS;
+      } else {
+        selected = false;
+      }
+    } else {
+      token = ct;
+      int original = b.canonical[(long long)h * g.SORT + ct];
+      int compact = b.mapping[(long long)h * g.CAP + original / g.BS];
+      source = ((long long)h * g.CAP + compact) * g.BS + original % g.BS;
+    }
+  }
+  long long index = (long long)row * (g.HOT + 1) + slot;
+  if (lane == 0) tags[index] = selected ? token : -1;
+  if (selected && lane < 16) {
+    int location = b.locs[index];
+    data[(long long)location * 16 + lane] = kv[source * 16 + lane];
+  }
+}
+
+int sort_items(int n) {
+  int items = 1;
+  while (items * 1024 < n) items *= 2;
+  return items;
+}
+
+template <template <int> class K>
+struct Dummy {};
+
+int check_geometry(const cxs_plan_geometry* geo, Geo* out) {
+  if (!geo) return set_error(CXS_ERR_INVALID, "null plan geometry");
+  Geo g{};
+  g.Q = geo->queries;
+  g.H = geo->heads;
+  g.W = geo->width;
+  g.BS = geo->block_size;
+  g.MAP = geo->map_blocks;
+  g.CAP = geo->per_head;
+  g.SORT = geo->sort_extent;
+  g.HOT = geo->hot;
+  g.MAXH = geo->max_history;
+  g.REGIONS = geo->regions;
+  g.PAGE = geo->page_size;
+  g.CONSUMERS = geo->consumer_ctas;
+  g.ORDER = geo->read_order;
+  g.PRIVATE = geo->private_plan;
+  g.POOL = geo->pool_tokens;
+  if (g.Q < 1 || g.H < 1 || g.W < 1 || g.BS < 1 || (g.BS & (g.BS - 1)) || g.MAP < 1 ||
+      g.CAP < 1 || g.HOT < 1 || g.REGIONS < 1 || g.PAGE < 1 || g.CONSUMERS < 1)
+    return set_error(CXS_ERR_INVALID, "nonempty plan geometry and power-of-two BS required");
+  if (g.ORDER < CXS_ORDER_PHYSICAL || g.ORDER > CXS_ORDER_DEPTH_SHARED)
+    return set_error(CXS_ERR_INVALID, "unknown read order %d", g.ORDER);
+  if ((long long)g.MAP * g.BS > kInt32Max)
+    return set_error(CXS_ERR_INVALID, "absolute token addressing must fit int32");
+  if (g.SORT < g.HOT) return set_error(CXS_ERR_INVALID, "sort_extent must cover hot");
+  g.P = g.H * g.CAP;
+  g.R = g.Q * g.H;
+  g.HASH = 1;
+  while (g.HASH < 2 * g.HOT) g.HASH *= 2;
+  if (g.MAP + 1 > kMaxMapBlocks)
+    return set_error(CXS_ERR_CAPACITY, "map_blocks %d exceeds %d", g.MAP, kMaxMapBlocks - 1);
+  if (g.P > kMaxPhysical)
+    return set_error(CXS_ERR_CAPACITY, "physical blocks %d exceed %d", g.P, kMaxPhysical);
+  if (g.HOT > kMaxHot) return set_error(CXS_ERR_CAPACITY, "hot %d exceeds %d", g.HOT, kMaxHot);
+  if (g.PRIVATE && g.W > 32)
+    return set_error(CXS_ERR_CAPACITY, "query-private plan supports width <= 32");
+  if (g.PRIVATE && g.CAP != g.Q * g.W)
+    return set_error(CXS_ERR_INVALID, "query-private per_head must equal queries * width");
+  if (!g.PRIVATE && g.CAP > g.MAP)
+    return set_error(CXS_ERR_INVALID, "per_head cannot exceed map_blocks");
+  *out = g;
+  return CXS_OK;
+}
+
+template <int ITEMS>
+int launch_publish(const Geo& g, const cxs_plan_buffers& b, unsigned long long bound, int end_bit,
+                   cudaStream_t stream) {
+  size_t smem = sizeof(typename cub::BlockRadixSort<unsigned long long, 1024, ITEMS>::TempStorage);
+  CXS_CUDA(cudaFuncSetAttribute(publish_kernel<ITEMS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)smem));
+  publish_kernel<ITEMS><<<1, 1024, smem, stream>>>(g, b, bound, end_bit);
+  CXS_LAUNCH_CHECK("publish_kernel");
+  return CXS_OK;
+}
+
+template <int ITEMS>
+int launch_hot(const Geo& g, const cxs_plan_buffers& b, cudaStream_t stream) {
+  size_t smem = sizeof(typename cub::BlockRadixSort<unsigned long long, 1024, ITEMS>::TempStorage);
+  CXS_CUDA(cudaFuncSetAttribute(hot_select_kernel<ITEMS>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  hot_select_kernel<ITEMS><<<g.H, 1024, smem, stream>>>(g, b);
+  CXS_LAUNCH_CHECK("hot_select_kernel");
+  return CXS_OK;
+}
+
+}  // namespace
+
+extern "C" int cxs_plan_check(const cxs_plan_geometry* geometry) {
+  Geo g;
+  return check_geometry(geometry, &g);
+}
+
+extern "C" int cxs_plan(const cxs_plan_geometry* geometry, const cxs_plan_buffers* buffers,
+                        void* stream_ptr) {
+  Geo g;
+  int status = check_geometry(geometry, &g);
+  if (status != CXS_OK) return status;
+  if (!buffers) return set_error(CXS_ERR_INVALID, "null plan buffers");
+  const cxs_plan_buffers& b = *buffers;
+  if (g.PRIVATE && (!b.private_required || !b.private_occurrences || !b.canonical))
+    return set_error(CXS_ERR_INVALID, "query-private plan buffers missing");
+  cudaStream_t stream = (cudaStream_t)stream_ptr;
+  int max_depth = ((g.R + g.CONSUMERS - 1) / g.CONSUMERS) * g.W;
+  int warps_per_cta = 8;
+  int row_grid = (g.Q * g.H + warps_per_cta - 1) / warps_per_cta;
+  int r_grid = (g.R + warps_per_cta - 1) / warps_per_cta;
+
+  reset_kernel<<<296, 512, 0, stream>>>(g, b, max_depth);
+  CXS_LAUNCH_CHECK("reset_kernel");
+  if (!g.PRIVATE) {
+    insert_kernel<<<row_grid, warps_per_cta * 32, 0, stream>>>(g, b);
+    CXS_LAUNCH_CHECK("insert_kernel");
+    size_t bitmap = (size_t)((g.MAP + 31) / 32) * 4;
+    if (bitmap > 48 * 1024)
+      CXS_CUDA(cudaFuncSetAttribute(compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)bitmap));
+    compact_kernel<<<g.H, 1024, bitmap, stream>>>(g, b);
+    CXS_LAUNCH_CHECK("compact_kernel");
+    references_kernel<<<row_grid, warps_per_cta * 32, 0, stream>>>(g, b);
+    CXS_LAUNCH_CHECK("references_kernel");
+  } else {
+    private_references_kernel<<<row_grid, warps_per_cta * 32, 0, stream>>>(g, b);
+    CXS_LAUNCH_CHECK("private_references_kernel");
+    private_compact_kernel<<<g.H, 1024, 0, stream>>>(g, b);
+    CXS_LAUNCH_CHECK("private_compact_kernel");
+  }
+  {
+    dim3 grid((g.CAP + warps_per_cta - 1) / warps_per_cta, g.H);
+    size_t smem = (size_t)g.HASH * 8;
+    if (smem > 48 * 1024)
+      CXS_CUDA(cudaFuncSetAttribute(addresses_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem));
+    addresses_kernel<<<grid, warps_per_cta * 32, smem, stream>>>(g, b);
+    CXS_LAUNCH_CHECK("addresses_kernel");
+  }
+  occurrences_kernel<<<r_grid, warps_per_cta * 32, 0, stream>>>(g, b);
+  CXS_LAUNCH_CHECK("occurrences_kernel");
+  unsigned long long bound;
+  if (g.ORDER == CXS_ORDER_PHYSICAL) {
+    bound = (unsigned long long)g.P;
+  } else {
+    depth_kernel<<<r_grid, warps_per_cta * 32, 0, stream>>>(g, b);
+    CXS_LAUNCH_CHECK("depth_kernel");
+    if (g.ORDER == CXS_ORDER_DEPTH_SHARED) {
+      near_kernel<<<r_grid, warps_per_cta * 32, 0, stream>>>(g, b);
+      CXS_LAUNCH_CHECK("near_kernel");
+    }
+    bound = ((unsigned long long)(max_depth + 1) * (unsigned long long)(g.R + 1) +
+             (unsigned long long)g.R) *
+            (unsigned long long)g.P;
+  }
+  int end_bit = 1;
+  while (end_bit < 64 && ((bound + (unsigned long long)g.P) >> end_bit)) ++end_bit;
+  switch (sort_items(g.P)) {
+    case 1: status = launch_publish<1>(g, b, bound, end_bit, stream); break;
+    case 2: status = launch_publish<2>(g, b, bound, end_bit, stream); break;
+    case 4: status = launch_publish<4>(g, b, bound, end_bit, stream); break;
+    case 8: status = launch_publish<8>(g, b, bound, end_bit, stream); break;
+    default: status = launch_publish<16>(g, b, bound, end_bit, stream); break;
+  }
+  if (status != CXS_OK) return status;
+  switch (sort_items(g.HOT)) {
+    case 1: status = launch_hot<1>(g, b, stream); break;
+    case 2: status = launch_hot<2>(g, b, stream); break;
+    default: status = launch_hot<4>(g, b, stream); break;
+  }
+  return status;
+}
+
+extern "C" int cxs_plan_commit_hot(const cxs_plan_geometry* geometry,
+                                   const cxs_plan_buffers* buffers, const void* kv, int32_t* tags,
+                                   void* hot_data, void* stream_ptr) {
+  Geo g;
+  int status = check_geometry(geometry, &g);
+  if (status != CXS_OK) return status;
+  if (!buffers || !kv || !tags || !hot_data)
+    return set_error(CXS_ERR_INVALID, "null commit argument");
+  int warps = g.H * g.HOT;
+  commit_kernel<<<(warps + 7) / 8, 256, 0, (cudaStream_t)stream_ptr>>>(
+      g, *buffers, (const uint4*)kv, tags, (uint4*)hot_data);
+  CXS_LAUNCH_CHECK("commit_kernel");
+  return CXS_OK;
+}

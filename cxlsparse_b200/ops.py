@@ -1,0 +1,59 @@
+"""NSA local branches on the device: compressed attention + top-n selection.
+
+Mirrors ``cxl_recsys/models/nsa/ops.py`` / ``fla.py``:
+``compressed_attention_select(query, compressed, positions, total, block_size,
+count)`` returns ``(output [Q, H, G, 64] bf16, blocks [Q, H, width] int32)``
+with width = min(count, ceil(total / block_size)) (fla.py:6-62), and
+``append_compressed`` mean-pools complete blocks (ops.py:62-70). The window
+branch and the gate mix run inside the transport's fetch/attend launch.
+"""
+
+import torch
+
+from . import _lib
+
+
+def compressed_attention_select(query, compressed, positions, total, block_size, count, *,
+                                scores=None):
+    """Compressed-token attention and top-n block ids; ``scores`` optionally
+    receives the [Q, H, C] fp32 block scores the selection was made from."""
+    queries, heads, groups, dim = query.shape
+    if groups != 16 or dim != 64 or query.dtype != torch.bfloat16:
+        raise ValueError("query must be bf16 [Q, H, 16, 64]")
+    if compressed.ndim != 3 or compressed.shape[1:] != (heads, 128):
+        raise ValueError("compressed must be [C, H, 128] (K || V)")
+    query = query.contiguous()
+    compressed = compressed.contiguous()
+    positions = positions.to(torch.int32).contiguous()
+    width = min(count, (total + block_size - 1) // block_size)
+    output = torch.empty_like(query)
+    blocks = torch.empty((queries, heads, width), dtype=torch.int32, device=query.device)
+    if scores is not None and scores.shape != (queries, heads, len(compressed)):
+        raise ValueError("scores must be [Q, H, C] fp32")
+    stream = torch.cuda.current_stream(query.device)
+    _lib.check(_lib.lib().cxs_compressed_select(
+        query.data_ptr(), compressed.data_ptr() if len(compressed) else None, len(compressed),
+        positions.data_ptr(), queries, heads, block_size, count, total, output.data_ptr(),
+        blocks.data_ptr(), _lib.ptr(scores), stream.cuda_stream))
+    return output, blocks
+
+
+def block_summaries(tokens, block_size):
+    """Mean of each complete block of ``tokens`` [n, H, 128] -> [n // BS, H, 128]."""
+    tokens = tokens.contiguous()
+    count = len(tokens) // block_size
+    out = torch.empty((count, *tokens.shape[1:]), dtype=tokens.dtype, device=tokens.device)
+    if count:
+        stream = torch.cuda.current_stream(tokens.device)
+        _lib.check(_lib.lib().cxs_block_summaries(tokens.data_ptr(), len(tokens),
+                                                  tokens.shape[1], block_size, out.data_ptr(),
+                                                  stream.cuda_stream))
+    return out
+
+
+def append_compressed(compressed, tail, current, block_size):
+    """(summaries + new complete blocks of tail||current, new tail) (ops.py:62-70)."""
+    values = torch.cat((tail, current))
+    count = len(values) // block_size
+    added = block_summaries(values[: count * block_size], block_size)
+    return torch.cat((compressed, added)), values[count * block_size:].clone()

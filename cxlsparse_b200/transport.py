@@ -1,0 +1,331 @@
+"""GR selected-block transport: the drop-in for the reference's TMA transport.
+
+Mirrors ``cxl_recsys/models/nsa/transport.py:127-706`` (``GRSelectedTransport``
+with ``consumer_backend="tma"``): ``run(query, blocks, positions, fetches,
+block_size)`` returns ``(output [Q, H, G, 64] bf16, DeferredLayerCounters)``;
+the output is a borrowed view valid until the next call (transport.py:703).
+Workspaces are cached by shape key with an LRU bound and a byte budget
+(transport.py:243-409); plan + fetch/attend can be replayed from a CUDA graph
+(transport.py:624-631); the hot-set commit runs once, outside the graph
+(transport.py:641).
+
+Besides the reference behaviour, ``run`` accepts the NSA window / compressed
+branches and gates (``window=``, ``compressed=``, ``gates=``); the same launch
+then returns the gate-mixed attention output of all three branches
+(models/nsa/model.py:466-473), so the model needs no separate window or mix
+kernels.
+
+All device work goes through ``libcxlsparse_b200.so``; there is no fallback.
+"""
+
+import math
+import time
+from collections import OrderedDict
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .planning import ActivePlanAdapter, QueryPrivatePlanAdapter
+
+QUERY_BUCKETS = (64, 128, 256, 512, 1024, 2048, 4096)
+
+
+class GRWorkspaceLimit(RuntimeError):
+    """Capacity refusal before any plan/IO/hot state has been submitted."""
+
+
+def query_bucket(active_q, buckets=QUERY_BUCKETS):
+    """Smallest bucket holding ``active_q`` rows (models/nsa/dispatch.py:25-33)."""
+    if active_q < 1:
+        raise ValueError("A query bucket requires at least one active row")
+    for capacity in buckets:
+        if active_q <= capacity:
+            return capacity
+    raise GRWorkspaceLimit(f"Query length {active_q} exceeds bucket limit {buckets[-1]}")
+
+
+@dataclass
+class DeferredLayerCounters:
+    """[H, 7] planner statistics resolved at the forward boundary.
+
+    Columns: unique, unique_old, hits, misses, old_refs, local_refs, errors
+    (mempool/device_plan.py:16-42). ``errors`` additionally carries the
+    fetch/attend device error word.
+    """
+
+    statistics: torch.Tensor
+    launches: int
+    backend: str = "host"
+    device_error: torch.Tensor | None = None
+
+    def materialize(self, rows=None):
+        if rows is None:
+            rows = self.statistics.tolist()
+        if any(row[6] for row in rows):
+            raise ValueError(
+                "Top-K must contain causal positions or -1 padding, with bound history slots")
+        if self.device_error is not None:
+            code = int(self.device_error.item())
+            if code:
+                raise RuntimeError(f"NSA fetch/attend device error word {code:#x}")
+        owner = next((i for i, row in enumerate(rows) if row[3]), None)
+        return [
+            dict(hits=r[2], misses=r[3], old_references=r[4],
+                 deduplicated_references=r[4] - r[1], local_tokens=r[5],
+                 planner_calls=int(i == 0),
+                 h2d_transfers=int(i == owner),
+                 fetch_kernel_launches=self.launches if i == 0 else 0)
+            for i, r in enumerate(rows)
+        ]
+
+
+def workspace_estimate(queries, cached, heads, groups, width, bs, *, cross_query_dedup=True):
+    """Host-known conservative bound (transport.py:90-124)."""
+    q = query_bucket(queries)
+    logical = max(64, math.ceil((cached + q) / (64 * bs)) * 64)
+    physical = heads * (min(logical, q * width) if cross_query_dedup else q * width)
+    rows = q * heads
+    return (physical * bs * 384 + 2 * rows * (width + 5) * 4 + rows * groups * 64 * 16
+            + logical * heads * 16 + 4 * 1024**2)
+
+
+class GRSelectedTransport:
+    """Plan, fetch and attend one layer's selected blocks for one user."""
+
+    def __init__(self, cache, *, read_order="consumption_depth", cross_query_dedup=True,
+                 cuda_graphs=False, capacity=8, workspace_bytes=2 * 1024**3,
+                 hot_policy="frequency", spin_limit=1 << 32, query_group=1):
+        if read_order not in _lib.READ_ORDERS:
+            raise ValueError("Invalid NSA read priority configuration")
+        if hot_policy not in ("frequency", "static"):
+            raise ValueError("hot_policy must be 'frequency' or 'static'")
+        if query_group != 1:
+            raise ValueError("Only single-token consumers (query_group=1) are supported")
+        if capacity < 1 or workspace_bytes < 1:
+            raise ValueError("Invalid GR selected resource policy")
+        _lib.lib()  # fail loudly now if the extension is missing
+        self.cache, self.pool = cache, cache.pool
+        self.read_order, self.cross_query_dedup = read_order, cross_query_dedup
+        self.hot_policy, self.spin_limit = hot_policy, spin_limit
+        adapter = ActivePlanAdapter if cross_query_dedup else QueryPrivatePlanAdapter
+        self.active_plan = adapter(cache, read_order=read_order)
+        self.cuda_graphs, self.capacity = cuda_graphs, capacity
+        self.workspace_budget = workspace_bytes
+        self.workspaces = OrderedDict()
+        self.descriptors = OrderedDict()
+        self.workspace_allocations = self.workspace_evictions = 0
+        self.captures = self.replays = 0
+        self.calls = 0
+        self.submitted = False
+        self.last_done = torch.cuda.Event()
+        self.last_stats = {}
+        self._capacity_cache = {}
+
+    # -- reference surface -----------------------------------------------
+    def refusal(self, queries, cached, heads, groups, width, bs):
+        """Reason to refuse before any side effect, else None (transport.py:215-237)."""
+        if not 1 <= queries <= QUERY_BUCKETS[-1]:
+            return "query_bucket_limit"
+        if groups != 16 or bs not in (16, 32, 64):
+            return "geometry"
+        estimate = workspace_estimate(queries, cached, heads, groups, width, bs,
+                                      cross_query_dedup=self.cross_query_dedup)
+        return "workspace_budget" if estimate > self.workspace_budget else None
+
+    def close(self):
+        if self.submitted:
+            self.last_done.synchronize()
+        for w in self.workspaces.values():
+            w.pop("graph", None)
+        self.workspaces.clear()
+
+    @property
+    def graphs(self):
+        return dict(entries=sum("graph" in w for w in self.workspaces.values()),
+                    captures=self.captures, replays=self.replays)
+
+    # -- workspace ---------------------------------------------------------
+    def _attention_warps(self, bs):
+        if bs not in self._capacity_cache:
+            value = _lib.c_i32(0)
+            _lib.check(_lib.lib().cxs_attend_capacity(bs, value))
+            self._capacity_cache[bs] = value.value
+        return self._capacity_cache[bs]
+
+    def _workspace(self, qb, heads, width, fetches, bs, window_shape):
+        logical = max(f["cached_length"] + qb for f in fetches)
+        map_blocks = max(64, math.ceil(logical / (64 * bs)) * 64)
+        key = (qb, heads, width, bs, map_blocks, window_shape)
+        if key in self.workspaces:
+            self.workspaces.move_to_end(key)
+            return self.workspaces[key]
+        estimate = workspace_estimate(qb, max(f["cached_length"] for f in fetches), heads, 16,
+                                      width, bs, cross_query_dedup=self.cross_query_dedup)
+        if estimate > self.workspace_budget:
+            raise GRWorkspaceLimit(
+                f"GR workspace estimate {estimate} exceeds {self.workspace_budget} bytes")
+        resident = sum(w["allocated_bytes"] for w in self.workspaces.values())
+        while self.workspaces and (len(self.workspaces) >= self.capacity
+                                   or resident + estimate > self.workspace_budget):
+            if self.submitted:
+                self.last_done.synchronize()
+            _, old = self.workspaces.popitem(last=False)
+            old.pop("graph", None)
+            resident -= old["allocated_bytes"]
+            self.workspace_evictions += 1
+        rows = qb * heads
+        consumers = min(rows, self._attention_warps(bs))
+        device = self.cache.data.device
+        w = self.active_plan.allocate(qb, heads, width, fetches, bs, map_blocks=map_blocks,
+                                      consumer_ctas=consumers, device=device)
+        p = w["physical"]
+
+        def empty(shape, dtype=torch.int32):
+            return torch.empty(shape, dtype=dtype, device=device)
+
+        w.update(
+            query=torch.zeros((qb, heads, 16, 64), dtype=torch.bfloat16, device=device),
+            blocks=torch.full((qb, heads, width), -1, dtype=torch.int32, device=device),
+            in_positions=torch.full((qb,), -1, dtype=torch.int32, device=device),
+            desc=empty((heads, 5), torch.int64),
+            kv=torch.zeros((p, bs, 128), dtype=torch.bfloat16, device=device),
+            sources=empty((p,), torch.int64), kinds=empty((p,)), ready=empty((p,)),
+            control=torch.zeros((4,), dtype=torch.int32, device=device),
+            error=torch.zeros((1,), dtype=torch.int32, device=device),
+            output=torch.zeros((qb, heads, 16, 64), dtype=torch.bfloat16, device=device),
+            window_shape=window_shape,
+        )
+        if window_shape is not None:
+            window_len = window_shape[0]
+            w.update(
+                window_kv=torch.zeros((window_len, heads, 128), dtype=torch.bfloat16,
+                                      device=device),
+                compressed=torch.zeros((qb, heads, 16, 64), dtype=torch.bfloat16, device=device),
+                gates=torch.zeros((qb, heads, 16, 3), dtype=torch.bfloat16, device=device),
+            )
+        self.active_plan.bind(w, w["blocks"], w["in_positions"], w["desc"],
+                              self.pool.region_bases)
+        w["c_attend_buffers"] = _lib.AttendBuffers(
+            query=w["query"].data_ptr(), kv=w["kv"].data_ptr(),
+            all_ids=w["all_ids"].data_ptr(), all_counts=w["all_counts"].data_ptr(),
+            row_positions=w["positions"].data_ptr(), starts=w["starts"].data_ptr(),
+            valid=w["valid"].data_ptr(), flags=w["flags"].data_ptr(),
+            ioids=w["ioids"].data_ptr(), missing=w["missing"].data_ptr(),
+            address=w["address"].data_ptr(), sources=w["sources"].data_ptr(),
+            kinds=w["kinds"].data_ptr(), ready=w["ready"].data_ptr(),
+            control=w["control"].data_ptr(), error=w["error"].data_ptr(),
+            window_kv=_lib.ptr(w.get("window_kv")), compressed=_lib.ptr(w.get("compressed")),
+            gates=_lib.ptr(w.get("gates")), out=w["output"].data_ptr())
+        w["allocated_bytes"] = sum(v.numel() * v.element_size() for v in w.values()
+                                   if isinstance(v, torch.Tensor))
+        self.workspaces[key] = w
+        self.workspace_allocations += 1
+        return w
+
+    def _execute(self, w, window_start, window):
+        stream = torch.cuda.current_stream(self.cache.data.device)
+        self.active_plan.plan(w, stream)
+        geometry = _lib.AttendGeometry(
+            queries=w["queries"], heads=w["heads"], width=w["width"], block_size=w["bs"],
+            physical=w["physical"], window=window if w["window_shape"] else 0,
+            window_len=w["window_shape"][0] if w["window_shape"] else 0,
+            gate=1 if w["window_shape"] else 0, window_start=window_start,
+            spin_limit=self.spin_limit)
+        _lib.check(_lib.lib().cxs_fetch_attend(geometry, w["c_attend_buffers"],
+                                               stream.cuda_stream))
+
+    # -- main entry --------------------------------------------------------
+    def run(self, query, blocks, positions, fetches, block_size, *, trace=False,
+            window=None, window_kv=None, window_start=0, compressed=None, gates=None):
+        if trace:
+            raise ValueError("Collect device activity separately from GR timing")
+        if (query.ndim != 4 or blocks.ndim != 3 or query.shape[:2] != blocks.shape[:2]
+                or len(fetches) != query.shape[1] or positions.shape != (len(query),)
+                or blocks.dtype != torch.int32
+                or positions.dtype not in (torch.int32, torch.int64)
+                or query.shape[2:] != (16, 64) or query.dtype != torch.bfloat16
+                or any(t.device != query.device for t in (blocks, positions))):
+            raise ValueError("Invalid GR query/selection geometry")
+        fused = window is not None
+        if fused and (window_kv is None or compressed is None or gates is None):
+            raise ValueError("Fused branches need window_kv, compressed and gates")
+        begin = time.perf_counter_ns()
+        device = query.device
+        stream = torch.cuda.current_stream(device)
+        if self.submitted:
+            stream.wait_event(self.last_done)
+        if self.cache.has_last_use:
+            stream.wait_event(self.cache.last_use)
+        q_count, heads, width = blocks.shape
+        qb = query_bucket(q_count)
+        window_shape = (len(window_kv), window) if fused else None
+        w = self._workspace(qb, heads, width, fetches, block_size, window_shape)
+        # Stage inputs into the workspace's static buffers (graph-safe).
+        w["query"][:q_count].copy_(query)
+        w["blocks"][:q_count].copy_(blocks)
+        w["in_positions"][:q_count].copy_(positions)
+        if q_count < qb:
+            w["blocks"][q_count:].fill_(-1)
+            w["in_positions"][q_count:].fill_(-1)
+        layout = tuple((f["row"], f["cached_length"], f["history_length"],
+                        f["current_kv"].data_ptr(), len(f["current_kv"])) for f in fetches)
+        host_desc = self.descriptors.get(layout)
+        if host_desc is None:
+            host_desc = torch.tensor(layout, dtype=torch.int64, pin_memory=True)
+            self.descriptors[layout] = host_desc
+            if len(self.descriptors) > 128:
+                self.descriptors.popitem(last=False)
+        else:
+            self.descriptors.move_to_end(layout)
+        w["desc"].copy_(host_desc, non_blocking=True)
+        if fused:
+            w["window_kv"].copy_(window_kv)
+            w["compressed"][:q_count].copy_(compressed)
+            w["gates"][:q_count].copy_(gates)
+        for f in fetches:
+            f["current_kv"].record_stream(stream)
+        if self.cuda_graphs:
+            graph_key = (window_start, window)
+            if w.get("graph_key") != graph_key:
+                w.pop("graph", None)
+                self._execute(w, window_start, window)  # warm-up, then capture
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    self._execute(w, window_start, window)
+                w["graph"], w["graph_key"] = graph, graph_key
+                self.captures += 1
+            w["graph"].replay()
+            self.replays += 1
+        else:
+            self._execute(w, window_start, window)
+        counters = DeferredLayerCounters(w["stats"].clone(), 1, self.pool.backend,
+                                         w["error"].clone())
+        self.pool._pending_read_counts.append((w["region_counts"].clone(), 1))
+        if self.hot_policy == "frequency":
+            self.active_plan.retain_hot(w, w["kv"], stream)
+        self.last_done.record(stream)
+        self.cache.last_use.record(stream)
+        self.cache.has_last_use = self.submitted = True
+        self.cache.planner_calls += 1
+        self.calls += 1
+        self.last_stats = dict(
+            backend=self.pool.backend,
+            planner="active_gpu" if self.cross_query_dedup else "query_private_gpu",
+            cross_query_dedup=self.cross_query_dedup, read_order=self.read_order,
+            effective_q=q_count, query_bucket=qb, history=[f["history_length"] for f in fetches],
+            consumer="tma_bounded_rows", consumer_ctas=w["consumer_ctas"],
+            io_policy="tma_block_ready", tma_copy="bulk_1d",
+            partial_block_policy="external_token_gather", cpu_selection_downloads=0,
+            fused_branches=fused, workspace_allocations=self.workspace_allocations,
+            workspace_evictions=self.workspace_evictions,
+            workspace_bytes=sum(x["allocated_bytes"] for x in self.workspaces.values()),
+            logical_block_capacity=w["map_blocks"], active_block_capacity=w["physical"],
+            persistent_mapping_bytes=w["persistent_mapping_bytes"],
+            total_submit_wall_ms=(time.perf_counter_ns() - begin) / 1e6,
+        )
+        return w["output"][:q_count], counters
+
+    def workspace(self):
+        """The most recently used workspace (inspection helper for tests)."""
+        return next(reversed(self.workspaces.values()))

@@ -1,0 +1,260 @@
+/*
+ * cxlsparse_b200 C ABI: the drop-in boundary for the NSA generative-
+ * recommendation selected-block path of Sispheqgj/cxlsparse, rebuilt for
+ * B200 (sm_100a).
+ *
+ * Conventions
+ *  - Plain pointers and sizes only; every device pointer is a CUDA device (or
+ *    UVA host-mapped) address on the current device; `stream` is a
+ *    cudaStream_t passed as void*.
+ *  - Every entry point returns CXS_OK (0) or a CXS_ERR_* code and never
+ *    throws. cxs_last_error() returns a thread-local message for the last
+ *    failure on the calling thread.
+ *  - Launch entry points only enqueue work on `stream`: no host
+ *    synchronisation, no device allocation, no host<->device copies, so they
+ *    can be captured in a CUDA graph (the reference captures plan + execute,
+ *    models/nsa/transport.py:624-631).
+ *  - Device-side failures (invalid selections, bounded-wait timeouts) are
+ *    reported through device words the caller reads after the stream
+ *    completes (planner stats column 6, and the `error` word of
+ *    cxs_fetch_attend), mirroring DeferredLayerCounters
+ *    (mempool/device_plan.py:16-42).
+ *
+ * Reference citations are file:line within the reference project.
+ */
+#ifndef CXLSPARSE_B200_H
+#define CXLSPARSE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CXS_ABI_VERSION 1
+
+enum cxs_status {
+  CXS_OK = 0,
+  CXS_ERR_INVALID = 1,      /* bad geometry / argument (reference: ValueError) */
+  CXS_ERR_CUDA = 2,         /* a CUDA runtime call failed */
+  CXS_ERR_CAPACITY = 3,     /* capacity refusal before any side effect
+                               (reference: GRWorkspaceLimit, transport.py:24-25) */
+  CXS_ERR_REGISTRATION = 4, /* host pool registration failed */
+  CXS_ERR_UNSUPPORTED = 5   /* device lacks a required feature */
+};
+
+/* Bits of the device error word written by cxs_fetch_attend. */
+#define CXS_DEVICE_ERR_READY_TIMEOUT 1 /* an attention warp gave up waiting on ready[b] */
+#define CXS_DEVICE_ERR_COPY_TIMEOUT 2  /* a bulk copy did not complete within the limit */
+#define CXS_DEVICE_ERR_BAD_BLOCK 4     /* a plan entry was out of range */
+
+/* Read-order policies (planning/read_order.py:11-18). */
+#define CXS_ORDER_PHYSICAL 0
+#define CXS_ORDER_DEPTH 1        /* "consumption_depth" */
+#define CXS_ORDER_DEPTH_SHARED 2 /* "consumption_depth_shared" */
+
+int cxs_abi_version(void);
+const char* cxs_last_error(void);
+
+/* ------------------------------------------------------------------ pool ---
+ * Backing pool outside HBM: NUMA-local pinned host memory, registered for
+ * mapped device access with device VA == host VA.
+ */
+
+/* Allocate `bytes` of anonymous host memory bound to NUMA node `numa_node`
+ * (-1: the node of CUDA device `device`, or no binding if unknown), touch it,
+ * and register it with cudaHostRegister(Mapped|Portable).
+ * Replaces the DRAM pool mapping + registration of mempool/pool.py:60 and
+ * mempool/native/cuda_registration.cuh:19-40. */
+int cxs_pool_create(size_t bytes, int device, int numa_node, void** host_base,
+                    int* bound_node);
+/* Unregister and unmap memory returned by cxs_pool_create. */
+int cxs_pool_destroy(void* host_base, size_t bytes);
+/* Register caller-owned host memory (mempool/native/cuda_registration.cuh:19-40):
+ * fails unless the device pointer equals the host pointer. */
+int cxs_pool_register(void* host_base, size_t bytes);
+/* Undo cxs_pool_register (mempool/native/cuda_registration.cuh:43-47). */
+int cxs_pool_unregister(void* host_base);
+/* NUMA node of a CUDA device's PCI function, or -1 if unknown. */
+int cxs_device_numa_node(int device);
+
+/* Scatter `count` bf16 KV records [count, 128] from device memory into pool
+ * token slots (page-striped over `regions` region bases). Replaces the region
+ * write kernel (mempool/native/region_write.cuh:14-51, mempool/cxl.py:194-228). */
+int cxs_pool_write(const void* records, const int64_t* slots, int64_t count,
+                   const int64_t* region_bases, int regions, int page_size,
+                   void* stream);
+
+/* -------------------------------------------------------------- planner ---
+ * Device-side fetch planner (planning/active.py:670-907 for the
+ * deduplicating plan; planning/query_private.py:258-457 for the no-dedup
+ * plan). Array meanings and layouts equal the reference workspace entries of
+ * the same name (planning/active.py:554-611).
+ */
+typedef struct cxs_plan_geometry {
+  int32_t queries;       /* token rows Q (row r = q * heads + head) */
+  int32_t heads;         /* KV heads H */
+  int32_t width;         /* selected blocks per row W */
+  int32_t block_size;    /* BS, a power of two */
+  int32_t map_blocks;    /* MAP: logical block capacity */
+  int32_t per_head;      /* CAP: compact slots per head */
+  int32_t sort_extent;   /* frequency table length per head */
+  int32_t hot;           /* hot replica tokens per cache row */
+  int32_t max_history;   /* host_locs row length */
+  int32_t regions;       /* pool region count */
+  int32_t page_size;     /* pool page size (tokens) */
+  int32_t consumer_ctas; /* consumers assumed by the depth order */
+  int32_t read_order;    /* CXS_ORDER_* */
+  int32_t private_plan;  /* 0 = dedup across rows, 1 = query-private */
+  int64_t pool_tokens;   /* pool capacity in token slots */
+} cxs_plan_geometry;
+
+typedef struct cxs_plan_buffers {
+  /* inputs */
+  const int32_t* blocks;    /* [Q, H, W] selected block ids, -1 padded */
+  const int32_t* positions; /* [Q] absolute positions, -1 = padded row */
+  const int64_t* desc;      /* [H, 5] (cache row, cached_len, history_len,
+                               current_kv address, current_len) */
+  const int64_t* bases;     /* [regions] pool region base addresses */
+  const int32_t* tags;      /* cache tags [rows, hot + 1] */
+  const int32_t* locs;      /* cache locations [rows, hot + 1] */
+  const int64_t* host_locs; /* cache token -> pool slot [rows, max_history] */
+  const void* hot_data;     /* cache hot KV data [rows * (hot + 1), 128] bf16 */
+  /* persistent + scratch (device) */
+  int32_t* mapping;         /* dedup: [H, MAP + 1]; private: [H, CAP] */
+  int32_t* insert_keys;     /* [H, CAP] */
+  int32_t* active_keys;     /* [H, CAP] */
+  int32_t* active_counts;   /* [H] */
+  int32_t* required;        /* [H, CAP] */
+  int32_t* frequencies;     /* [H, sort_extent] */
+  int32_t* stats;           /* [H, 7] */
+  int64_t* address;         /* [P, BS] */
+  int64_t* hbm;             /* [P, BS] */
+  int32_t* valid;           /* [P] */
+  int32_t* starts;          /* [P] */
+  int32_t* flags;           /* [P] missing */
+  int64_t* slots;           /* [P * BS] */
+  int32_t* ioids;           /* [P] */
+  int32_t* ranks;           /* [P] */
+  int32_t* missing;         /* [1] */
+  int32_t* all_ids;         /* [R, W] */
+  int32_t* all_counts;      /* [R] */
+  int32_t* row_positions;   /* [R] */
+  int32_t* region_counts;   /* [regions] */
+  int32_t* row_depth;       /* [R] */
+  int32_t* first_depth;     /* [P] */
+  int32_t* near_consumers;  /* [P] */
+  int32_t* chosen;          /* [H, hot] chosen hot indices */
+  /* query-private plan only (may be NULL otherwise) */
+  int32_t* private_required;    /* [H, CAP] */
+  int32_t* private_occurrences; /* [R, W] */
+  int32_t* canonical;           /* [H, sort_extent] */
+} cxs_plan_buffers;
+
+/* Bytes of dynamic shared memory / limits check for a geometry; returns
+ * CXS_ERR_CAPACITY for geometries the kernels refuse (before any launch). */
+int cxs_plan_check(const cxs_plan_geometry* geometry);
+
+/* Enqueue the whole plan: reset, dedup insert, sorted compaction, references,
+ * per-token source resolution, missing-block ranks, occurrence rows,
+ * read order, and the hot top-k choice. */
+int cxs_plan(const cxs_plan_geometry* geometry, const cxs_plan_buffers* buffers,
+             void* stream);
+
+/* Commit the chosen hot tokens once attention has completed: write tags and
+ * copy their KV from the staging buffer `kv` [P, BS, 128] bf16 into the
+ * cache hot data (planning/active.py:410-437, 909-925;
+ * planning/query_private.py:188-216). */
+int cxs_plan_commit_hot(const cxs_plan_geometry* geometry, const cxs_plan_buffers* buffers,
+                        const void* kv, int32_t* tags, void* hot_data, void* stream);
+
+/* ------------------------------------------------ IO + attention kernel ---
+ * One persistent launch with two warp roles (tma/transport.py:17-112 and
+ * tma/pipeline.py:96-742 are the reference's prepare + staged TMA kernel):
+ *  - IO warps take missing blocks in IOIDs order from a device cursor; full
+ *    contiguous 16-byte aligned external blocks move host -> shared -> HBM
+ *    with 1-D bulk TMA copies, mixed/tail blocks move with 16-byte vector
+ *    gathers; each then publishes ready[b] with st.release.gpu.
+ *  - attention warps own query rows; they first run the sliding-window
+ *    branch (HBM resident), then acquire ready[b] for each selected
+ *    occurrence in the original order, stage K and V through shared memory
+ *    with 2-D tensor TMA, and run online-softmax attention with tensor-core
+ *    MMAs; the epilogue optionally applies the sigmoid-gate mix
+ *    (models/nsa/model.py:470-473).
+ * A preceding prepare kernel (same call) classifies block sources, gathers
+ * resident blocks into the staging buffer and initialises ready flags.
+ */
+typedef struct cxs_attend_geometry {
+  int32_t queries;      /* Q token rows */
+  int32_t heads;        /* H */
+  int32_t width;        /* W */
+  int32_t block_size;   /* BS in {16, 32, 64} */
+  int32_t physical;     /* P = H * CAP */
+  int32_t window;       /* sliding window W_s (0: no window branch) */
+  int32_t window_len;   /* records in the window buffer */
+  int32_t gate;         /* 1: write the gate mix instead of the selected output */
+  int64_t window_start; /* absolute position of window record 0 */
+  int64_t spin_limit;   /* clock cycles before a bounded wait gives up */
+} cxs_attend_geometry;
+
+typedef struct cxs_attend_buffers {
+  const void* query;         /* [Q, H, 16, 64] bf16 */
+  void* kv;                  /* staging [P, BS, 128] bf16 */
+  const int32_t* all_ids;    /* [R, W] */
+  const int32_t* all_counts; /* [R] */
+  const int32_t* row_positions; /* [R] */
+  const int32_t* starts;     /* [P] */
+  const int32_t* valid;      /* [P] */
+  const int32_t* flags;      /* [P] missing */
+  const int32_t* ioids;      /* [P] */
+  const int32_t* missing;    /* [1] */
+  const int64_t* address;    /* [P, BS] per-token source addresses */
+  int64_t* sources;          /* [P] bulk source (or staging) per block */
+  int32_t* kinds;            /* [P] 0 resident, 1 bulk, 2 gather */
+  int32_t* ready;            /* [P] */
+  int32_t* control;          /* [4] device cursor/scratch, reset by the call */
+  int32_t* error;            /* [1] device error word (CXS_DEVICE_ERR_*), reset by the call */
+  const void* window_kv;     /* [window_len, H, 128] bf16 or NULL */
+  const void* compressed;    /* [Q, H, 16, 64] bf16 compressed-branch output (gate) */
+  const void* gates;         /* [Q, H, 16, 3] bf16 sigmoid gates (gate) */
+  void* out;                 /* [Q, H, 16, 64] bf16 */
+} cxs_attend_buffers;
+
+int cxs_fetch_attend(const cxs_attend_geometry* geometry, const cxs_attend_buffers* buffers,
+                     void* stream);
+
+/* Number of attention warps one cxs_fetch_attend launch runs on the current
+ * device for `block_size` (grid = resident CTAs x 8 warps). A plan's
+ * consumer_ctas should be min(rows, this) so that its consumption-depth order
+ * models the real consumers (tma/transport.py:63 uses min(rows, 256)). */
+int cxs_attend_capacity(int32_t block_size, int32_t* attention_warps);
+
+/* -------------------------------------------- compressed branch + top-n ---
+ * Compressed-token attention over complete summaries and top-n block
+ * selection from the summed GQA probabilities (models/nsa/ops.py:73-123;
+ * third_party/nsa_runtime/kernels.py:13-230). Selection order: current block
+ * first, then score descending with ties to the lower block id; width =
+ * min(count, ceil(total / BS)); entries after the current block are -1.
+ */
+int cxs_compressed_select(const void* query,      /* [Q, H, 16, 64] bf16 */
+                          const void* compressed, /* [C, H, 128] bf16 (K || V) */
+                          int32_t summaries,      /* C */
+                          const int32_t* positions, /* [Q] */
+                          int32_t queries, int32_t heads, int32_t block_size,
+                          int32_t count, int64_t total,
+                          void* out,              /* [Q, H, 16, 64] bf16 */
+                          int32_t* blocks,        /* [Q, H, width] */
+                          float* scores,          /* [Q, H, C] or NULL */
+                          void* stream);
+
+/* Mean-pool complete BS-token blocks of `tokens` records [n, H, 128] into
+ * `summaries` [n / BS, H, 128] bf16 (models/nsa/ops.py:62-70). */
+int cxs_block_summaries(const void* tokens, int64_t count, int32_t heads, int32_t block_size,
+                        void* summaries, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CXLSPARSE_B200_H */

@@ -1,0 +1,242 @@
+"""Generate golden fixtures by running the reference implementation itself.
+
+Usage:  python tests/golden/make_golden.py <reference project root>
+
+The reference (Sispheqgj/cxlsparse) is Python. This script imports it from the
+given checkout and runs:
+
+* ``ActivePlanAdapter.plan`` / ``QueryPrivatePlanAdapter.plan``
+  (``cxl_recsys/models/nsa/planning/{active,query_private}.py``) through the
+  Triton CPU interpreter (``TRITON_INTERPRET=1``) on CPU tensors, for several
+  residency modes, block sizes and read orders;
+* ``ops.compressed_attention_select`` / ``ops.window_attention`` torch CPU paths
+  (``cxl_recsys/models/nsa/ops.py``);
+* ``backends/io_plan.py:selected_attention_oracle`` (FP64).
+
+Outputs are small ``.npz`` files beside this script. The tests read only those
+files; nothing at test time needs the reference checkout.
+"""
+
+import os
+import sys
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+
+def _setup(reference_root):
+    os.environ["TRITON_INTERPRET"] = "1"
+    sys.path.insert(0, str(reference_root))
+
+
+def _cache(rows, hot, max_history, dim=128):
+    import torch
+
+    return SimpleNamespace(
+        hot=hot,
+        pool=None,
+        tags=torch.full((rows, hot + 1), -1, dtype=torch.int32),
+        locs=torch.arange(rows * (hot + 1), dtype=torch.int32).reshape(rows, hot + 1),
+        host_locs=torch.full((rows, max_history), -1, dtype=torch.int64),
+        data=torch.zeros((rows * (hot + 1), dim), dtype=torch.bfloat16),
+        max_history=max_history,
+    )
+
+
+PLAN_KEYS = (
+    "active_counts", "active_keys", "required", "stats", "address", "hbm", "slots",
+    "valid", "starts", "flags", "region_counts", "all_ids", "all_counts",
+    "positions", "ioids", "ranks", "missing", "frequencies",
+)
+
+
+def plan_case(name, *, seed, queries, heads, width, bs, hot, old, current,
+              residency, read_order, private=False, regions=1, page_size=64,
+              pad_rows=0, map_blocks=None, consumer_ctas=None, max_history=None):
+    """One planner fixture from the reference planner under the interpreter."""
+    import torch
+
+    from cxl_recsys.models.nsa.planning.active import ActivePlanAdapter
+    from cxl_recsys.models.nsa.planning.query_private import QueryPrivatePlanAdapter
+
+    g = torch.Generator().manual_seed(seed)
+    total = old + current
+    max_history = max_history or (old + 64)
+    rows_cache = heads
+    cache = _cache(rows_cache, hot, max_history)
+    pool_pages = (heads * (old + page_size) // page_size) + 2
+    cache.pool = SimpleNamespace(backend="cxl" if regions > 1 else "dram",
+                                 region_count=regions, pages=pool_pages,
+                                 page_size=page_size)
+    # Backing slots: a shuffled page list per head, so pages are not adjacent.
+    page_perm = torch.randperm(pool_pages, generator=g)
+    pages_per_head = -(-old // page_size)
+    for h in range(heads):
+        pages = page_perm[h * pages_per_head:(h + 1) * pages_per_head]
+        token = torch.arange(old)
+        cache.host_locs[h, :old] = pages[token // page_size] * page_size + token % page_size
+    # Hot residency per head.
+    for h in range(heads):
+        if residency == "hit":
+            hot_tokens = list(range(min(old, hot)))
+        elif residency == "partial":
+            pool = torch.randperm(old, generator=g)[: min(hot, old) // 2].tolist()
+            hot_tokens = sorted(pool)
+        else:
+            hot_tokens = []
+        if hot_tokens:
+            cache.tags[h, : len(hot_tokens)] = torch.tensor(hot_tokens, dtype=torch.int32)
+    # Selections: random, with duplicates, causal tails and invalid future picks.
+    q_total = queries + pad_rows
+    positions = torch.full((q_total,), -1, dtype=torch.int64)
+    positions[:queries] = old + torch.arange(queries) % max(current, 1)
+    blocks = torch.full((q_total, heads, width), -1, dtype=torch.int32)
+    if residency != "empty":
+        for q in range(queries):
+            current_block = int(positions[q]) // bs
+            for h in range(heads):
+                picks = torch.randint(0, current_block + 1, (width,), generator=g)
+                picks[0] = current_block
+                drop = torch.rand(width, generator=g) < 0.15
+                picks[drop] = -1
+                blocks[q, h] = picks.to(torch.int32)
+    current_kv = [torch.zeros((max(current, 1), 128), dtype=torch.bfloat16)
+                  for _ in range(heads)]
+    fetches = [dict(row=h, cached_length=old, history_length=old,
+                    current_kv=current_kv[h][:current]) for h in range(heads)]
+    query = torch.zeros((q_total, heads, 16, 64), dtype=torch.bfloat16)
+    adapter_cls = QueryPrivatePlanAdapter if private else ActivePlanAdapter
+    adapter = adapter_cls(cache, chunk_blocks=64)
+    w = adapter.allocate(query, blocks, fetches, bs, map_blocks=map_blocks,
+                         occurrence_only=True, read_order=read_order)
+    w["consumer_ctas"] = consumer_ctas or min(256, w["rows"])
+    current_ptr = [0x7F0000000000 + h * 0x100000 for h in range(heads)]
+    desc = torch.tensor([(h, old, old, current_ptr[h], current) for h in range(heads)],
+                        dtype=torch.int64)
+    bases = torch.tensor([0x500000000000 + r * 0x10000000 for r in range(regions)],
+                         dtype=torch.int64)
+    chosen = adapter.plan(blocks, positions, desc, bases, w, read_order=read_order)
+    out = dict(
+        blocks=blocks.numpy(), positions=positions.numpy(), desc=desc.numpy(),
+        tags=cache.tags.numpy(), locs=cache.locs.numpy(),
+        host_locs=cache.host_locs.numpy(), bases=bases.numpy(),
+        hot_data=np.int64(cache.data.data_ptr()),
+        bs=bs, hot=hot, map_blocks=w["map_blocks"], pool_tokens=pool_pages * page_size,
+        page_size=page_size, consumer_ctas=w["consumer_ctas"],
+        read_order=read_order, private=int(private),
+        chosen=chosen.numpy(),
+    )
+    for key in PLAN_KEYS:
+        out["ref_" + key] = w[key].numpy()
+    if read_order.startswith("consumption_depth"):
+        out["ref_first_depth"] = w["dependency_first_depth"].numpy()
+        out["ref_near"] = w["dependency_near_consumers"].numpy()
+    if private:
+        out["ref_hot_canonical"] = w["hot_canonical"].numpy()
+        out["ref_private_mapping"] = w["mapping"].numpy()
+    np.savez_compressed(HERE / f"plan_{name}.npz", **out)
+    return out
+
+
+def attention_case(seed=71):
+    """Selected attention FP64 oracle on the reference transport test geometry."""
+    import torch
+
+    from cxl_recsys.models.nsa.backends.io_plan import selected_attention_oracle
+
+    g = torch.Generator().manual_seed(seed)
+    backing = torch.randn(80, 2, 128, generator=g).bfloat16()
+    query = torch.randn(13, 2, 16, 64, generator=g).bfloat16()
+    positions = torch.arange(67, 80)
+    blocks = torch.tensor([[[0, 1, 0, 4], [1, 0, 1, 4]]] * 13, dtype=torch.int32)
+    blocks[3] = -1
+    expected = selected_attention_oracle(query, backing, blocks, positions, 16)
+    np.savez_compressed(
+        HERE / "attention_selected.npz",
+        backing=backing.view(torch.int16).numpy(), query=query.view(torch.int16).numpy(),
+        positions=positions.numpy(), blocks=blocks.numpy(), expected=expected.numpy())
+
+
+def select_cases():
+    """Compressed attention + top-n and window attention, torch CPU paths."""
+    import torch
+
+    from cxl_recsys.models.nsa import ops
+
+    out = {}
+    for i, (length, bs, count, chunk) in enumerate(
+            [(300, 16, 16, 40), (4096 + 128, 64, 16, 24), (97, 16, 16, 33)]):
+        g = torch.Generator().manual_seed(100 + i)
+        blocks_total = length // bs
+        key = torch.randn(blocks_total, 2, 64, generator=g).bfloat16()
+        value = torch.randn(blocks_total, 2, 64, generator=g).bfloat16()
+        query = torch.randn(chunk, 2, 16, 64, generator=g).bfloat16()
+        positions = torch.arange(length - chunk, length)
+        o, sel = ops.compressed_attention_select(
+            query.float(), key.float(), value.float(), positions, length, bs, count)
+        out[f"c{i}_query"] = query.view(torch.int16).numpy()
+        out[f"c{i}_key"] = key.view(torch.int16).numpy()
+        out[f"c{i}_value"] = value.view(torch.int16).numpy()
+        out[f"c{i}_positions"] = positions.numpy()
+        out[f"c{i}_meta"] = np.array([length, bs, count])
+        out[f"c{i}_output"] = o.numpy()
+        out[f"c{i}_selected"] = sel.numpy()
+    # Deterministic ties (tests/test_nsa_fla.py:39-54): zero scores everywhere.
+    q = torch.zeros(3, 2, 16, 64)
+    kv = torch.zeros(40, 2, 64)
+    pos = torch.tensor([17, 95, 401])
+    _, tie = ops.compressed_attention_select(q, kv, kv, pos, 640, 16, 16)
+    out["tie_selected"] = tie.numpy()
+    out["tie_positions"] = pos.numpy()
+    # Window branch CPU path (ops.py:194-205).
+    g = torch.Generator().manual_seed(9)
+    window, start, extend = 64, 200, 40
+    records = torch.randn(window - 1 + extend, 2, 128, generator=g).bfloat16()
+    query = torch.randn(extend, 2, 16, 64, generator=g).bfloat16()
+    positions = torch.arange(start + window - 1, start + window - 1 + extend)
+    local = ops.window_attention(query.float(), records.float(), positions, start,
+                                 window, 16)
+    out["win_records"] = records.view(torch.int16).numpy()
+    out["win_query"] = query.view(torch.int16).numpy()
+    out["win_positions"] = positions.numpy()
+    out["win_meta"] = np.array([window, start])
+    out["win_output"] = local.numpy()
+    np.savez_compressed(HERE / "select_window.npz", **out)
+
+
+def main():
+    if len(sys.argv) != 2:
+        raise SystemExit(__doc__)
+    _setup(Path(sys.argv[1]).resolve())
+    common = dict(heads=2, hot=32)
+    plan_case("miss_bs16_depth", seed=1, queries=13, width=4, bs=16, old=67,
+              current=13, residency="miss", read_order="consumption_depth", **common)
+    plan_case("partial_bs16_shared", seed=2, queries=13, width=4, bs=16, old=67,
+              current=13, residency="partial", read_order="consumption_depth_shared",
+              pad_rows=3, **common)
+    plan_case("hit_bs16_physical", seed=3, queries=9, width=5, bs=16, old=80,
+              current=9, residency="hit", read_order="physical", **common)
+    plan_case("empty_bs16", seed=4, queries=5, width=4, bs=16, old=40, current=5,
+              residency="empty", read_order="consumption_depth", **common)
+    plan_case("partial_bs64_depth", seed=5, queries=48, width=8, bs=64, old=1000,
+              current=48, residency="partial", read_order="consumption_depth",
+              regions=3, consumer_ctas=7, heads=2, hot=64)
+    plan_case("miss_bs64_shared_regions", seed=6, queries=40, width=16, bs=64,
+              old=2048, current=40, residency="miss",
+              read_order="consumption_depth_shared", regions=2, heads=2, hot=128)
+    plan_case("private_partial_bs16", seed=7, queries=13, width=4, bs=16, old=67,
+              current=13, residency="partial", read_order="consumption_depth",
+              private=True, map_blocks=64, **common)
+    plan_case("private_miss_bs64", seed=8, queries=24, width=8, bs=64, old=900,
+              current=24, residency="miss", read_order="consumption_depth",
+              private=True, regions=2, heads=2, hot=64)
+    attention_case()
+    select_cases()
+    print("fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

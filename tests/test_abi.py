@@ -1,0 +1,89 @@
+"""C-ABI boundary checks that need no GPU: symbols, struct layout, refusals."""
+
+import ctypes
+import re
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from cxlsparse_b200 import _lib
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "cxlsparse.h"
+
+
+def declared():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(cxs_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared()
+    assert set(names) == set(_lib.exported_symbols())
+    for name in names:
+        assert hasattr(lib, name), name
+    assert lib.cxs_abi_version() == 1
+
+
+def _c_layout(struct, fields):
+    body = "\n".join(f'printf("%zu\\n", offsetof({struct}, {f}));' for f in fields)
+    return body + f'\nprintf("%zu\\n", sizeof({struct}));'
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc required")
+def test_ctypes_structs_match_c_layout(tmp_path):
+    pairs = [("cxs_plan_geometry", _lib.PlanGeometry), ("cxs_plan_buffers", _lib.PlanBuffers),
+             ("cxs_attend_geometry", _lib.AttendGeometry),
+             ("cxs_attend_buffers", _lib.AttendBuffers)]
+    source = ["#include <stdio.h>", "#include <stddef.h>", '#include "cxlsparse.h"',
+              "int main(void) {"]
+    for name, cls in pairs:
+        source.append(_c_layout(name, [f for f, _ in cls._fields_]))
+    source.append("return 0; }")
+    c_file = tmp_path / "layout.c"
+    c_file.write_text("\n".join(source))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(HEADER.parent), str(c_file), "-o", str(exe)], check=True)
+    values = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True,
+                                             check=True).stdout.split()]
+    expected = []
+    for _, cls in pairs:
+        expected += [getattr(cls, f).offset for f, _ in cls._fields_] + [ctypes.sizeof(cls)]
+    assert values == expected
+
+
+def _geometry(**kw):
+    base = dict(queries=13, heads=2, width=4, block_size=16, map_blocks=64, per_head=52,
+                sort_extent=832, hot=32, max_history=131, regions=1, page_size=64,
+                consumer_ctas=26, read_order=1, private_plan=0, pool_tokens=1000)
+    base.update(kw)
+    return _lib.PlanGeometry(**base)
+
+
+def test_plan_geometry_refusals_before_any_launch():
+    lib = _lib.lib()
+    assert lib.cxs_plan_check(_geometry()) == _lib.OK
+    assert lib.cxs_plan_check(_geometry(block_size=24)) == _lib.ERR_INVALID
+    assert lib.cxs_plan_check(_geometry(per_head=65)) == _lib.ERR_INVALID
+    assert lib.cxs_plan_check(_geometry(read_order=7)) == _lib.ERR_INVALID
+    assert lib.cxs_plan_check(_geometry(hot=8192, sort_extent=8192)) == _lib.ERR_CAPACITY
+    assert lib.cxs_plan_check(_geometry(map_blocks=1 << 19, per_head=52)) == _lib.ERR_CAPACITY
+    assert lib.cxs_plan_check(_geometry(private_plan=1, width=40, per_head=520)) == \
+        _lib.ERR_CAPACITY
+    with pytest.raises(_lib.CapacityError):
+        _lib.check(lib.cxs_plan_check(_geometry(hot=8192, sort_extent=8192)))
+    with pytest.raises(ValueError):
+        _lib.check(lib.cxs_plan_check(_geometry(block_size=24)))
+
+
+def test_invalid_attend_arguments_are_rejected_without_a_device():
+    lib = _lib.lib()
+    g = _lib.AttendGeometry(queries=1, heads=2, width=4, block_size=24, physical=8)
+    b = _lib.AttendBuffers()
+    assert lib.cxs_fetch_attend(g, b, None) == _lib.ERR_INVALID
+    g.block_size, g.gate = 16, 1
+    assert lib.cxs_fetch_attend(g, b, None) == _lib.ERR_INVALID
+    assert b"gate" in lib.cxs_last_error()
