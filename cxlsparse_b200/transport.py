@@ -121,6 +121,7 @@ class GRSelectedTransport:
         self.last_done = torch.cuda.Event()
         self.last_stats = {}
         self._capacity_cache = {}
+        self._capture_stream = None
 
     # -- reference surface -----------------------------------------------
     def refusal(self, queries, cached, heads, groups, width, bs):
@@ -291,8 +292,12 @@ class GRSelectedTransport:
                 w.pop("graph", None)
                 self._execute(w, window_start, window)  # warm-up, then capture
                 graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph, stream=stream):
+                if self._capture_stream is None:
+                    self._capture_stream = torch.cuda.Stream(device)
+                self._capture_stream.wait_stream(stream)
+                with torch.cuda.graph(graph, stream=self._capture_stream):
                     self._execute(w, window_start, window)
+                stream.wait_stream(self._capture_stream)
                 w["graph"], w["graph_key"] = graph, graph_key
                 self.captures += 1
             w["graph"].replay()

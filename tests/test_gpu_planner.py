@@ -43,6 +43,8 @@ def run_device_plan(z, device, *, private=None, read_order=None, consumer_ctas=N
     positions = torch.from_numpy(z["positions"]).to(device, torch.int32)
     bases = torch.from_numpy(z["bases"]).to(device)
     buffers = adapter.bind(w, blocks, positions, desc, bases)
+    # The plan reads these on every (graph) replay: keep them alive with w.
+    w["_inputs"] = (blocks, positions, desc, bases, tags, locs, host_locs, cache)
     buffers.hot_data = int(z["hot_data"])
     # Stale scratch from an earlier call must not leak into the next plan.
     for key in ("address", "hbm", "slots", "valid", "all_ids", "chosen"):
