@@ -1,0 +1,341 @@
+"""Benchmark: NSA-1B-shaped GR extend at H=16K / E=256 on 1..N B200.
+
+One step = one 16-layer extend forward of E candidate tokens over a user's
+H-token history whose KV lives in the pinned host pool (BASELINE configs[1]
+shape). Per layer: compressed branch + top-n, the deduplicating fetch plan,
+the fused IO + window/selected attention + gate mix kernel, and the hot-set
+commit (all in libcxlsparse_b200.so); projections / FFN are cuBLAS GEMMs.
+Weak scaling: every rank serves its own user (users round-robin over GPUs,
+each GPU with its own pool slice); the per-user final hidden states are
+all-gathered with NCCL after each step (the only collective).
+
+Prints ONE JSON line (rank 0). ``--impl reference`` times the reference's CPU
+torch NSA path (restated in oracle/nsa_cpu.py) on the host cores instead.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "NSA-1B extend tok/s @H16K/E256 at 1–8 B200; KV-fetch GB/s vs PCIe5 peak"
+REFERENCE_TOK_S = 13503.0  # derived H100 worker tok/s @H16K/E256 (E / worker p50)
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    p.add_argument("--history", type=int, default=16384)
+    p.add_argument("--extend", type=int, default=256)
+    p.add_argument("--layers", type=int, default=16)
+    p.add_argument("--read-order", default="consumption_depth")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(gpu), "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows]
+        max_sm = max(float(r[2]) for r in rows)
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v})
+        loaded = [s for s, r in zip(sm, rows) if float(r[3]) > 200] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max_sm, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup(torch):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def measure_pcie(torch, device):
+    """Pinned host -> HBM copy bandwidth (GB/s), best of 5 x 256 MiB."""
+    size = 256 * 1024**2
+    host = torch.empty(size, dtype=torch.uint8, pin_memory=True)
+    dev = torch.empty(size, dtype=torch.uint8, device=device)
+    best = 0.0
+    for _ in range(5):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        dev.copy_(host, non_blocking=True)
+        end.record()
+        end.synchronize()
+        best = max(best, size / (start.elapsed_time(end) / 1e3) / 1e9)
+    del host, dev
+    return best
+
+
+def cpu_baseline(args, torch):
+    from oracle.nsa_cpu import time_cpu_extend
+
+    threads = os.cpu_count() or 1
+    one_layer, _ = time_cpu_extend(extend=args.extend, history=args.history, layers=1,
+                                   threads=threads)
+    layers = max(1, min(args.layers, int(20.0 / max(one_layer, 1e-3))))
+    seconds, cores = time_cpu_extend(extend=args.extend, history=args.history, layers=layers,
+                                     threads=threads)
+    per_forward = seconds * args.layers / layers
+    return {"value": args.extend / per_forward, "unit": "tok/s", "cores": cores,
+            "kind": "port",
+            "sample": f"{layers} of {args.layers} layers of one H={args.history}/E={args.extend} "
+                      "extend forward (fp32 torch CPU restatement of the reference path), "
+                      "scaled to the full forward"}
+
+
+def run_reference(args):
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from oracle.nsa_cpu import time_cpu_extend
+
+    threads = os.cpu_count() or 1
+    one_layer, _ = time_cpu_extend(extend=args.extend, history=args.history, layers=1,
+                                   threads=threads)
+    budget = 150.0 / max(1, args.steps + args.warmup)  # whole run within a few minutes
+    layers = max(1, min(args.layers, int(budget / max(one_layer, 1e-3))))
+    seconds, cores = time_cpu_extend(extend=args.extend, history=args.history, layers=layers,
+                                     steps=args.steps, warmup=args.warmup, threads=threads)
+    per_forward = seconds * args.layers / layers
+    value = args.extend / per_forward
+    sample = (f"{layers} of {args.layers} layers per step of the H={args.history}/E={args.extend} "
+              "extend forward, scaled to the full forward")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_forward * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) history KV)",
+        "config": workload(args),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "torch_threads": torch.get_num_threads(),
+    }))
+
+
+def workload(args):
+    return {"workload": f"BASELINE configs[1]: NSA-1B-shaped extend, H={args.history}, "
+                        f"E={args.extend}, 1 user per GPU",
+            "history": args.history, "extend": args.extend, "layers": args.layers,
+            "hidden": 2048, "heads": "32q/2kv", "block_size": 64, "top_n": 16,
+            "window": 512, "compression": "mean pooling, block = stride = 64",
+            "hot": "256 tokens per (layer, kv head), reference frequency policy",
+            "pool": "NUMA-local pinned host memory, cudaHostRegister mapped",
+            "read_order": args.read_order,
+            "l2": "inputs larger than L2: 1.4 GB of weights stream per step",
+            "parallelism": f"users sharded, {args.gpus} user(s) on {args.gpus} GPU(s)"}
+
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = dist_setup(torch)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from cxlsparse_b200 import _lib
+    from cxlsparse_b200.model import NSAConfig, NSAExtendModel
+
+    cfg = NSAConfig(layers=args.layers)
+    model = NSAExtendModel(cfg, device=device, seed=0, max_history=args.history + args.extend,
+                           read_order=args.read_order)
+    g = torch.Generator().manual_seed(1000 + rank)
+    history = torch.randint(0, cfg.vocab, (args.history,), generator=g).to(device)
+    candidates = torch.randint(0, cfg.vocab, (args.extend,), generator=g)
+    t0 = time.perf_counter()
+    model.prefill(history)
+    prefill_s = time.perf_counter() - t0
+    launches_before = _lib.lib().cxs_launch_count()
+    graph, static_ids, static_out, counters = model.capture_extend(args.extend)
+    launches_per_step = _lib.lib().cxs_launch_count() - launches_before
+    static_ids.copy_(candidates.to(device))
+    pcie = measure_pcie(torch, device)
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    gathered = torch.empty((world, cfg.hidden), dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    # Fetch statistics of one steady-state step (hot set already committed).
+    graph.replay()
+    torch.cuda.synchronize(device)
+    stats = torch.stack([c.statistics for c in counters]).cpu()   # [L, H, 7]
+    errors = [int(c.device_error.item()) for c in counters]
+    if any(errors) or stats[..., 6].any():
+        raise RuntimeError(f"device plan/attend errors: {errors}")
+    fetched_bytes = int(stats[..., 3].sum()) * 256
+    attended = int(stats[..., 4].sum() + stats[..., 5].sum())
+
+    # --- device-resident timed region --------------------------------------
+    sampler = ClockSampler(local)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    end.record(stream)
+    barrier()
+    device_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+
+    # --- end-to-end: pinned H2D ids, replay, gather scores, D2H ------------
+    host_ids = candidates.pin_memory()
+    host_out = torch.empty((world, cfg.hidden), dtype=torch.bfloat16, pin_memory=True)
+    barrier()
+    start.record(stream)
+    for _ in range(args.steps):
+        static_ids.copy_(host_ids, non_blocking=True)
+        graph.replay()
+        last = static_out[-1]
+        if dist is not None:
+            dist.all_gather_into_tensor(gathered, last.contiguous())
+        else:
+            gathered[0].copy_(last)
+        host_out.copy_(gathered, non_blocking=True)
+    end.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    clocks = sampler.stop()
+
+    # --- fused fetch/attend kernel timing (eager step, events on its stream)
+    model.transport.kernel_timing = []
+    model.counters.clear()
+    model.extend(static_ids)
+    torch.cuda.synchronize(device)
+    durations = [s.elapsed_time(e) for s, e, _ in model.transport.kernel_timing]
+    model.transport.kernel_timing = None
+    kernel_ms = statistics.mean(durations)
+    layer_fetch = fetched_bytes / args.layers
+    rows = args.extend * cfg.kv_heads
+    window_tokens = rows * cfg.window
+    algorithmic = (attended / args.layers + window_tokens) * 256 + layer_fetch
+    peak, peak_kind = peaks()
+
+    result = None
+    if rank == 0:
+        tokens = world * args.extend
+        value = tokens / (device_ms / 1e3)
+        e2e = tokens / (e2e_ms / 1e3)
+        achieved = algorithmic / (kernel_ms / 1e3) / 1e9
+        hbm = peak["hbm_gbs"]
+        result = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": device_ms,
+            "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / REFERENCE_TOK_S, "dtype": "bf16",
+            "data": "synthetic: seeded random token ids, random N(0,0.02) weights, "
+                    "history KV computed by the model (chunked prefill)",
+            "config": workload(args),
+            "e2e": {"value": e2e, "unit": "tok/s",
+                    "h2d_bytes_per_step": args.extend * 8,
+                    "d2h_bytes_per_step": world * cfg.hidden * 2},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "fetch_attend_kernel<64>",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None,
+                         "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"
+                         if peak_kind == "measured" else "fallback",
+                         "algorithmic_bytes_per_launch": algorithmic,
+                         "launch_ms": kernel_ms},
+            "fetch": {"bytes_per_step": fetched_bytes,
+                      "gb_s_in_kernel": layer_fetch / (kernel_ms / 1e3) / 1e9,
+                      "gb_s_over_step": fetched_bytes / (device_ms / 1e3) / 1e9,
+                      "pcie_h2d_peak_gb_s": pcie,
+                      "frac_of_pcie_in_kernel": layer_fetch / (kernel_ms / 1e3) / 1e9 / pcie,
+                      "misses_tokens_per_step": int(stats[..., 3].sum()),
+                      "hits_tokens_per_step": int(stats[..., 2].sum())},
+            "clocks": clocks,
+            "prefill_s": prefill_s,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(args, torch)
+        print(json.dumps(result))
+    if dist is not None:
+        del graph
+        dist.barrier()
+        dist.destroy_process_group()
+    model.close()
+    return result
+
+
+def main():
+    args = parse()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

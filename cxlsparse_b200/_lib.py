@@ -90,6 +90,7 @@ def lib():
         sigs = {
             "cxs_abi_version": (c_i32, []),
             "cxs_last_error": (ctypes.c_char_p, []),
+            "cxs_launch_count": (c_i64, []),
             "cxs_pool_create": (c_i32, [ctypes.c_size_t, c_i32, c_i32,
                                         ctypes.POINTER(c_vp), ctypes.POINTER(c_i32)]),
             "cxs_pool_destroy": (c_i32, [c_vp, ctypes.c_size_t]),
@@ -144,7 +145,7 @@ def stream_handle(device=None):
 
 def exported_symbols():
     """Names the header declares (used by the CPU symbol test)."""
-    return ("cxs_abi_version", "cxs_last_error", "cxs_pool_create", "cxs_pool_destroy",
+    return ("cxs_abi_version", "cxs_last_error", "cxs_launch_count", "cxs_pool_create", "cxs_pool_destroy",
             "cxs_pool_register", "cxs_pool_unregister", "cxs_device_numa_node",
             "cxs_pool_write", "cxs_plan_check", "cxs_plan", "cxs_plan_commit_hot",
             "cxs_fetch_attend", "cxs_attend_capacity", "cxs_compressed_select",

@@ -424,6 +424,7 @@ int launch(const cxs_attend_geometry& g, const cxs_attend_buffers& b, cudaStream
   config.attrs = attr;
   config.numAttrs = 1;
   CXS_CUDA(cudaLaunchKernelEx(&config, fetch_attend_kernel<BS>, kv_map, win_map, a));
+  cxs_host::count_launch();
   return CXS_OK;
 }
 

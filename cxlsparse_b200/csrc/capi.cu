@@ -25,6 +25,10 @@ int check_cuda(cudaError_t err, const char* what) {
   return set_error(CXS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
 }
 
+static unsigned long long g_launches = 0;
+
+void count_launch() { __atomic_add_fetch(&g_launches, 1ull, __ATOMIC_RELAXED); }
+
 }  // namespace cxs_host
 
 using cxs_host::set_error;
@@ -32,6 +36,10 @@ using cxs_host::set_error;
 extern "C" int cxs_abi_version(void) { return CXS_ABI_VERSION; }
 
 extern "C" const char* cxs_last_error(void) { return cxs_host::g_error; }
+
+extern "C" int64_t cxs_launch_count(void) {
+  return (int64_t)__atomic_load_n(&cxs_host::g_launches, __ATOMIC_RELAXED);
+}
 
 // ------------------------------------------------------------------- pool ---
 

@@ -152,6 +152,7 @@ __device__ __forceinline__ int warp_sum(int v) {
 namespace cxs_host {
 int set_error(int code, const char* fmt, ...);
 int check_cuda(cudaError_t err, const char* what);
+void count_launch();  // one kernel enqueued by this library
 }  // namespace cxs_host
 
 #define CXS_CUDA(call)                                                     \
@@ -164,4 +165,5 @@ int check_cuda(cudaError_t err, const char* what);
   do {                                                                     \
     cudaError_t _e = cudaGetLastError();                                   \
     if (_e != cudaSuccess) return cxs_host::check_cuda(_e, what);          \
+    cxs_host::count_launch();                                              \
   } while (0)

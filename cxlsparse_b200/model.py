@@ -1,0 +1,229 @@
+"""NSA-1B-shaped extend model around the selected-block transport.
+
+The per-layer structure follows ``cxl_recsys/models/nsa/model.py:440-492,
+592-827``: RMSNorm -> q/k/v/g projections -> RoPE -> compressed summaries
+(ops.py:62-70) -> compressed branch + top-n -> selected transport with the
+window branch and gate mix -> o_proj -> RMSNorm -> SwiGLU FFN. Projections and
+the FFN are plain cuBLAS GEMMs through torch (out of scope for new kernels);
+every attention branch, the planner and the backing-pool IO run in
+``libcxlsparse_b200.so``.
+
+Weights are random N(0, 0.02) (norm weights 1) with a fixed seed: no
+checkpoint is needed to measure the path. ``prefill`` pushes a user's history
+through the same layers in chunks, writing each layer's history KV into the
+pinned backing pool (the reference's persistent KV write,
+model.py:659-688); ``extend`` runs one GR candidate suffix over that history
+without appending to it.
+"""
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+from .mempool import HiSparseCache, MemoryPool
+from .transport import GRSelectedTransport
+
+
+@dataclass
+class NSAConfig:
+    layers: int = 16
+    hidden: int = 2048
+    q_heads: int = 32
+    kv_heads: int = 2
+    head_dim: int = 64
+    ffn: int = 5632
+    vocab: int = 32000
+    rms_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    block_size: int = 64
+    block_counts: int = 16
+    window: int = 512
+    hot: int = 256
+
+    @property
+    def groups(self):
+        return self.q_heads // self.kv_heads
+
+
+@dataclass
+class UserState:
+    row: int
+    length: int = 0
+    pages: list = field(default_factory=list)        # [layer][head] -> page list
+    summaries: list = field(default_factory=list)    # [layer] -> [C, H, 128] bf16
+    tails: list = field(default_factory=list)        # [layer] -> [<BS, H, 128]
+    windows: list = field(default_factory=list)      # [layer] -> [<=W-1, H, 128]
+
+
+def rms_norm(hidden, weight, eps):
+    value = hidden.float()
+    normalized = value * torch.rsqrt(value.square().mean(-1, keepdim=True) + eps)
+    return normalized.to(hidden.dtype) * weight
+
+
+def rotary(query, key, positions, inv_freq):
+    frequency = positions.float()[:, None] * inv_freq[None, :]
+    phase = torch.cat((frequency, frequency), -1)
+    cosine = phase.cos().to(query.dtype)[:, None, :]
+    sine = phase.sin().to(query.dtype)[:, None, :]
+
+    def rotate(value):
+        left, right = value.chunk(2, -1)
+        return value * cosine + torch.cat((-right, left), -1) * sine
+
+    return rotate(query), rotate(key)
+
+
+class NSAExtendModel:
+    """Random-init NSA model whose attention runs on the B200 selected path."""
+
+    def __init__(self, cfg=None, *, device="cuda", seed=0, max_users=1, max_history=16384,
+                 hot_policy="frequency", read_order="consumption_depth",
+                 cross_query_dedup=True, pool_regions=1, chunk=1024):
+        self.cfg = cfg = cfg or NSAConfig()
+        self.device = torch.device(device)
+        self.max_history, self.chunk = max_history, chunk
+        g = torch.Generator(device="cpu").manual_seed(seed)
+
+        def normal(*shape):
+            return (torch.randn(*shape, generator=g) * 0.02).to(torch.bfloat16).to(self.device)
+
+        d, kvd = cfg.hidden, cfg.kv_heads * cfg.head_dim
+        self.embed = normal(cfg.vocab, d)
+        self.final_norm = torch.ones(d, dtype=torch.bfloat16, device=self.device)
+        self.layers = []
+        for _ in range(cfg.layers):
+            self.layers.append(dict(
+                in_norm=torch.ones(d, dtype=torch.bfloat16, device=self.device),
+                post_norm=torch.ones(d, dtype=torch.bfloat16, device=self.device),
+                q=normal(cfg.q_heads * cfg.head_dim, d), k=normal(kvd, d), v=normal(kvd, d),
+                g=normal(cfg.q_heads * 3, d), o=normal(d, cfg.q_heads * cfg.head_dim),
+                gate=normal(cfg.ffn, d), up=normal(cfg.ffn, d), down=normal(d, cfg.ffn)))
+        self.inv_freq = 1.0 / (cfg.rope_theta ** (
+            torch.arange(0, cfg.head_dim, 2, device=self.device).float() / cfg.head_dim))
+        pages_per_user = cfg.layers * cfg.kv_heads * math.ceil(max_history / 64)
+        self.pool = MemoryPool(pages_per_user * max_users, 128, "host", page_size=64,
+                               regions=pool_regions, device=self.device)
+        self.cache = HiSparseCache(self.pool, rows=max_users * cfg.layers * cfg.kv_heads,
+                                   max_history=max_history, hot=cfg.hot,
+                                   topk=min(cfg.hot, 256), dim=128)
+        self.transport = GRSelectedTransport(
+            self.cache, read_order=read_order, cross_query_dedup=cross_query_dedup,
+            hot_policy=hot_policy, capacity=4)
+        self.users = {}
+        self.counters = []
+
+    # -- state -------------------------------------------------------------
+    def user(self, name):
+        if name not in self.users:
+            cfg = self.cfg
+            empty = torch.empty((0, cfg.kv_heads, 128), dtype=torch.bfloat16, device=self.device)
+            pages_needed = math.ceil(self.max_history / 64)
+            self.users[name] = UserState(
+                row=len(self.users) * cfg.layers * cfg.kv_heads,
+                pages=[[self.pool.allocate(pages_needed) for _ in range(cfg.kv_heads)]
+                       for _ in range(cfg.layers)],
+                summaries=[empty] * cfg.layers, tails=[empty] * cfg.layers,
+                windows=[empty] * cfg.layers)
+        return self.users[name]
+
+    # -- one layer -----------------------------------------------------------
+    def _layer(self, index, hidden, positions, st, *, append):
+        cfg, w = self.cfg, self.layers[index]
+        old = st.length
+        x = rms_norm(hidden, w["in_norm"], cfg.rms_eps)
+        q = F.linear(x, w["q"]).view(-1, cfg.q_heads, cfg.head_dim)
+        k = F.linear(x, w["k"]).view(-1, cfg.kv_heads, cfg.head_dim)
+        v = F.linear(x, w["v"]).view(-1, cfg.kv_heads, cfg.head_dim)
+        gates = torch.sigmoid(F.linear(x, w["g"])).view(-1, cfg.kv_heads, cfg.groups, 3)
+        q, k = rotary(q, k, positions, self.inv_freq)
+        query = q.reshape(-1, cfg.kv_heads, cfg.groups, cfg.head_dim)
+        records = torch.cat((k, v), -1).contiguous()
+        total = old + len(records)
+        compressed, tail = ops.append_compressed(st.summaries[index], st.tails[index], records,
+                                                 cfg.block_size)
+        cmp_out, blocks = ops.compressed_attention_select(
+            query, compressed, positions, total, cfg.block_size, cfg.block_counts)
+        window_kv = torch.cat((st.windows[index], records))
+        window_start = old - len(st.windows[index])
+        base = st.row + index * cfg.kv_heads
+        fetches = [dict(row=base + h, cached_length=old, history_length=old,
+                        current_kv=records[:, h].contiguous()) for h in range(cfg.kv_heads)]
+        mixed, counters = self.transport.run(
+            query, blocks, positions, fetches, cfg.block_size, window=cfg.window,
+            window_kv=window_kv, window_start=window_start, compressed=cmp_out, gates=gates)
+        self.counters.append(counters)
+        hidden = hidden + F.linear(mixed.reshape(len(hidden), -1), w["o"])
+        x = rms_norm(hidden, w["post_norm"], cfg.rms_eps)
+        hidden = hidden + F.linear(F.silu(F.linear(x, w["gate"])) * F.linear(x, w["up"]),
+                                   w["down"])
+        if append:
+            self._append(index, st, records, compressed, tail, window_kv)
+        return hidden
+
+    def _append(self, index, st, records, compressed, tail, window_kv):
+        """Persist this chunk as history: pool write, slot table, summaries, window."""
+        cfg = self.cfg
+        old = st.length
+        for h in range(cfg.kv_heads):
+            slots = self.pool.token_slots(st.pages[index][h], old, old + len(records))
+            self.pool.write_many(slots, records[:, h].contiguous(), asynchronous=True)
+            self.cache.append_slots(st.row + index * cfg.kv_heads + h, old, slots)
+        st.summaries[index], st.tails[index] = compressed, tail
+        st.windows[index] = window_kv[max(0, len(window_kv) - cfg.window + 1):].clone()
+
+    # -- public entry points -----------------------------------------------------
+    def forward(self, token_ids, positions, user="user", *, append=False):
+        """Run the layers over ``token_ids`` (int64, device) at ``positions``."""
+        st = self.user(user)
+        hidden = F.embedding(token_ids, self.embed)
+        for index in range(self.cfg.layers):
+            hidden = self._layer(index, hidden, positions, st, append=append)
+        if append:
+            st.length += len(token_ids)
+        return rms_norm(hidden, self.final_norm, self.cfg.rms_eps)
+
+    def prefill(self, token_ids, user="user"):
+        """Push a history through the model chunk by chunk, persisting its KV."""
+        st = self.user(user)
+        for begin in range(0, len(token_ids), self.chunk):
+            ids = token_ids[begin:begin + self.chunk]
+            positions = torch.arange(st.length, st.length + len(ids), device=self.device)
+            self.forward(ids, positions, user, append=True)
+            self.counters.clear()
+        self.pool.flush_read_stats()
+        torch.cuda.synchronize(self.device)
+
+    def extend(self, token_ids, user="user"):
+        """GR candidate suffix over the stored history (history is not appended)."""
+        st = self.user(user)
+        positions = torch.arange(st.length, st.length + len(token_ids), device=self.device)
+        return self.forward(token_ids, positions, user, append=False)
+
+    def capture_extend(self, extend_tokens, user="user", warmup=2):
+        """Capture one extend forward in a CUDA graph with static input/output."""
+        st = self.user(user)
+        static_ids = torch.zeros(extend_tokens, dtype=torch.int64, device=self.device)
+        positions = torch.arange(st.length, st.length + extend_tokens, device=self.device)
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                self.counters.clear()
+                self.forward(static_ids, positions, user)
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        torch.cuda.synchronize(self.device)
+        self.counters.clear()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            static_out = self.forward(static_ids, positions, user)
+        graph_counters = list(self.counters)
+        self.counters.clear()
+        return graph, static_ids, static_out, graph_counters
+
+    def close(self):
+        self.transport.close()
+        self.pool.close()

@@ -122,6 +122,10 @@ class GRSelectedTransport:
         self.last_stats = {}
         self._capacity_cache = {}
         self._capture_stream = None
+        self._graph_refs = []
+        # When a list, eager calls append (start, end, workspace) CUDA events
+        # bracketing the fetch/attend launch on its stream (bench roofline).
+        self.kernel_timing = None
 
     # -- reference surface -----------------------------------------------
     def refusal(self, queries, cached, heads, groups, width, bs):
@@ -233,8 +237,15 @@ class GRSelectedTransport:
             window_len=w["window_shape"][0] if w["window_shape"] else 0,
             gate=1 if w["window_shape"] else 0, window_start=window_start,
             spin_limit=self.spin_limit)
+        timing = self.kernel_timing is not None and not torch.cuda.is_current_stream_capturing()
+        if timing:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
         _lib.check(_lib.lib().cxs_fetch_attend(geometry, w["c_attend_buffers"],
                                                stream.cuda_stream))
+        if timing:
+            end.record(stream)
+            self.kernel_timing.append((start, end, w))
 
     # -- main entry --------------------------------------------------------
     def run(self, query, blocks, positions, fetches, block_size, *, trace=False,
@@ -254,10 +265,16 @@ class GRSelectedTransport:
         begin = time.perf_counter_ns()
         device = query.device
         stream = torch.cuda.current_stream(device)
-        if self.submitted:
-            stream.wait_event(self.last_done)
-        if self.cache.has_last_use:
-            stream.wait_event(self.cache.last_use)
+        # Inside a caller's CUDA-graph capture (a whole captured forward) the
+        # stream order already serialises calls; events are not recorded.
+        capturing = torch.cuda.is_current_stream_capturing()
+        if capturing and self.cuda_graphs:
+            raise ValueError("cuda_graphs=True cannot nest inside a caller's capture")
+        if not capturing:
+            if self.submitted:
+                stream.wait_event(self.last_done)
+            if self.cache.has_last_use:
+                stream.wait_event(self.cache.last_use)
         q_count, heads, width = blocks.shape
         qb = query_bucket(q_count)
         window_shape = (len(window_kv), window) if fused else None
@@ -279,6 +296,8 @@ class GRSelectedTransport:
                 self.descriptors.popitem(last=False)
         else:
             self.descriptors.move_to_end(layout)
+        if capturing:
+            self._graph_refs.append(host_desc)  # the captured copy reads this buffer
         w["desc"].copy_(host_desc, non_blocking=True)
         if fused:
             w["window_kv"].copy_(window_kv)
@@ -306,11 +325,13 @@ class GRSelectedTransport:
             self._execute(w, window_start, window)
         counters = DeferredLayerCounters(w["stats"].clone(), 1, self.pool.backend,
                                          w["error"].clone())
-        self.pool._pending_read_counts.append((w["region_counts"].clone(), 1))
+        if not capturing:
+            self.pool._pending_read_counts.append((w["region_counts"].clone(), 1))
         if self.hot_policy == "frequency":
             self.active_plan.retain_hot(w, w["kv"], stream)
-        self.last_done.record(stream)
-        self.cache.last_use.record(stream)
+        if not capturing:
+            self.last_done.record(stream)
+            self.cache.last_use.record(stream)
         self.cache.has_last_use = self.submitted = True
         self.cache.planner_calls += 1
         self.calls += 1

@@ -56,6 +56,9 @@ enum cxs_status {
 
 int cxs_abi_version(void);
 const char* cxs_last_error(void);
+/* Kernels this library has enqueued so far in this process (diagnostic; a
+ * CUDA-graph replay re-runs captured launches without counting them again). */
+int64_t cxs_launch_count(void);
 
 /* ------------------------------------------------------------------ pool ---
  * Backing pool outside HBM: NUMA-local pinned host memory, registered for
