@@ -34,14 +34,17 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
-    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=("ours", "reference"))
     p.add_argument("--history", type=int, default=16384)
     p.add_argument("--extend", type=int, default=256)
     p.add_argument("--layers", type=int, default=16)
     p.add_argument("--read-order", default="consumption_depth")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile-step", action="store_true",
+                   help="after prefill, run one eager extend inside the NVTX range "
+                        "'profile_step' and exit (for ncu --nvtx-include profile_step/)")
     return p.parse_args()
 
 
@@ -65,7 +68,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(gpu), "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+                 "-i", str(gpu), "-lms", "50"], stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
 
@@ -82,7 +85,8 @@ class ClockSampler:
         sm = [float(r[1]) for r in rows]
         max_sm = max(float(r[2]) for r in rows)
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v})
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9])
+                          if v.strip() == "Active"})
         loaded = [s for s, r in zip(sm, rows) if float(r[3]) > 200] or sm
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max_sm, "reasons": reasons,
                 "samples": len(rows)}
@@ -200,9 +204,19 @@ def run_ours(args):
     t0 = time.perf_counter()
     model.prefill(history)
     prefill_s = time.perf_counter() - t0
-    launches_before = _lib.lib().cxs_launch_count()
+    if args.profile_step:
+        ids = candidates.to(device)
+        for _ in range(args.warmup):
+            model.extend(ids)
+        torch.cuda.synchronize(device)
+        torch.cuda.nvtx.range_push("profile_step")
+        model.extend(ids)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize(device)
+        model.close()
+        return None
     graph, static_ids, static_out, counters = model.capture_extend(args.extend)
-    launches_per_step = _lib.lib().cxs_launch_count() - launches_before
+    launches_per_step = model.captured_launches
     static_ids.copy_(candidates.to(device))
     pcie = measure_pcie(torch, device)
 

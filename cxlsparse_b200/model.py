@@ -217,9 +217,13 @@ class NSAExtendModel:
         torch.cuda.current_stream(self.device).wait_stream(stream)
         torch.cuda.synchronize(self.device)
         self.counters.clear()
+        from . import _lib
+
         graph = torch.cuda.CUDAGraph()
+        before = _lib.lib().cxs_launch_count()
         with torch.cuda.graph(graph, stream=stream):
             static_out = self.forward(static_ids, positions, user)
+        self.captured_launches = _lib.lib().cxs_launch_count() - before
         graph_counters = list(self.counters)
         self.counters.clear()
         return graph, static_ids, static_out, graph_counters
