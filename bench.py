@@ -194,6 +194,7 @@ def run_ours(args):
     torch.cuda.set_device(device)
     from cxlsparse_b200 import _lib
     from cxlsparse_b200.model import NSAConfig, NSAExtendModel
+    from cxlsparse_b200.sharding import gather_scores
 
     cfg = NSAConfig(layers=args.layers)
     model = NSAExtendModel(cfg, device=device, seed=0, max_history=args.history + args.extend,
@@ -271,7 +272,7 @@ def run_ours(args):
         graph.replay()
         last = static_out[-1]
         if dist is not None:
-            dist.all_gather_into_tensor(gathered, last.contiguous())
+            gathered.copy_(gather_scores(last))
         else:
             gathered[0].copy_(last)
         host_out.copy_(gathered, non_blocking=True)
