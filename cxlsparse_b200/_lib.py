@@ -107,6 +107,8 @@ def lib():
             "cxs_fetch_attend": (c_i32, [ctypes.POINTER(AttendGeometry),
                                          ctypes.POINTER(AttendBuffers), c_vp]),
             "cxs_attend_capacity": (c_i32, [c_i32, ctypes.POINTER(c_i32)]),
+            "cxs_fetch_attend_noalloc": (c_i32, [ctypes.POINTER(AttendGeometry),
+                                                 ctypes.POINTER(AttendBuffers), c_vp]),
             "cxs_compressed_select": (c_i32, [c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_i32,
                                               c_i32, c_i64, c_vp, c_vp, c_vp, c_vp]),
             "cxs_block_summaries": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
@@ -148,5 +150,6 @@ def exported_symbols():
     return ("cxs_abi_version", "cxs_last_error", "cxs_launch_count", "cxs_pool_create", "cxs_pool_destroy",
             "cxs_pool_register", "cxs_pool_unregister", "cxs_device_numa_node",
             "cxs_pool_write", "cxs_plan_check", "cxs_plan", "cxs_plan_commit_hot",
-            "cxs_fetch_attend", "cxs_attend_capacity", "cxs_compressed_select",
+            "cxs_fetch_attend", "cxs_attend_capacity", "cxs_fetch_attend_noalloc",
+            "cxs_compressed_select",
             "cxs_block_summaries")

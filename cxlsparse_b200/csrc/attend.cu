@@ -8,6 +8,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "cxs_common.cuh"
 #include "tile_attn.cuh"
 
@@ -465,4 +467,69 @@ extern "C" int cxs_attend_capacity(int32_t block_size, int32_t* attention_warps)
   if (status != CXS_OK) return status;
   *attention_warps = grid * kAttnWarps;
   return CXS_OK;
+}
+
+// ------------------------------------------------ allocation-free variant ---
+// Scratch for cxs_fetch_attend_noalloc: per-block bulk sources, source kinds
+// and ready flags plus the IO work cursor, for at most
+// CXS_NOALLOC_MAX_PHYSICAL blocks. Every GPU that loads this library holds it
+// until the process exits; all calls on a device share it.
+namespace {
+
+constexpr size_t kScratchSources = 0;
+constexpr size_t kScratchKinds = kScratchSources + 8ull * CXS_NOALLOC_MAX_PHYSICAL;
+constexpr size_t kScratchReady = kScratchKinds + 4ull * CXS_NOALLOC_MAX_PHYSICAL;
+constexpr size_t kScratchControl = kScratchReady + 4ull * CXS_NOALLOC_MAX_PHYSICAL;
+constexpr size_t kScratchBytes = kScratchControl + 256;
+
+static __device__ __align__(256) unsigned char g_attend_scratch[kScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+unsigned char* g_scratch_address[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (the host-side symbol itself is not a device address).
+int scratch_address(unsigned char** out) {
+  int device = 0;
+  CXS_CUDA(cudaGetDevice(&device));
+  if (device < 0 || device >= kMaxDevices)
+    return set_error(CXS_ERR_UNSUPPORTED, "device index %d beyond %d", device, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_address[device]) {
+    void* address = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&address, g_attend_scratch);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(CXS_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    }
+    g_scratch_address[device] = static_cast<unsigned char*>(address);
+  }
+  *out = g_scratch_address[device];
+  return CXS_OK;
+}
+
+}  // namespace
+
+extern "C" int cxs_fetch_attend_noalloc(const cxs_attend_geometry* geometry,
+                                        const cxs_attend_buffers* buffers, void* stream) {
+  if (!geometry || !buffers) return set_error(CXS_ERR_INVALID, "null attend argument");
+  if (geometry->physical > CXS_NOALLOC_MAX_PHYSICAL)
+    return set_error(CXS_ERR_CAPACITY,
+                     "cxs_fetch_attend_noalloc handles at most %d physical blocks (got %d); "
+                     "use cxs_fetch_attend with caller-provided scratch",
+                     CXS_NOALLOC_MAX_PHYSICAL, geometry->physical);
+  if (!buffers->error) return set_error(CXS_ERR_INVALID, "error word output required");
+  unsigned char* scratch = nullptr;
+  int status = scratch_address(&scratch);
+  if (status != CXS_OK) return status;
+  // Same launches as cxs_fetch_attend; only the scratch arrays change. The
+  // prepare kernel rewrites sources, kinds and ready for every block and
+  // zeroes the IO cursor and the error word before the IO/attention kernel.
+  cxs_attend_buffers b = *buffers;
+  b.sources = reinterpret_cast<int64_t*>(scratch + kScratchSources);
+  b.kinds = reinterpret_cast<int32_t*>(scratch + kScratchKinds);
+  b.ready = reinterpret_cast<int32_t*>(scratch + kScratchReady);
+  b.control = reinterpret_cast<int32_t*>(scratch + kScratchControl);
+  return cxs_fetch_attend(geometry, &b, stream);
 }

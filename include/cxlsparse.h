@@ -233,6 +233,27 @@ int cxs_fetch_attend(const cxs_attend_geometry* geometry, const cxs_attend_buffe
  * models the real consumers (tma/transport.py:63 uses min(rows, 256)). */
 int cxs_attend_capacity(int32_t block_size, int32_t* attention_warps);
 
+/* Allocation-free variant of cxs_fetch_attend. No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory
+ * themselves, for example a plugin inside a host process whose own allocator
+ * owns all of the GPU's memory, or code that must not call cudaMalloc after
+ * start-up because cudaMalloc can synchronise the whole device.
+ *
+ * The caller passes the same geometry and buffers as for cxs_fetch_attend
+ * (inputs, the staging buffer `kv`, `out` and the `error` word), but
+ * `sources`, `kinds`, `ready` and `control` are ignored: that scratch lives in
+ * a static device array of this library sized for CXS_NOALLOC_MAX_PHYSICAL
+ * blocks (about 256 KiB on every GPU that loads the library, held until the
+ * process exits). Larger geometries are rejected with CXS_ERR_CAPACITY.
+ * The first call on each device looks up the array's device address with
+ * that device current; make that first call before any stream capture.
+ * All calls share the one array and each call re-initialises it, so calls
+ * that overlap on the GPU (different streams, or another thread) race and
+ * must be serialised by the caller. Nothing is allocated by this entry point. */
+#define CXS_NOALLOC_MAX_PHYSICAL 16384
+int cxs_fetch_attend_noalloc(const cxs_attend_geometry* geometry,
+                             const cxs_attend_buffers* buffers, void* stream);
+
 /* -------------------------------------------- compressed branch + top-n ---
  * Compressed-token attention over complete summaries and top-n block
  * selection from the summed GQA probabilities (models/nsa/ops.py:73-123;
