@@ -207,11 +207,12 @@ def run_ours(args):
     prefill_s = time.perf_counter() - t0
     if args.profile_step:
         ids = candidates.to(device)
+        model.prepare_fast(args.extend)
         for _ in range(args.warmup):
-            model.extend(ids)
+            model.extend_fast(ids)
         torch.cuda.synchronize(device)
         torch.cuda.nvtx.range_push("profile_step")
-        model.extend(ids)
+        model.extend_fast(ids)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(device)
         model.close()
@@ -284,7 +285,7 @@ def run_ours(args):
     # --- fused fetch/attend kernel timing (eager step, events on its stream)
     model.transport.kernel_timing = []
     model.counters.clear()
-    model.extend(static_ids)
+    model.extend_fast(static_ids)
     torch.cuda.synchronize(device)
     durations = [s.elapsed_time(e) for s, e, _ in model.transport.kernel_timing]
     model.transport.kernel_timing = None

@@ -112,6 +112,10 @@ def lib():
             "cxs_compressed_select": (c_i32, [c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_i32,
                                               c_i32, c_i64, c_vp, c_vp, c_vp, c_vp]),
             "cxs_block_summaries": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
+            "cxs_rms_norm": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, ctypes.c_float, c_vp]),
+            "cxs_qkv_rope": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp,
+                                     c_i32, c_vp, c_i32, c_vp, c_vp]),
+            "cxs_silu_mul": (c_i32, [c_vp, c_i32, c_i32, c_vp, c_vp]),
         }
         for name, (restype, argtypes) in sigs.items():
             fn = getattr(handle, name)
@@ -152,4 +156,4 @@ def exported_symbols():
             "cxs_pool_write", "cxs_plan_check", "cxs_plan", "cxs_plan_commit_hot",
             "cxs_fetch_attend", "cxs_attend_capacity", "cxs_fetch_attend_noalloc",
             "cxs_compressed_select",
-            "cxs_block_summaries")
+            "cxs_block_summaries", "cxs_rms_norm", "cxs_qkv_rope", "cxs_silu_mul")

@@ -442,39 +442,56 @@ __global__ void __launch_bounds__(1024) publish_kernel(Geo g, cxs_plan_buffers b
 
 // --------------------------------------------------------------- hot top-k ---
 // Top-`hot` indices of a head's frequency table by (frequency desc, index asc)
-// (active.py:449-500; stable argsort fallback active.py:884-888): radix-select
-// the threshold frequency, keep every larger one and the lowest-index ties,
-// then sort the `hot` winners.
+// (active.py:449-500; stable argsort fallback active.py:884-888): find the
+// threshold frequency by a radix select over the significant bytes of the
+// maximum, keep every larger frequency and the lowest-index ties, then sort
+// the `hot` winners. Histograms use warp-aggregated shared atomics because
+// most frequencies share a few small values.
 template <int ITEMS>
 __global__ void __launch_bounds__(1024) hot_select_kernel(Geo g, cxs_plan_buffers b) {
   typedef cub::BlockRadixSort<unsigned long long, 1024, ITEMS> Sort;
   typedef cub::BlockScan<int, 1024> Scan;
+  typedef cub::BlockReduce<unsigned int, 1024> Reduce;
   extern __shared__ __align__(16) unsigned char sort_mem[];
   auto& temp = *reinterpret_cast<typename Sort::TempStorage*>(sort_mem);
   __shared__ typename Scan::TempStorage scan;
+  __shared__ typename Reduce::TempStorage reduce;
   __shared__ int hist[256];
-  __shared__ unsigned int prefix_s, mask_s;
-  __shared__ int remaining_s, chosen_count, eq_taken;
+  __shared__ unsigned int prefix_s, mask_s, max_s;
+  __shared__ int remaining_s, greater_base, equal_base;
   __shared__ unsigned long long cand[kMaxHot];
   int h = blockIdx.x;
+  int lane = threadIdx.x & 31;
   const int32_t* freq = b.frequencies + (long long)h * g.SORT;
   int n = g.SORT;
+  unsigned int local_max = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) local_max = max(local_max, (unsigned)freq[i]);
+  unsigned int fmax = Reduce(reduce).Reduce(local_max, cub::Max());
   if (threadIdx.x == 0) {
+    max_s = fmax;
     prefix_s = 0;
-    mask_s = 0;
     remaining_s = g.HOT;
-    chosen_count = 0;
-    eq_taken = 0;
+    greater_base = 0;
+    equal_base = 0;
+    int top = 0;  // highest byte holding a set bit of the maximum
+    while (top < 24 && (fmax >> (top + 8))) top += 8;
+    mask_s = top >= 24 ? 0u : ~((1u << (top + 8)) - 1u);  // bytes above `top` are zero
+    hist[0] = top;                                        // smuggle `top` to all threads
   }
   __syncthreads();
-  // Radix select over the 31-bit frequency, most significant byte first.
-  for (int shift = 24; shift >= 0; shift -= 8) {
+  int top = hist[0];
+  __syncthreads();
+  for (int shift = top; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     unsigned int prefix = prefix_s, mask = mask_s;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      unsigned int f = (unsigned int)freq[i];
-      if ((f & mask) == prefix) atomicAdd(&hist[(f >> shift) & 255], 1);
+    for (int base = 0; base < n; base += blockDim.x) {
+      int i = base + threadIdx.x;
+      unsigned int f = i < n ? (unsigned)freq[i] : 0u;
+      bool active = i < n && (f & mask) == prefix;
+      unsigned int digit = active ? (f >> shift) & 255u : 256u + lane;
+      unsigned peers = __match_any_sync(0xffffffffu, digit);
+      if (active && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -491,26 +508,25 @@ __global__ void __launch_bounds__(1024) hot_select_kernel(Geo g, cxs_plan_buffer
     __syncthreads();
   }
   unsigned int threshold = prefix_s;
-  int need_eq = remaining_s;  // ties at the threshold, lowest indices first
-  // Gather: every frequency above the threshold, plus the first ties in index order.
+  int need_eq = remaining_s;                 // ties at the threshold, lowest indices first
+  int greater_total = g.HOT - need_eq;       // every frequency above the threshold
+  // Ordered gather: one scan per chunk of (greater, equal) counts packed in an int.
   for (int base = 0; base < n; base += blockDim.x) {
     int i = base + threadIdx.x;
-    unsigned int f = i < n ? (unsigned int)freq[i] : 0u;
+    unsigned int f = i < n ? (unsigned)freq[i] : 0u;
     bool greater = i < n && f > threshold;
     bool equal = i < n && f == threshold;
-    if (greater) {
-      int slot = atomicAdd(&chosen_count, 1);
-      cand[slot] = ((unsigned long long)(0x7FFFFFFFu - f) << 32) | (unsigned int)i;
-    }
-    int eq_prefix, eq_total;
-    Scan(scan).ExclusiveSum((int)equal, eq_prefix, eq_total);
-    int taken = eq_taken;
-    if (equal && taken + eq_prefix < need_eq) {
-      int slot = atomicAdd(&chosen_count, 1);
-      cand[slot] = ((unsigned long long)(0x7FFFFFFFu - f) << 32) | (unsigned int)i;
-    }
+    int packed = (greater ? 1 : 0) + (equal ? (1 << 16) : 0), prefix, total;
+    Scan(scan).ExclusiveSum(packed, prefix, total);
+    unsigned long long key = ((unsigned long long)(0x7FFFFFFFu - f) << 32) | (unsigned int)i;
+    if (greater) cand[greater_base + (prefix & 0xFFFF)] = key;
+    int eq_rank = equal_base + (prefix >> 16);
+    if (equal && eq_rank < need_eq) cand[greater_total + eq_rank] = key;
     __syncthreads();
-    if (threadIdx.x == 0) eq_taken = taken + eq_total;
+    if (threadIdx.x == 0) {
+      greater_base += total & 0xFFFF;
+      equal_base += total >> 16;
+    }
     __syncthreads();
   }
   unsigned long long keys[ITEMS];

@@ -277,6 +277,26 @@ int cxs_compressed_select(const void* query,      /* [Q, H, 16, 64] bf16 */
 int cxs_block_summaries(const void* tokens, int64_t count, int32_t heads, int32_t block_size,
                         void* summaries, void* stream);
 
+/* ------------------------------------------------------- layer glue ---
+ * Fused elementwise steps around the cuBLAS projections of one NSA layer,
+ * keeping the reference's bf16 rounding sequence
+ * (models/tensor_ops.py:6-26, models/nsa/model.py:440-492). */
+
+/* out[r] = bf16(bf16(x[r] * rsqrt(mean(x[r]^2) + eps)) * weight), bf16 rows. */
+int cxs_rms_norm(const void* x, const void* weight, void* out, int32_t rows, int32_t dim,
+                 float eps, void* stream);
+/* From the fused projection [tokens, q_heads*64 | kv*64 (k) | kv*64 (v) | q_heads*3 (g)]
+ * (row stride proj_stride elements): rotary q/k (rotate-half, inv_freq [32]),
+ * write query [tokens, q_heads, 64], records [tokens, kv, 128] (K || V, row
+ * stride records_stride), per-head current KV [kv][tokens, 128] (head stride
+ * current_stride) and sigmoid gates [tokens, q_heads * 3]. */
+int cxs_qkv_rope(const void* proj, int32_t proj_stride, const int32_t* positions,
+                 const float* inv_freq, int32_t tokens, int32_t q_heads, int32_t kv_heads,
+                 void* query, void* records, int32_t records_stride, void* current,
+                 int32_t current_stride, void* gates, void* stream);
+/* out[r, c] = bf16(silu(gate_up[r, c])) * gate_up[r, ffn + c] (SwiGLU). */
+int cxs_silu_mul(const void* gate_up, int32_t rows, int32_t ffn, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

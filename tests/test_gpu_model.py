@@ -23,6 +23,9 @@ def test_prefill_then_extend_graph_matches_eager(cuda):
         # The pool holds exactly the records the cache slot table points at.
         assert (model.cache.host_locs[: cfg.layers * cfg.kv_heads, :2048] >= 0).all()
         eager = model.extend(ids).clone()
+        model.prepare_fast(64)
+        fast = model.extend_fast(ids).clone()
+        torch.testing.assert_close(fast.float(), eager.float(), rtol=0.02, atol=0.02)
         graph, static_ids, static_out, counters = model.capture_extend(64)
         static_ids.copy_(ids)
         graph.replay()
