@@ -101,6 +101,11 @@ def lib():
             "cxs_plan_check": (c_i32, [ctypes.POINTER(PlanGeometry)]),
             "cxs_plan": (c_i32, [ctypes.POINTER(PlanGeometry), ctypes.POINTER(PlanBuffers),
                                  c_vp]),
+            "cxs_plan_core": (c_i32, [ctypes.POINTER(PlanGeometry), ctypes.POINTER(PlanBuffers),
+                                      c_vp]),
+            "cxs_plan_select_commit_hot": (c_i32, [ctypes.POINTER(PlanGeometry),
+                                                   ctypes.POINTER(PlanBuffers), c_vp, c_vp,
+                                                   c_vp, c_vp]),
             "cxs_plan_commit_hot": (c_i32, [ctypes.POINTER(PlanGeometry),
                                             ctypes.POINTER(PlanBuffers), c_vp, c_vp, c_vp,
                                             c_vp]),
@@ -153,7 +158,8 @@ def exported_symbols():
     """Names the header declares (used by the CPU symbol test)."""
     return ("cxs_abi_version", "cxs_last_error", "cxs_launch_count", "cxs_pool_create", "cxs_pool_destroy",
             "cxs_pool_register", "cxs_pool_unregister", "cxs_device_numa_node",
-            "cxs_pool_write", "cxs_plan_check", "cxs_plan", "cxs_plan_commit_hot",
+            "cxs_pool_write", "cxs_plan_check", "cxs_plan", "cxs_plan_core",
+            "cxs_plan_select_commit_hot", "cxs_plan_commit_hot",
             "cxs_fetch_attend", "cxs_attend_capacity", "cxs_fetch_attend_noalloc",
             "cxs_compressed_select",
             "cxs_block_summaries", "cxs_rms_norm", "cxs_qkv_rope", "cxs_silu_mul")

@@ -48,6 +48,31 @@ struct AttendArgs {
   __nv_bfloat16* out;
 };
 
+// Warp gather of one BS-token block: token t comes from address[t] (HBM or
+// host-mapped pool memory, 256 contiguous bytes) when t < count and the
+// address is set, otherwise zeros. Loads are issued in independent batches of
+// eight 16-byte vectors per lane so that their latencies overlap.
+template <int BS>
+__device__ __forceinline__ void gather_block(const int64_t* __restrict__ address, int count,
+                                             uint4* __restrict__ dst, int lane) {
+  constexpr int kPerLane = BS * 16 / 32;  // 16-byte vectors per lane
+  constexpr int kBatch = kPerLane < 8 ? kPerLane : 8;
+#pragma unroll
+  for (int b0 = 0; b0 < kPerLane; b0 += kBatch) {
+    uint4 value[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      int i = lane + 32 * (b0 + k);
+      int t = i >> 4, v = i & 15;
+      long long src = address[t];
+      value[k] = make_uint4(0, 0, 0, 0);
+      if (t < count && src != 0) value[k] = __ldcv(reinterpret_cast<const uint4*>(src) + v);
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) dst[lane + 32 * (b0 + k)] = value[k];
+  }
+}
+
 // ---------------------------------------------------------------- prepare ---
 // One warp per physical block: classify (0 resident, 1 full contiguous
 // aligned external block, 2 mixed/tail external block), gather resident
@@ -81,12 +106,10 @@ __global__ void prepare_kernel(int P, int BS, const int64_t* __restrict__ addres
   }
   if (missing || count <= 0) return;
   // Resident block: every token comes from HBM (hot replica or current KV).
-  for (int i = lane; i < BS * 16; i += 32) {
-    int t = i / 16, v = i % 16;
-    long long src = a[t];
-    uint4 value = make_uint4(0, 0, 0, 0);
-    if (t < count && src != 0) value = reinterpret_cast<const uint4*>(src)[v];
-    dst[i] = value;
+  switch (BS) {
+    case 16: gather_block<16>(a, count, dst, lane); break;
+    case 32: gather_block<32>(a, count, dst, lane); break;
+    default: gather_block<64>(a, count, dst, lane); break;
   }
 }
 
@@ -141,18 +164,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         phase ^= 1;
       } else {
         // Mixed-tier or tail block: 16-byte vector gathers, tail zero-filled.
-        const int64_t* addr = a.address + (long long)block * BS;
-        int count = a.valid[block];
-        uint4* out = reinterpret_cast<uint4*>(dst);
-        constexpr int kVectors = BS * 16;
-#pragma unroll 4
-        for (int i = lane; i < kVectors; i += 32) {
-          int t = i / 16, v = i % 16;
-          long long src = addr[t];
-          uint4 value = make_uint4(0, 0, 0, 0);
-          if (t < count && src != 0) value = reinterpret_cast<const uint4*>(src)[v];
-          out[i] = value;
-        }
+        gather_block<BS>(a.address + (long long)block * BS, a.valid[block],
+                         reinterpret_cast<uint4*>(dst), lane);
         __threadfence();
         cxs::fence_proxy_async_global();
         __syncwarp();

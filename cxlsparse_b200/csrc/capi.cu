@@ -162,13 +162,23 @@ extern "C" int cxs_pool_write(const void* records, const int64_t* slots, int64_t
 }
 
 // Mean of BS consecutive tokens per (summary, head, channel), fp32 accumulate.
+// 128 channels x 8 token groups per CTA; partial sums reduced in shared memory.
 __global__ void block_summaries_kernel(const __nv_bfloat16* __restrict__ tokens, int heads,
                                        int bs, __nv_bfloat16* __restrict__ out) {
-  int summary = blockIdx.x, head = blockIdx.y, c = threadIdx.x;  // 128 channels
+  __shared__ float partial[8][128];
+  int summary = blockIdx.x, head = blockIdx.y;
+  int c = threadIdx.x & 127, group = threadIdx.x >> 7;
   const __nv_bfloat16* base = tokens + ((int64_t)summary * bs * heads + head) * 128 + c;
   float acc = 0.f;
-  for (int t = 0; t < bs; ++t) acc += __bfloat162float(base[(int64_t)t * heads * 128]);
-  out[((int64_t)summary * heads + head) * 128 + c] = __float2bfloat16_rn(acc / (float)bs);
+  for (int t = group; t < bs; t += 8) acc += __bfloat162float(base[(int64_t)t * heads * 128]);
+  partial[group][c] = acc;
+  __syncthreads();
+  if (group == 0) {
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sum += partial[k][c];
+    out[((int64_t)summary * heads + head) * 128 + c] = __float2bfloat16_rn(sum / (float)bs);
+  }
 }
 
 extern "C" int cxs_block_summaries(const void* tokens, int64_t count, int32_t heads,
@@ -178,7 +188,7 @@ extern "C" int cxs_block_summaries(const void* tokens, int64_t count, int32_t he
   int64_t n = count / block_size;
   if (!n) return CXS_OK;
   dim3 grid((unsigned)n, heads);
-  block_summaries_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(
+  block_summaries_kernel<<<grid, 1024, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)tokens, heads, block_size, (__nv_bfloat16*)summaries);
   CXS_LAUNCH_CHECK("block_summaries_kernel");
   return CXS_OK;

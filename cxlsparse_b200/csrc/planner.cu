@@ -759,8 +759,21 @@ extern "C" int cxs_plan_check(const cxs_plan_geometry* geometry) {
   return check_geometry(geometry, &g);
 }
 
+static int plan_impl(const cxs_plan_geometry* geometry, const cxs_plan_buffers* buffers,
+                     void* stream_ptr, bool hot);
+
 extern "C" int cxs_plan(const cxs_plan_geometry* geometry, const cxs_plan_buffers* buffers,
                         void* stream_ptr) {
+  return plan_impl(geometry, buffers, stream_ptr, true);
+}
+
+extern "C" int cxs_plan_core(const cxs_plan_geometry* geometry, const cxs_plan_buffers* buffers,
+                             void* stream_ptr) {
+  return plan_impl(geometry, buffers, stream_ptr, false);
+}
+
+static int plan_impl(const cxs_plan_geometry* geometry, const cxs_plan_buffers* buffers,
+                     void* stream_ptr, bool hot) {
   Geo g;
   int status = check_geometry(geometry, &g);
   if (status != CXS_OK) return status;
@@ -827,13 +840,30 @@ extern "C" int cxs_plan(const cxs_plan_geometry* geometry, const cxs_plan_buffer
     case 8: status = launch_publish<8>(g, b, bound, end_bit, stream); break;
     default: status = launch_publish<16>(g, b, bound, end_bit, stream); break;
   }
-  if (status != CXS_OK) return status;
+  if (status != CXS_OK || !hot) return status;
   switch (sort_items(g.HOT)) {
     case 1: status = launch_hot<1>(g, b, stream); break;
     case 2: status = launch_hot<2>(g, b, stream); break;
     default: status = launch_hot<4>(g, b, stream); break;
   }
   return status;
+}
+
+extern "C" int cxs_plan_select_commit_hot(const cxs_plan_geometry* geometry,
+                                          const cxs_plan_buffers* buffers, const void* kv,
+                                          int32_t* tags, void* hot_data, void* stream_ptr) {
+  Geo g;
+  int status = check_geometry(geometry, &g);
+  if (status != CXS_OK) return status;
+  if (!buffers) return set_error(CXS_ERR_INVALID, "null plan buffers");
+  cudaStream_t stream = (cudaStream_t)stream_ptr;
+  switch (sort_items(g.HOT)) {
+    case 1: status = launch_hot<1>(g, *buffers, stream); break;
+    case 2: status = launch_hot<2>(g, *buffers, stream); break;
+    default: status = launch_hot<4>(g, *buffers, stream); break;
+  }
+  if (status != CXS_OK) return status;
+  return cxs_plan_commit_hot(geometry, buffers, kv, tags, hot_data, stream_ptr);
 }
 
 extern "C" int cxs_plan_commit_hot(const cxs_plan_geometry* geometry,

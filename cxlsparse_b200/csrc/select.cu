@@ -9,9 +9,11 @@
 //    score descending with ties to the lower block id; width =
 //    min(count, ceil(total / BS)); remaining entries -1.
 //
-// One warp per (query row, KV head); 64-summary tiles staged by 3-D tensor TMA.
-// Pass 1: online softmax + PV (compressed branch output). Pass 2: recompute
-// scores with the final per-head max / normaliser and reduce over heads.
+// One CTA of 4 warps per (query row, KV head); the warps split the 64-summary
+// tiles (staged by 3-D tensor TMA). Pass 1: per-warp online softmax + PV,
+// merged across warps in shared memory (compressed branch output). Pass 2:
+// scores recomputed with the merged per-head max / normaliser, reduced over
+// heads; warp 0 selects the top-n.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -43,15 +45,16 @@ struct SelectArgs {
 
 __global__ void __launch_bounds__(kWarps * 32)
     compressed_select_kernel(const __grid_constant__ CUtensorMap map, SelectArgs a) {
+  // One CTA per (query row, KV head); warp w owns summary tiles w, w + 4, ...
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   int score_len = a.score_len;
   uint8_t* k_tile = smem + warp * 2 * kTileBytes;
   uint8_t* v_tile = k_tile + kTileBytes;
-  float* scores = reinterpret_cast<float*>(smem + kWarps * 2 * kTileBytes) + warp * score_len;
-  uint64_t* bars =
-      reinterpret_cast<uint64_t*>(smem + kWarps * 2 * kTileBytes + kWarps * score_len * 4);
+  float* scores = reinterpret_cast<float*>(smem + kWarps * 2 * kTileBytes);
+  float* merge = scores + score_len;                    // [kWarps][16 m | 16 l | 16x64 o]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + kWarps * (32 + 16 * 64));
   uint64_t* bar = &bars[warp];
   if (lane == 0) {
     cxs::mbar_init(bar, 1);
@@ -60,20 +63,21 @@ __global__ void __launch_bounds__(kWarps * 32)
   __syncwarp();
   uint32_t k_addr = cxs::smem_addr(k_tile), v_addr = cxs::smem_addr(v_tile);
   uint32_t phase = 0;
-  int row = blockIdx.x * kWarps + warp;
-  if (row >= a.Q * a.H) return;
+  int row = blockIdx.x;
   int q = row / a.H, h = row % a.H;
   int pos = a.positions[q];
   int g = lane >> 2, c = lane & 3;
   int nc = pos >= 0 ? min((pos + 1) / a.BS, a.C) : 0;  // complete summaries
   int tiles = (nc + kTileKeys - 1) / kTileKeys;
   long long spin = 1ll << 31;
+  for (int i = threadIdx.x; i < score_len; i += blockDim.x) scores[i] = 0.f;
   uint32_t qa[4][4];
   cxs::load_query(a.query + (long long)row * cxs::kGroups * cxs::kDim, lane, qa);
-  // Pass 1: online softmax over complete summaries; compressed output.
+  // Pass 1: each warp runs online softmax + PV over its tiles.
   cxs::Softmax<kTileKeys> sm;
   sm.reset();
-  for (int t = 0; t < tiles; ++t) {
+  bool ok = true;
+  for (int t = warp; t < tiles && ok; t += kWarps) {
     if (lane == 0) {
       cxs::fence_proxy_async_shared();
       cxs::mbar_expect_tx(bar, 2 * kTileBytes);
@@ -83,26 +87,64 @@ __global__ void __launch_bounds__(kWarps * 32)
     __syncwarp();
     if (!cxs::mbar_wait_bounded(bar, phase, spin, a.error)) {
       cxs::mbar_wait_bounded(bar, phase, spin, a.error);
-      return;
+      ok = false;
+      break;
     }
     phase ^= 1;
     int base = t * kTileKeys;
     sm.step(qa, k_addr, v_addr, lane, [&](int k) { return base + k < nc; });
     __syncwarp();
   }
-  uint32_t packed[8][2];
-  sm.finish(packed);
-  __nv_bfloat16* orow = a.out + (long long)row * cxs::kGroups * cxs::kDim;
+  // Merge the warps' (max, sum, accumulator) per head through shared memory.
+  float* mine = merge + warp * (32 + 16 * 64);
+  if (c == 0) {
+    mine[g] = sm.m[0];
+    mine[g + 8] = sm.m[1];
+    mine[16 + g] = sm.l[0];
+    mine[16 + g + 8] = sm.l[1];
+  }
 #pragma unroll
   for (int n = 0; n < 8; ++n) {
-    *reinterpret_cast<uint32_t*>(orow + g * 64 + n * 8 + 2 * c) = packed[n][0];
-    *reinterpret_cast<uint32_t*>(orow + (g + 8) * 64 + n * 8 + 2 * c) = packed[n][1];
+    int dim = n * 8 + 2 * c;
+    mine[32 + g * 64 + dim] = sm.o[n][0];
+    mine[32 + g * 64 + dim + 1] = sm.o[n][1];
+    mine[32 + (g + 8) * 64 + dim] = sm.o[n][2];
+    mine[32 + (g + 8) * 64 + dim + 1] = sm.o[n][3];
   }
-  // Pass 2: block scores = sum over heads of exp(s - m) / l.
-  float inv[2] = {sm.l[0] > 0.f ? 1.f / sm.l[0] : 0.f, sm.l[1] > 0.f ? 1.f / sm.l[1] : 0.f};
-  for (int i = lane; i < score_len; i += 32) scores[i] = 0.f;
-  __syncwarp();
-  for (int t = 0; t < tiles; ++t) {
+  __syncthreads();
+  // Global per-head max / normaliser (every warp needs them for pass 2).
+  float gm[2], gl[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    int head = g + r * 8;
+    float m = -INFINITY;
+    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, merge[w * (32 + 16 * 64) + head]);
+    float l = 0.f;
+    for (int w = 0; w < kWarps; ++w) {
+      float mw = merge[w * (32 + 16 * 64) + head];
+      if (mw != -INFINITY) l += merge[w * (32 + 16 * 64) + 16 + head] * expf(mw - m);
+    }
+    gm[r] = m;
+    gl[r] = l;
+  }
+  // Output: 16 heads x 64 dims spread over the CTA's 128 threads.
+  __nv_bfloat16* orow = a.out + (long long)row * cxs::kGroups * cxs::kDim;
+  for (int e = threadIdx.x; e < 16 * 64; e += blockDim.x) {
+    int head = e / 64;
+    float m = -INFINITY, l = 0.f, acc = 0.f;
+    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, merge[w * (32 + 16 * 64) + head]);
+    for (int w = 0; w < kWarps; ++w) {
+      const float* part = merge + w * (32 + 16 * 64);
+      if (part[head] == -INFINITY) continue;
+      float f = expf(part[head] - m);
+      l += part[16 + head] * f;
+      acc += part[32 + e] * f;
+    }
+    orow[e] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
+  }
+  // Pass 2: block scores = sum over heads of exp(s - M) / L with the merged M, L.
+  float inv[2] = {gl[0] > 0.f ? 1.f / gl[0] : 0.f, gl[1] > 0.f ? 1.f / gl[1] : 0.f};
+  for (int t = warp; t < tiles && ok; t += kWarps) {
     if (lane == 0) {
       cxs::fence_proxy_async_shared();
       cxs::mbar_expect_tx(bar, kTileBytes);
@@ -111,11 +153,12 @@ __global__ void __launch_bounds__(kWarps * 32)
     __syncwarp();
     if (!cxs::mbar_wait_bounded(bar, phase, spin, a.error)) {
       cxs::mbar_wait_bounded(bar, phase, spin, a.error);
-      return;
+      ok = false;
+      break;
     }
     phase ^= 1;
-    float s[kTileKeys / 8][4];
-    cxs::score_tile<kTileKeys>(qa, k_addr, lane, s);
+    float sc[kTileKeys / 8][4];
+    cxs::score_tile<kTileKeys>(qa, k_addr, lane, sc);
 #pragma unroll
     for (int nt = 0; nt < kTileKeys / 8; ++nt) {
 #pragma unroll
@@ -123,7 +166,7 @@ __global__ void __launch_bounds__(kWarps * 32)
         int key = t * kTileKeys + nt * 8 + 2 * c + e;
         float p = 0.f;
         if (key < nc)
-          p = expf(s[nt][e] - sm.m[0]) * inv[0] + expf(s[nt][e + 2] - sm.m[1]) * inv[1];
+          p = expf(sc[nt][e] - gm[0]) * inv[0] + expf(sc[nt][e + 2] - gm[1]) * inv[1];
         p += __shfl_xor_sync(0xffffffffu, p, 4);
         p += __shfl_xor_sync(0xffffffffu, p, 8);
         p += __shfl_xor_sync(0xffffffffu, p, 16);
@@ -132,11 +175,13 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
     __syncwarp();
   }
-  __syncwarp();
+  __syncthreads();
   if (a.scores) {
     float* srow = a.scores + (long long)row * a.C;
-    for (int i = lane; i < a.C; i += 32) srow[i] = scores[i];
+    for (int i = threadIdx.x; i < a.C; i += blockDim.x) srow[i] = scores[i];
   }
+  __syncthreads();
+  if (warp != 0) return;
   // Top-n: current block first, then (score desc, block asc) among earlier blocks.
   int32_t* brow = a.blocks + (long long)row * a.width;
   int current = pos >= 0 ? pos / a.BS : -1;
@@ -234,12 +279,13 @@ extern "C" int cxs_compressed_select(const void* query, const void* compressed, 
   if (longest > (1 << 20)) return set_error(CXS_ERR_CAPACITY, "too many blocks");
   int score_len = (int)((longest + 3) & ~3ll);
   a.score_len = score_len;
-  size_t smem = 1024 + (size_t)kWarps * 2 * kTileBytes + (size_t)kWarps * score_len * 4 + kWarps * 8;
+  size_t smem = 1024 + (size_t)kWarps * 2 * kTileBytes + (size_t)score_len * 4 +
+                (size_t)kWarps * (32 + 16 * 64) * 4 + kWarps * 8;
   if (smem > 227 * 1024) return set_error(CXS_ERR_CAPACITY, "too many summaries for one warp");
   CXS_CUDA(cudaFuncSetAttribute(compressed_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)smem));
   int rows = queries * heads;
-  compressed_select_kernel<<<(rows + kWarps - 1) / kWarps, kWarps * 32, smem, (cudaStream_t)stream>>>(
+  compressed_select_kernel<<<rows, kWarps * 32, smem, (cudaStream_t)stream>>>(
       map, a);
   CXS_LAUNCH_CHECK("compressed_select_kernel");
   return CXS_OK;

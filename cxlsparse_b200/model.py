@@ -112,7 +112,7 @@ class NSAExtendModel:
                                    topk=min(cfg.hot, 256), dim=128)
         self.transport = GRSelectedTransport(
             self.cache, read_order=read_order, cross_query_dedup=cross_query_dedup,
-            hot_policy=hot_policy, capacity=cfg.layers + 4)
+            hot_policy=hot_policy, capacity=cfg.layers + 4, async_hot=True)
         self.fast = None
         self.users = {}
         self.counters = []
@@ -291,6 +291,7 @@ class NSAExtendModel:
         hidden = F.embedding(token_ids, self.embed)
         for index in range(self.cfg.layers):
             hidden = self._layer_fast(index, hidden)
+        self.transport.join()
         out = torch.empty_like(hidden)
         _lib.check(_lib.lib().cxs_rms_norm(
             hidden.data_ptr(), self.final_norm.data_ptr(), out.data_ptr(), len(hidden),

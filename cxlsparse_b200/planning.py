@@ -131,11 +131,22 @@ class ActivePlanAdapter:
         w["c_buffers"] = _lib.PlanBuffers(**fields)
         return w["c_buffers"]
 
-    def plan(self, w, stream=None):
-        """Enqueue the full plan on ``stream`` (the current stream by default)."""
+    def plan(self, w, stream=None, *, defer_hot=False):
+        """Enqueue the plan on ``stream`` (current stream by default).
+
+        ``defer_hot`` leaves the hot top-k choice to ``select_and_retain_hot``.
+        """
         stream = stream or torch.cuda.current_stream(self.cache.data.device)
-        _lib.check(_lib.lib().cxs_plan(w["c_geometry"], w["c_buffers"], stream.cuda_stream))
+        fn = _lib.lib().cxs_plan_core if defer_hot else _lib.lib().cxs_plan
+        _lib.check(fn(w["c_geometry"], w["c_buffers"], stream.cuda_stream))
         return w["chosen"]
+
+    def select_and_retain_hot(self, w, kv, stream=None):
+        """Hot top-k choice + commit (after ``plan(defer_hot=True)`` and attention)."""
+        stream = stream or torch.cuda.current_stream(self.cache.data.device)
+        _lib.check(_lib.lib().cxs_plan_select_commit_hot(
+            w["c_geometry"], w["c_buffers"], kv.data_ptr(), self.cache.tags.data_ptr(),
+            self.cache.data.data_ptr(), stream.cuda_stream))
 
     def retain_hot(self, w, kv, stream=None):
         """Commit the chosen hot tokens after attention (active.py:909-925)."""

@@ -95,7 +95,8 @@ class GRSelectedTransport:
 
     def __init__(self, cache, *, read_order="consumption_depth", cross_query_dedup=True,
                  cuda_graphs=False, capacity=8, workspace_bytes=2 * 1024**3,
-                 hot_policy="frequency", spin_limit=1 << 32, query_group=1):
+                 hot_policy="frequency", spin_limit=1 << 32, query_group=1,
+                 async_hot=False):
         if read_order not in _lib.READ_ORDERS:
             raise ValueError("Invalid NSA read priority configuration")
         if hot_policy not in ("frequency", "static"):
@@ -126,6 +127,9 @@ class GRSelectedTransport:
         # When a list, eager calls append (start, end, workspace) CUDA events
         # bracketing the fetch/attend launch on its stream (bench roofline).
         self.kernel_timing = None
+        self.async_hot = async_hot
+        self._hot_stream = None
+        self._hot_pending = False
 
     # -- reference surface -----------------------------------------------
     def refusal(self, queries, cached, heads, groups, width, bs):
@@ -250,9 +254,9 @@ class GRSelectedTransport:
         b.gates = _lib.ptr(gates)
         w["binding"] = "direct"
 
-    def _execute(self, w, window_start, window):
+    def _execute(self, w, window_start, window, defer_hot=False):
         stream = torch.cuda.current_stream(self.cache.data.device)
-        self.active_plan.plan(w, stream)
+        self.active_plan.plan(w, stream, defer_hot=defer_hot)
         geometry = _lib.AttendGeometry(
             queries=w["queries"], heads=w["heads"], width=w["width"], block_size=w["bs"],
             physical=w["physical"], window=window if w["window_shape"] else 0,
@@ -283,6 +287,11 @@ class GRSelectedTransport:
                 or any(t.device != query.device for t in (blocks, positions))):
             raise ValueError("Invalid GR query/selection geometry")
         fused = window is not None
+        # A dedicated (per-layer) workspace lets the hot top-k choice and the
+        # commit run on a side stream, overlapped with the caller's next work;
+        # the caller joins with ``join()`` before the cache is planned again.
+        async_hot = (self.async_hot and workspace_id is not None and not self.cuda_graphs
+                     and self.hot_policy == "frequency")
         if fused and (window_kv is None or compressed is None or gates is None):
             raise ValueError("Fused branches need window_kv, compressed and gates")
         begin = time.perf_counter_ns()
@@ -361,7 +370,7 @@ class GRSelectedTransport:
             w["graph"].replay()
             self.replays += 1
         else:
-            self._execute(w, window_start, window)
+            self._execute(w, window_start, window, defer_hot=async_hot)
         if workspace_id is None:
             counters = DeferredLayerCounters(w["stats"].clone(), 1, self.pool.backend,
                                              w["error"].clone())
@@ -369,7 +378,14 @@ class GRSelectedTransport:
             counters = DeferredLayerCounters(w["stats"], 1, self.pool.backend, w["error"])
         if not capturing:
             self.pool._pending_read_counts.append((w["region_counts"].clone(), 1))
-        if self.hot_policy == "frequency":
+        if async_hot:
+            if self._hot_stream is None:
+                self._hot_stream = torch.cuda.Stream(device)
+            self._hot_stream.wait_stream(stream)
+            with torch.cuda.stream(self._hot_stream):
+                self.active_plan.select_and_retain_hot(w, w["kv"], self._hot_stream)
+            self._hot_pending = True
+        elif self.hot_policy == "frequency":
             self.active_plan.retain_hot(w, w["kv"], stream)
         if not capturing:
             self.last_done.record(stream)
@@ -393,6 +409,16 @@ class GRSelectedTransport:
             total_submit_wall_ms=(time.perf_counter_ns() - begin) / 1e6,
         )
         return w["output"][:q_count], counters
+
+    def join(self, stream=None):
+        """Make ``stream`` (current by default) wait for side-stream hot commits."""
+        if self._hot_pending:
+            stream = stream or torch.cuda.current_stream(self.cache.data.device)
+            stream.wait_stream(self._hot_stream)
+            self._hot_pending = False
+            if not torch.cuda.is_current_stream_capturing():
+                self.last_done.record(stream)
+                self.cache.last_use.record(stream)
 
     def workspace(self):
         """The most recently used workspace (inspection helper for tests)."""

@@ -165,6 +165,17 @@ int cxs_plan_check(const cxs_plan_geometry* geometry);
 int cxs_plan(const cxs_plan_geometry* geometry, const cxs_plan_buffers* buffers,
              void* stream);
 
+/* cxs_plan without the hot top-k choice, for callers that run the choice
+ * and the commit later (for example on a second stream, overlapped with the
+ * next layer) through cxs_plan_select_commit_hot. */
+int cxs_plan_core(const cxs_plan_geometry* geometry, const cxs_plan_buffers* buffers,
+                  void* stream);
+
+/* Hot top-k choice followed by cxs_plan_commit_hot (pairs with cxs_plan_core). */
+int cxs_plan_select_commit_hot(const cxs_plan_geometry* geometry,
+                               const cxs_plan_buffers* buffers, const void* kv, int32_t* tags,
+                               void* hot_data, void* stream);
+
 /* Commit the chosen hot tokens once attention has completed: write tags and
  * copy their KV from the staging buffer `kv` [P, BS, 128] bf16 into the
  * cache hot data (planning/active.py:410-437, 909-925;
