@@ -42,6 +42,11 @@ def parse():
     p.add_argument("--layers", type=int, default=16)
     p.add_argument("--read-order", default="consumption_depth")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", default="extend", choices=("extend", "dedup"),
+                   help="dedup: BASELINE configs[2] stress (16 candidates x 128 tokens, "
+                        "all history cold), prints its own JSON line")
+    p.add_argument("--sigma", type=float, default=0.5)
+    p.add_argument("--candidates", type=int, default=16)
     p.add_argument("--profile-step", action="store_true",
                    help="after prefill, run one eager extend inside the NVTX range "
                         "'profile_step' and exit (for ncu --nvtx-include profile_step/)")
@@ -295,6 +300,9 @@ def run_ours(args):
     window_tokens = rows * cfg.window
     algorithmic = (attended / args.layers + window_tokens) * 256 + layer_fetch
     peak, peak_kind = peaks()
+    # Fetched-byte reduction of the deduplicating plan vs the query-private
+    # plan on the same selections and cache state (reference traffic metric).
+    shared_miss, private_miss = model.compare_private_plan(static_ids)
 
     result = None
     if rank == 0:
@@ -329,6 +337,9 @@ def run_ours(args):
                       "frac_of_pcie_in_kernel": layer_fetch / (kernel_ms / 1e3) / 1e9 / pcie,
                       "misses_tokens_per_step": int(stats[..., 3].sum()),
                       "hits_tokens_per_step": int(stats[..., 2].sum())},
+            "dedup": {"shared_bytes_per_step": shared_miss * 256,
+                      "private_bytes_per_step": private_miss * 256,
+                      "fetched_byte_reduction": 1 - shared_miss / max(private_miss, 1)},
             "clocks": clocks,
             "prefill_s": prefill_s,
         }
@@ -343,8 +354,55 @@ def run_ours(args):
     return result
 
 
+def run_dedup(args):
+    """16 candidate queries of E=128 sharing one H=16K history,
+    all history cold; candidate hidden states = shared base + N(0, sigma).
+    The candidates are packed into one suffix (worker/prompt.py:24-55)."""
+    import torch
+
+    from cxlsparse_b200.model import NSAConfig, NSAExtendModel
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = NSAConfig(layers=args.layers)
+    E = args.candidates * 128
+    model = NSAExtendModel(cfg, device=device, seed=0, max_history=args.history + E,
+                           hot_policy="static")
+    g = torch.Generator().manual_seed(2000)
+    history = torch.randint(0, cfg.vocab, (args.history,), generator=g).to(device)
+    model.prefill(history)
+    model.cache.tags.fill_(-1)  # hot replica of 0 blocks: all history cold
+    base = torch.randn(128, cfg.hidden, generator=g)
+    hidden = torch.cat([base + args.sigma * torch.randn(128, cfg.hidden, generator=g)
+                        for _ in range(args.candidates)]).to(device, torch.bfloat16)
+    ids = torch.zeros(E, dtype=torch.int64, device=device)
+    model.prepare_fast(E)
+    for _ in range(args.warmup):
+        model.extend_fast(ids, hidden)
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        model.counters.clear()
+        model.extend_fast(ids, hidden)
+    end.record()
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / args.steps
+    shared, private = model.compare_private_plan(ids, hidden)
+    print(json.dumps({
+        "workload": "BASELINE configs[2] dedup stress", "sigma": args.sigma,
+        "candidates": args.candidates, "extend_rows": E, "history": args.history,
+        "ms_per_step": ms, "tok_s": E / (ms / 1e3),
+        "shared_bytes_per_step": shared * 256, "private_bytes_per_step": private * 256,
+        "fetched_byte_reduction": 1 - shared / max(private, 1)}))
+    model.close()
+
+
 def main():
     args = parse()
+    if args.workload == "dedup":
+        run_dedup(args)
+        return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":

@@ -440,6 +440,46 @@ __global__ void __launch_bounds__(1024) publish_kernel(Geo g, cxs_plan_buffers b
   }
 }
 
+// Physical-order publish for plans beyond one CTA (active.py:298-305): chunk
+// counts of missing blocks, a scan over chunks, then an ordered compaction.
+constexpr int kChunk = 1024;
+
+__global__ void __launch_bounds__(kChunk) chunk_count_kernel(Geo g, cxs_plan_buffers b,
+                                                             int32_t* chunk_counts) {
+  typedef cub::BlockReduce<int, kChunk> Reduce;
+  __shared__ typename Reduce::TempStorage reduce;
+  int i = blockIdx.x * kChunk + threadIdx.x;
+  int miss = i < g.P && b.flags[i] != 0;
+  int total = Reduce(reduce).Sum(miss);
+  if (threadIdx.x == 0) chunk_counts[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(kChunk) chunk_compact_kernel(Geo g, cxs_plan_buffers b,
+                                                               const int32_t* chunk_counts,
+                                                               int chunks) {
+  typedef cub::BlockScan<int, kChunk> Scan;
+  __shared__ typename Scan::TempStorage scan;
+  __shared__ int base;
+  if (threadIdx.x == 0) {
+    int sum = 0, all = 0;
+    for (int c = 0; c < chunks; ++c) {
+      if (c < (int)blockIdx.x) sum += chunk_counts[c];
+      all += chunk_counts[c];
+    }
+    base = sum;
+    if (blockIdx.x == 0) b.missing[0] = all;
+  }
+  __syncthreads();
+  int i = blockIdx.x * kChunk + threadIdx.x;
+  int miss = i < g.P && b.flags[i] != 0;
+  int prefix;
+  Scan(scan).ExclusiveSum(miss, prefix);
+  if (miss) {
+    b.ioids[base + prefix] = i;
+    b.ranks[i] = base + prefix;
+  }
+}
+
 // --------------------------------------------------------------- hot top-k ---
 // Top-`hot` indices of a head's frequency table by (frequency desc, index asc)
 // (active.py:449-500; stable argsort fallback active.py:884-888): find the
@@ -718,8 +758,14 @@ int check_geometry(const cxs_plan_geometry* geo, Geo* out) {
   while (g.HASH < 2 * g.HOT) g.HASH *= 2;
   if (g.MAP + 1 > kMaxMapBlocks)
     return set_error(CXS_ERR_CAPACITY, "map_blocks %d exceeds %d", g.MAP, kMaxMapBlocks - 1);
-  if (g.P > kMaxPhysical)
-    return set_error(CXS_ERR_CAPACITY, "physical blocks %d exceed %d", g.P, kMaxPhysical);
+  if (g.P > kMaxPhysical && g.ORDER != CXS_ORDER_PHYSICAL)
+    return set_error(CXS_ERR_CAPACITY,
+                     "consumption-depth order supports at most %d physical blocks (got %d)",
+                     kMaxPhysical, g.P);
+  if (g.P > kMaxPhysical && (g.P + kChunk - 1) / kChunk > g.R)
+    return set_error(CXS_ERR_CAPACITY, "physical blocks %d need more rows of scratch", g.P);
+  if (g.P > (1 << 24))
+    return set_error(CXS_ERR_CAPACITY, "physical blocks %d exceed %d", g.P, 1 << 24);
   if (g.HOT > kMaxHot) return set_error(CXS_ERR_CAPACITY, "hot %d exceeds %d", g.HOT, kMaxHot);
   if (g.PRIVATE && g.W > 32)
     return set_error(CXS_ERR_CAPACITY, "query-private plan supports width <= 32");
@@ -833,7 +879,16 @@ static int plan_impl(const cxs_plan_geometry* geometry, const cxs_plan_buffers* 
   }
   int end_bit = 1;
   while (end_bit < 64 && ((bound + (unsigned long long)g.P) >> end_bit)) ++end_bit;
-  switch (sort_items(g.P)) {
+  if (g.P > kMaxPhysical) {
+    // Only physical order reaches here (check_geometry): chunked compaction.
+    int chunks = (g.P + kChunk - 1) / kChunk;
+    int32_t* chunk_counts = b.row_depth;  // unused by the physical order; >= chunks entries
+    chunk_count_kernel<<<chunks, kChunk, 0, stream>>>(g, b, chunk_counts);
+    CXS_LAUNCH_CHECK("chunk_count_kernel");
+    chunk_compact_kernel<<<chunks, kChunk, 0, stream>>>(g, b, chunk_counts, chunks);
+    CXS_LAUNCH_CHECK("chunk_compact_kernel");
+    status = CXS_OK;
+  } else switch (sort_items(g.P)) {
     case 1: status = launch_publish<1>(g, b, bound, end_bit, stream); break;
     case 2: status = launch_publish<2>(g, b, bound, end_bit, stream); break;
     case 4: status = launch_publish<4>(g, b, bound, end_bit, stream); break;

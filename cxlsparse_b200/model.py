@@ -114,6 +114,7 @@ class NSAExtendModel:
             self.cache, read_order=read_order, cross_query_dedup=cross_query_dedup,
             hot_policy=hot_policy, capacity=cfg.layers + 4, async_hot=True)
         self.fast = None
+        self.probe, self.probe_counters = None, []
         self.users = {}
         self.counters = []
 
@@ -272,6 +273,9 @@ class NSAExtendModel:
         total = L["window_start"] + L["kept"] + E
         cmp_out, blocks = ops.compressed_attention_select(
             query, L["summaries"], positions, total, cfg.block_size, cfg.block_counts)
+        if self.probe is not None:  # comparison plan on the same selections / cache state
+            self.probe_counters.append(self.probe.plan_only(
+                query, blocks, positions, L["fetches"], cfg.block_size, workspace_id=index))
         mixed, counters = self.transport.run(
             query, blocks, positions, L["fetches"], cfg.block_size, window=cfg.window,
             window_kv=L["window_buf"], window_start=L["window_start"], compressed=cmp_out,
@@ -284,11 +288,15 @@ class NSAExtendModel:
         _lib.check(lib.cxs_silu_mul(gate_up.data_ptr(), E, cfg.ffn, f["mlp"].data_ptr(), stream))
         return torch.addmm(hidden, f["mlp"], w["down"].t())
 
-    def extend_fast(self, token_ids):
-        """Extend step through the fused glue (after ``prepare_fast``)."""
+    def extend_fast(self, token_ids, hidden=None):
+        """Extend step through the fused glue (after ``prepare_fast``).
+
+        ``hidden`` optionally replaces the token embeddings (synthetic
+        candidate hidden states)."""
         if self.fast is None or len(token_ids) != self.fast["E"]:
             raise ValueError("prepare_fast(len(token_ids)) first")
-        hidden = F.embedding(token_ids, self.embed)
+        if hidden is None:
+            hidden = F.embedding(token_ids, self.embed)
         for index in range(self.cfg.layers):
             hidden = self._layer_fast(index, hidden)
         self.transport.join()
@@ -321,6 +329,24 @@ class NSAExtendModel:
         graph_counters = list(self.counters)
         self.counters.clear()
         return graph, static_ids, static_out, graph_counters
+
+    def compare_private_plan(self, token_ids, hidden=None):
+        """One eager extend step that also plans each layer query-privately
+        (reference QueryPrivatePlanAdapter semantics) on the same selections
+        and cache state; returns (dedup misses, private misses) in tokens."""
+        self.probe = GRSelectedTransport(self.cache, cross_query_dedup=False,
+                                         read_order="physical", hot_policy="static",
+                                         capacity=self.cfg.layers + 2)
+        self.probe_counters, self.counters = [], []
+        try:
+            self.extend_fast(token_ids, hidden)
+            torch.cuda.synchronize(self.device)
+            shared = sum(int(c.statistics[:, 3].sum()) for c in self.counters)
+            private = sum(int(c.statistics[:, 3].sum()) for c in self.probe_counters)
+        finally:
+            self.probe.close()
+            self.probe, self.probe_counters = None, []
+        return shared, private
 
     def close(self):
         self.transport.close()

@@ -193,12 +193,14 @@ class GRSelectedTransport:
         def empty(shape, dtype=torch.int32):
             return torch.empty(shape, dtype=dtype, device=device)
 
+        plan_only = isinstance(workspace_id, tuple) and workspace_id[:1] == ("plan_only",)
+        staging_blocks = 1 if plan_only else p  # planner-only workspaces move no payload
         w.update(
             query=torch.zeros((qb, heads, 16, 64), dtype=torch.bfloat16, device=device),
             blocks=torch.full((qb, heads, width), -1, dtype=torch.int32, device=device),
             in_positions=torch.full((qb,), -1, dtype=torch.int32, device=device),
             desc=empty((heads, 5), torch.int64),
-            kv=torch.zeros((p, bs, 128), dtype=torch.bfloat16, device=device),
+            kv=torch.zeros((staging_blocks, bs, 128), dtype=torch.bfloat16, device=device),
             sources=empty((p,), torch.int64), kinds=empty((p,)), ready=empty((p,)),
             control=torch.zeros((4,), dtype=torch.int32, device=device),
             error=torch.zeros((1,), dtype=torch.int32, device=device),
@@ -409,6 +411,25 @@ class GRSelectedTransport:
             total_submit_wall_ms=(time.perf_counter_ns() - begin) / 1e6,
         )
         return w["output"][:q_count], counters
+
+    def plan_only(self, query, blocks, positions, fetches, block_size, *, workspace_id=None):
+        """Run only the fetch planner on these selections (no IO, attention or
+        commit) and return its DeferredLayerCounters: used to compare the
+        fetched bytes of the deduplicating and query-private plans."""
+        q_count, heads, width = blocks.shape
+        qb = query_bucket(q_count)
+        w = self._workspace(qb, heads, width, fetches, block_size, None, ("plan_only",))
+        layout = tuple((f["row"], f["cached_length"], f["history_length"],
+                        f["current_kv"].data_ptr(), len(f["current_kv"])) for f in fetches)
+        self._bind_static(w)
+        w["blocks"][:q_count].copy_(blocks)
+        w["in_positions"][:q_count].copy_(positions)
+        if q_count < qb:
+            w["blocks"][q_count:].fill_(-1)
+            w["in_positions"][q_count:].fill_(-1)
+        w["desc"].copy_(torch.tensor(layout, dtype=torch.int64, device=query.device))
+        self.active_plan.plan(w, torch.cuda.current_stream(query.device), defer_hot=True)
+        return DeferredLayerCounters(w["stats"].clone(), 1, self.pool.backend)
 
     def join(self, stream=None):
         """Make ``stream`` (current by default) wait for side-stream hot commits."""

@@ -110,3 +110,39 @@ def test_device_plan_replays_in_a_cuda_graph(cuda):
         torch.cuda.synchronize()
         for key, value in expected.items():
             assert torch.equal(w[key], value), key
+
+
+def test_large_private_plan_physical_publish(cuda):
+    """Plans beyond one publish CTA (P > 16384) use the chunked compaction."""
+    from cxlsparse_b200.mempool import HiSparseCache, MemoryPool
+
+    pool = MemoryPool(16 * 2 + 8, 128, page_size=64)
+    try:
+        cache = HiSparseCache(pool, rows=2, max_history=1024 + 1100, hot=64, topk=64)
+        for h in range(2):
+            cache.bind(h, pool.token_slots(pool.allocate(16), 0, 1024))
+        adapter = planning.QueryPrivatePlanAdapter(cache, read_order="physical")
+        g = torch.Generator().manual_seed(5)
+        q = 1100
+        positions = torch.arange(1024, 1024 + q, dtype=torch.int32)
+        blocks = torch.randint(0, 16, (q, 2, 16), generator=g, dtype=torch.int32)
+        fetches = [dict(row=h, cached_length=1024, history_length=1024,
+                        current_kv=torch.empty(q, 128, device=cuda)) for h in range(2)]
+        w = adapter.allocate(q, 2, 16, fetches, 64, device=cuda)
+        assert w["physical"] > 16384
+        desc = torch.tensor([(h, 1024, 1024, 1 << 40, q) for h in range(2)], device=cuda)
+        blocks_d, positions_d = blocks.to(cuda), positions.to(cuda)
+        adapter.bind(w, blocks_d, positions_d, desc, pool.region_bases)
+        w["_inputs"] = (blocks_d, positions_d, desc)
+        adapter.plan(w)
+        torch.cuda.synchronize()
+        flags = w["flags"].cpu().numpy()
+        ioids, ranks, missing = P.physical_order(flags)
+        assert int(w["missing"].item()) == missing > 16384
+        assert np.array_equal(w["ioids"].cpu().numpy()[:missing], ioids[:missing])
+        assert np.array_equal(w["ranks"].cpu().numpy()[flags.astype(bool)],
+                              ranks[flags.astype(bool)])
+        assert int(w["stats"][:, 3].sum()) == sum(int(v) for v in w["valid"].cpu().numpy()
+                                                  [flags.astype(bool)])
+    finally:
+        pool.close()
