@@ -4,30 +4,32 @@
 // and the staged TMA kernel tma/pipeline.py:96-742 (IO CTAs :347-421,
 // consumer CTAs :436-655, online-softmax block step :172-257). This is a new
 // sm_100a design: one cooperative launch whose CTAs each run one IO warp and
-// eight attention warps; see cxs_fetch_attend in include/cxlsparse.h.
+// four tcgen05 attention warps; see cxs_fetch_attend in include/cxlsparse.h.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <climits>
 #include <mutex>
 
 #include "cxs_common.cuh"
 #include "tile_attn.cuh"
+#include "tile_tc.cuh"
 
 using cxs::kTokenBytes;
-using cxs::Softmax;
 using cxs::bf16_round;
 using cxs::unpack_bf16;
 using cxs_host::set_error;
 
 namespace {
 
-constexpr int kAttnWarps = 8;
+constexpr int kAttnWarps = cxs::tc::kEngines;     // one per TMEM subpartition
+constexpr int kTmemAlloc = kAttnWarps * cxs::tc::kTmemCols;  // 512: all of TMEM
 constexpr int kThreads = 32 * (1 + kAttnWarps);
 
 struct AttendArgs {
   int Q, H, W, BS, P, window, window_len, gate;
   long long window_start, spin_limit;
-  int consumers;  // attention warps that own rows: min(rows, grid * kAttnWarps)
+  int consumers;  // attention warps of the launch: grid * kAttnWarps
   const __nv_bfloat16* query;
   __nv_bfloat16* kv;
   const int32_t* all_ids;
@@ -113,27 +115,304 @@ __global__ void prepare_kernel(int P, int BS, const int64_t* __restrict__ addres
   }
 }
 
+// ------------------------------------------------------- attention warps ---
+// One attention warp (engine `w` of its CTA): query rows with index
+// w * gridDim.x + blockIdx.x + k * consumers. Per row it runs the
+// sliding-window tiles, then the row's selected occurrences in list order
+// (duplicates attended again, as the reference does), on the tcgen05 engine
+// of tile_tc.cuh, and writes the (gate-mixed) output.
+//
+// Per tile t in stage st (K/V double-buffered; one mbarrier commit C_t per
+// tile covers P.V of tile t-1 and S of tile t):
+//   A  every lane waits C_t; lane 0 starts the copy of tile t+1 into the other
+//      stage (acquire-waiting on ready[b] for a selected block)
+//   B  softmax of S(t) -> P, running max/denominator, O rescale in TMEM
+//   C  the warp agrees on the status of every wait; a failure ends the launch
+//      for this warp after its copies have landed
+//   D  lane 0 issues O += P.V(t), waits for tile t+1, issues S(t+1), commits
+template <int BS>
+__device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
+                                               const CUtensorMap& win_map, const AttendArgs& a,
+                                               uint8_t* q_tile, uint8_t* p_tile, uint8_t* wbase,
+                                               int w, uint32_t tmem) {
+  namespace tc = cxs::tc;
+  const tc::WarpSmem ws{wbase};
+  const int lane = threadIdx.x % 32, half = lane >> 4;
+  const bool leader = lane == 0;
+  const int m = 32 * w + lane;  // this lane's row of the Q / P tiles and of S / O
+  const uint32_t lane_off = (uint32_t)(32 * w) << 16;
+  const uint32_t s_col = tmem, o_col = tmem + 64;  // MMA destinations
+  const uint32_t s_addr = s_col + lane_off, o_addr = o_col + lane_off;
+  const uint32_t id_s = tc::idesc_bf16(128, 64, 0, 0), id_o = tc::idesc_bf16(128, 64, 0, 1);
+  const uint32_t q_addr = cxs::smem_addr(q_tile), p_addr = cxs::smem_addr(p_tile);
+  uint32_t tma_phases = 0, mma_phase = 0;  // bit s of tma_phases: phase of stage s
+  int stage = 0;
+  const int rows = a.Q * a.H;
+  if (leader) {
+    cxs::tma_prefetch_desc(&kv_map);
+    if (a.window) cxs::tma_prefetch_desc(&win_map);
+  }
+  auto mma_scores = [&](int stg) {  // S = Q . K(stg)^T
+    const uint32_t ka = cxs::smem_addr(ws.k(stg));
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      tc::mma(s_col, tc::desc_sw128(q_addr + 32 * k, 16, 1024),
+              tc::desc_sw128(ka + 32 * k, 16, 1024), id_s, k);
+  };
+  auto mma_output = [&](int stg, bool accumulate) {  // O (+)= P . V(stg)
+    const uint32_t va = cxs::smem_addr(ws.v(stg));
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      tc::mma(o_col, tc::desc_sw128(p_addr + 32 * k, 16, 1024),
+              tc::desc_sw128(va + 2048 * k, 16, 1024), id_o, accumulate || k > 0);
+  };
+  for (int row = w * gridDim.x + blockIdx.x; row < rows; row += a.consumers) {
+    const int h = row % a.H;
+    const int pos = a.row_positions[row];
+    // Window: logical positions [w_lo, w_hi] (positions and window bounds fit
+    // int32: host-checked), in tiles of 64 from w_lo.
+    int w_lo = 1, w_hi = 0;
+    if (a.window > 0 && pos >= 0) {
+      const int w_first = (int)a.window_start, w_last = w_first + a.window_len - 1;
+      w_lo = max(max(pos - a.window + 1, 0), w_first);
+      w_hi = min(pos, w_last);
+    }
+    const int n_win = w_lo <= w_hi ? (w_hi - w_lo) / tc::kTileRows + 1 : 0;
+    const int count = pos >= 0 ? min(a.all_counts[row], a.W) : 0;
+    const int total = n_win + count;
+    // Lane i holds selected occurrence i (block id and first position).
+    int my_block = -1, my_start = 0;
+    if (lane < count) {
+      my_block = a.all_ids[(long long)row * a.W + lane];
+      if (my_block >= 0 && my_block < a.P) my_start = a.starts[my_block];
+    }
+    tc::write_query_row(q_tile, a.query, row, m, lane);
+    cxs::fence_proxy_async_shared();
+    __syncwarp();
+    // Lane 0: start the copy of tile t into stage stg (false: bad block or
+    // ready wait failed).
+    auto issue = [&](int t, int block, int stg) -> bool {
+      if (t < n_win) {
+        cxs::mbar_expect_tx(ws.tma_bar(stg), 2 * tc::kTileBytes);
+        tc::window_load(ws.k(stg), ws.v(stg), &win_map, h,
+                        w_lo + t * tc::kTileRows - (int)a.window_start, ws.tma_bar(stg));
+        return true;
+      }
+      if (block < 0 || block >= a.P) {
+        atomicOr(a.error, cxs::kErrBadBlock);
+        return false;
+      }
+      if (!cxs::wait_ready_bounded(&a.ready[block], a.spin_limit, a.error)) return false;
+      cxs::fence_proxy_async_global();
+      cxs::mbar_expect_tx(ws.tma_bar(stg), 2 * BS * 128);
+      cxs::tma_load_2d(ws.k(stg), &kv_map, 0, block * BS, ws.tma_bar(stg));
+      cxs::tma_load_2d(ws.v(stg), &kv_map, 64, block * BS, ws.tma_bar(stg));
+      return true;
+    };
+    bool alive = true;
+    float m_run = -INFINITY, l_run = 0.f;
+    uint32_t win_packed[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) win_packed[i] = 0;
+    if (total > 0) {
+      bool step_ok = true;  // lane 0: every wait of the coming step succeeded
+      const int block0 = __shfl_sync(0xffffffffu, my_block, 0);
+      if (leader) {
+        step_ok = issue(0, n_win > 0 ? -1 : block0, stage);
+        if (step_ok) {
+          step_ok = tc::bounded_wait(ws.tma_bar(stage), (tma_phases >> stage) & 1u, a.spin_limit,
+                                     a.error, cxs::kErrCopyTimeout);
+          tma_phases ^= 1u << stage;
+        }
+        if (step_ok) {
+          tc::fence_after();
+          mma_scores(stage);
+        }
+        tc::commit(ws.mma_bar());
+      }
+      for (int t = 0; t < total; ++t) {
+        const int st = stage;
+        const bool first_of_branch = t == 0 || t == n_win;
+        // A
+        const bool waited = tc::bounded_wait(ws.mma_bar(), mma_phase, a.spin_limit, a.error,
+                                             cxs::kErrCopyTimeout);
+        mma_phase ^= 1;
+        tc::fence_after();
+        if (t == n_win && n_win > 0) {
+          // Window branch complete: keep its normalised bf16 output, restart.
+          float o[32];
+          tc::combine_o(o_addr, half, o);
+          const float den = l_run > 0.f ? l_run : 1.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) win_packed[i] = cxs::pack_bf16(o[2 * i] / den, o[2 * i + 1] / den);
+          m_run = -INFINITY;
+          l_run = 0.f;
+        }
+        const int cur_block = __shfl_sync(0xffffffffu, my_block, (t - n_win) & 31);
+        const int cur_start = __shfl_sync(0xffffffffu, my_start, (t - n_win) & 31);
+        const int next_block = __shfl_sync(0xffffffffu, my_block, (t + 1 - n_win) & 31);
+        bool next_issued = false;
+        if (leader && t + 1 < total) {
+          next_issued = issue(t + 1, next_block, st ^ 1);
+          step_ok = step_ok && next_issued;
+        }
+        // B
+        int lo = 0, hi = -1;
+        if (t < n_win) {
+          const int t0 = w_lo + t * tc::kTileRows;
+          lo = 0;
+          hi = min(w_hi - t0, tc::kTileRows - 1);
+        } else if (cur_block >= 0 && cur_block < a.P) {
+          hi = min(pos - cur_start, BS - 1);
+        }
+        const float m_old = m_run;
+        const float factor = tc::softmax_half(p_tile, s_addr, lo, hi, m_run, l_run, m, half);
+        if (!first_of_branch) tc::rescale_o(o_addr, factor, m_old != -INFINITY && factor != 1.f);
+        cxs::fence_proxy_async_shared();
+        tc::fence_before();
+        // C
+        const bool ok = __all_sync(0xffffffffu, waited) && __shfl_sync(0xffffffffu, step_ok, 0);
+        if (!ok) {
+          if (leader && next_issued)  // let the copy land before shared memory is released
+            tc::bounded_wait(ws.tma_bar(st ^ 1), (tma_phases >> (st ^ 1)) & 1u, a.spin_limit,
+                             a.error, cxs::kErrCopyTimeout);
+          alive = false;
+          break;
+        }
+        // D
+        if (leader) {
+          tc::fence_after();
+          mma_output(st, !first_of_branch);
+          if (t + 1 < total) {
+            step_ok = tc::bounded_wait(ws.tma_bar(st ^ 1), (tma_phases >> (st ^ 1)) & 1u,
+                                       a.spin_limit, a.error, cxs::kErrCopyTimeout);
+            tma_phases ^= 1u << (st ^ 1);
+            if (step_ok) mma_scores(st ^ 1);
+          }
+          tc::commit(ws.mma_bar());
+        }
+        __syncwarp();
+        stage ^= 1;
+      }
+      if (!alive) break;
+      // E: the last P.V is complete.
+      tc::bounded_wait(ws.mma_bar(), mma_phase, a.spin_limit, a.error, cxs::kErrCopyTimeout);
+      mma_phase ^= 1;
+      tc::fence_after();
+      if (n_win > 0 && total == n_win) {
+        float o[32];
+        tc::combine_o(o_addr, half, o);
+        const float den = l_run > 0.f ? l_run : 1.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) win_packed[i] = cxs::pack_bf16(o[2 * i] / den, o[2 * i + 1] / den);
+        l_run = 0.f;
+      }
+    }
+    // Epilogue: lane writes dims 32 * half .. 32 * half + 31 of head (lane & 15).
+    float o[32];
+    if (total > n_win) {
+      tc::combine_o(o_addr, half, o);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = 0.f;
+    }
+    const long long off = ((long long)row * 16 + (lane & 15)) * 64 + 32 * half;
+    const float den = l_run > 0.f ? l_run : 1.f;
+    uint4* dst = reinterpret_cast<uint4*>(a.out + off);
+    if (!a.gate) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          r[e] = cxs::pack_bf16(bf16_round(o[8 * c + 2 * e] / den),
+                                bf16_round(o[8 * c + 2 * e + 1] / den));
+        dst[c] = make_uint4(r[0], r[1], r[2], r[3]);
+      }
+    } else {
+      // Gate mix in the reference's bf16 rounding sequence (model.py:470-473).
+      const __nv_bfloat16* gp = a.gates + ((long long)row * 16 + (lane & 15)) * 3;
+      const float g0 = __bfloat162float(gp[0]), g1 = __bfloat162float(gp[1]),
+                  g2 = __bfloat162float(gp[2]);
+      const uint4* cmp = reinterpret_cast<const uint4*>(a.compressed + off);
+      const bool have_window = a.window > 0 && pos >= 0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 cv = cmp[c];
+        const uint32_t* cp = reinterpret_cast<const uint32_t*>(&cv);
+        uint32_t r[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 c2 = unpack_bf16(cp[e]);
+          const float2 w2 = have_window ? unpack_bf16(win_packed[4 * c + e]) : make_float2(0.f, 0.f);
+          float x0 = bf16_round(bf16_round(o[8 * c + 2 * e] / den) * g1);
+          float x1 = bf16_round(bf16_round(o[8 * c + 2 * e + 1] / den) * g1);
+          x0 = bf16_round(x0 + c2.x * g0);
+          x1 = bf16_round(x1 + c2.y * g0);
+          r[e] = cxs::pack_bf16(x0 + w2.x * g2, x1 + w2.y * g2);
+        }
+        dst[c] = make_uint4(r[0], r[1], r[2], r[3]);
+      }
+    }
+    __syncwarp();  // TMEM reads done before the next row's MMAs
+  }
+}
+
 // ------------------------------------------------------ IO + attention ---
+// Warps 0-3: attention warps (tcgen05 engine, tile_tc.cuh), one query row at
+// a time each. Warp 4: the IO warp.
 template <int BS>
 __global__ void __launch_bounds__(kThreads, 1)
     fetch_attend_kernel(const __grid_constant__ CUtensorMap kv_map,
                         const __grid_constant__ CUtensorMap win_map, AttendArgs a) {
-  constexpr int kTile = BS * 128;    // one K or V tile (BS rows x 128 bytes)
+  namespace tc = cxs::tc;
   constexpr int kBlockBytes = BS * kTokenBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* io_buf = smem;                                   // kBlockBytes
-  uint8_t* tiles = smem + ((kBlockBytes + 1023) & ~1023);   // kAttnWarps x (K, V)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + kAttnWarps * 2 * kTile);
-  int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  uint8_t* io_buf = smem;
+  uint8_t* q_tile = smem + ((kBlockBytes + 1023) & ~1023);
+  uint8_t* p_tile = q_tile + tc::kRowTileBytes;
+  uint8_t* warps_base = p_tile + tc::kRowTileBytes;
+  uint8_t* ctrl = warps_base + kAttnWarps * tc::WarpSmem::kBytes;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl);
+  uint64_t* io_bar = reinterpret_cast<uint64_t*>(ctrl + 64);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    for (int i = 0; i <= kAttnWarps; ++i) cxs::mbar_init(&bars[i], 1);
+    cxs::mbar_init(io_bar, 1);
+    for (int w = 0; w < kAttnWarps; ++w) {
+      tc::WarpSmem ws{warps_base + w * tc::WarpSmem::kBytes};
+      cxs::mbar_init(ws.tma_bar(0), 1);
+      cxs::mbar_init(ws.tma_bar(1), 1);
+      cxs::mbar_init(ws.mma_bar(), 1);
+    }
     cxs::fence_mbar_init();
   }
-  __syncthreads();
-
   if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     cxs::smem_addr(tmem_slot)),
+                 "r"(kTmemAlloc));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  // Zero the P tile (each lane only ever writes its own half of its row) and
+  // the K/V stages (rows beyond a short block, BS < 64, start at zero and
+  // afterwards only hold finite key/value data).
+  if (warp < kAttnWarps) {
+    for (int i = threadIdx.x; i < tc::kRowTileBytes / 16; i += 32 * kAttnWarps)
+      reinterpret_cast<uint4*>(p_tile)[i] = make_uint4(0, 0, 0, 0);
+    for (int w = 0; w < kAttnWarps; ++w)
+      for (int i = threadIdx.x; i < 4 * tc::kTileBytes / 16; i += 32 * kAttnWarps)
+        reinterpret_cast<uint4*>(warps_base + w * tc::WarpSmem::kBytes)[i] =
+            make_uint4(0, 0, 0, 0);
+  }
+  cxs::fence_proxy_async_shared();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == kAttnWarps) {
     // ------------------------------------------------------------ IO warp
+    uint64_t* bar = io_bar;
     uint32_t phase = 0;
     int missing = a.missing[0];
     while (true) {
@@ -152,12 +431,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           const void* src = reinterpret_cast<const void*>(a.sources[block]);
           cxs::fence_proxy_async_shared();
-          cxs::mbar_expect_tx(&bars[kAttnWarps], kBlockBytes);
-          cxs::bulk_g2s(io_buf, src, kBlockBytes, &bars[kAttnWarps]);
-          if (cxs::mbar_wait_bounded(&bars[kAttnWarps], phase, a.spin_limit, a.error)) {
+          cxs::mbar_expect_tx(bar, kBlockBytes);
+          cxs::bulk_g2s(io_buf, src, kBlockBytes, bar);
+          if (cxs::mbar_wait_bounded(bar, phase, a.spin_limit, a.error)) {
             cxs::bulk_s2g_and_wait(dst, io_buf, kBlockBytes);
           } else {
-            cxs::mbar_wait_bounded(&bars[kAttnWarps], phase, a.spin_limit, a.error);
+            cxs::mbar_wait_bounded(bar, phase, a.spin_limit, a.error);
           }
           cxs::fence_proxy_async_global();
         }
@@ -172,130 +451,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (lane == 0) cxs::st_release(&a.ready[block], 1);
     }
-    return;
+  } else {
+    attention_warp<BS>(kv_map, win_map, a, q_tile, p_tile, warps_base + warp * tc::WarpSmem::kBytes,
+                       warp, tmem_base + warp * tc::kTmemCols);
   }
-
-  // ------------------------------------------------------- attention warps
-  int aw = blockIdx.x * kAttnWarps + (warp - 1);
-  if (aw >= a.consumers) return;
-  uint8_t* k_tile = tiles + (warp - 1) * 2 * kTile;
-  uint8_t* v_tile = k_tile + kTile;
-  uint32_t k_addr = cxs::smem_addr(k_tile), v_addr = cxs::smem_addr(v_tile);
-  uint64_t* bar = &bars[warp - 1];
-  uint32_t phase = 0;
-  int rows = a.Q * a.H;
-  int g = lane >> 2, c = lane & 3;
-  if (lane == 0) {
-    cxs::tma_prefetch_desc(&kv_map);
-    if (a.window) cxs::tma_prefetch_desc(&win_map);
-  }
-  for (int row = aw; row < rows; row += a.consumers) {
-    int h = row % a.H;
-    int pos = a.row_positions[row];
-    uint32_t qa[4][4];
-    cxs::load_query(a.query + (long long)row * cxs::kGroups * cxs::kDim, lane, qa);
-    Softmax<BS> sm;
-    uint32_t win_out[8][2];
-    bool have_window = a.window > 0 && pos >= 0;
-    if (have_window) {
-      sm.reset();
-      long long lo = (long long)pos - a.window + 1;
-      int tiles_n = (a.window + BS - 1) / BS;
-      for (int j = 0; j < tiles_n; ++j) {
-        long long t0 = lo + (long long)j * BS;
-        if (t0 + BS - 1 < 0) continue;  // whole tile before position 0
-        long long local0 = t0 - a.window_start;
-        if (lane == 0) {
-          cxs::fence_proxy_async_shared();
-          cxs::mbar_expect_tx(bar, 2 * kTile);
-          // 3-D map {channel, head, record}: x channel, y head, z record.
-          cxs::tma_load_3d(k_addr, &win_map, 0, h, (int)local0, bar);
-          cxs::tma_load_3d(v_addr, &win_map, 64, h, (int)local0, bar);
-        }
-        __syncwarp();
-        if (!cxs::mbar_wait_bounded(bar, phase, a.spin_limit, a.error)) {
-          cxs::mbar_wait_bounded(bar, phase, a.spin_limit, a.error);  // drain the copy
-          return;
-        }
-        phase ^= 1;
-        long long win_lo = lo, win_len = a.window_len, wstart = a.window_start;
-        sm.step(qa, k_addr, v_addr, lane, [&](int t) {
-          long long logical = t0 + t;
-          long long local = logical - wstart;
-          return logical >= 0 && logical >= win_lo && logical <= pos && local >= 0 &&
-                 local < win_len;
-        });
-        __syncwarp();
-      }
-      sm.finish(win_out);
-    }
-    // Selected blocks in original order, each gated on ready[b].
-    sm.reset();
-    int count = pos >= 0 ? a.all_counts[row] : 0;
-    const int32_t* ids = a.all_ids + (long long)row * a.W;
-    for (int i = 0; i < count; ++i) {
-      int block = ids[i];
-      if (block < 0 || block >= a.P) {
-        if (lane == 0) atomicOr(a.error, cxs::kErrBadBlock);
-        continue;
-      }
-      bool ok = true;
-      if (lane == 0) {
-        ok = cxs::wait_ready_bounded(&a.ready[block], a.spin_limit, a.error);
-        if (ok) {
-          cxs::fence_proxy_async_global();
-          cxs::fence_proxy_async_shared();
-          cxs::mbar_expect_tx(bar, 2 * kTile);
-          cxs::tma_load_2d(k_tile, &kv_map, 0, block * BS, bar);
-          cxs::tma_load_2d(v_tile, &kv_map, 64, block * BS, bar);
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) return;  // ready timeout (or an earlier failure): the launch is invalid
-      if (!cxs::mbar_wait_bounded(bar, phase, a.spin_limit, a.error)) {
-        cxs::mbar_wait_bounded(bar, phase, a.spin_limit, a.error);  // drain the copy
-        return;
-      }
-      phase ^= 1;
-      int start = a.starts[block];
-      sm.step(qa, k_addr, v_addr, lane, [&](int t) { return start + t <= pos; });
-      __syncwarp();
-    }
-    uint32_t sel_out[8][2];
-    sm.finish(sel_out);
-    // Epilogue: selected output, or the gate mix of the three branches in the
-    // reference's bf16 rounding sequence (models/nsa/model.py:470-473).
-    __nv_bfloat16* orow = a.out + (long long)row * cxs::kGroups * cxs::kDim;
-    if (!a.gate) {
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        *reinterpret_cast<uint32_t*>(orow + g * 64 + n * 8 + 2 * c) = sel_out[n][0];
-        *reinterpret_cast<uint32_t*>(orow + (g + 8) * 64 + n * 8 + 2 * c) = sel_out[n][1];
-      }
-    } else {
-      const __nv_bfloat16* crow = a.compressed + (long long)row * cxs::kGroups * cxs::kDim;
-      const __nv_bfloat16* grow = a.gates + (long long)row * cxs::kGroups * 3;
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        int head = g + r * 8;
-        float g0 = __bfloat162float(grow[head * 3 + 0]);
-        float g1 = __bfloat162float(grow[head * 3 + 1]);
-        float g2 = __bfloat162float(grow[head * 3 + 2]);
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          int dim = n * 8 + 2 * c;
-          float2 sel = unpack_bf16(sel_out[n][r]);
-          float2 win = have_window ? unpack_bf16(win_out[n][r]) : make_float2(0.f, 0.f);
-          float2 cmp = unpack_bf16(*reinterpret_cast<const uint32_t*>(crow + head * 64 + dim));
-          float x0 = bf16_round(sel.x * g1), x1 = bf16_round(sel.y * g1);
-          x0 = bf16_round(x0 + cmp.x * g0);
-          x1 = bf16_round(x1 + cmp.y * g0);
-          x0 = x0 + win.x * g2;
-          x1 = x1 + win.y * g2;
-          *reinterpret_cast<uint32_t*>(orow + head * 64 + dim) = cxs::pack_bf16(x0, x1);
-        }
-      }
-    }
+  // All warps (IO included) meet before the TMEM columns are released.
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemAlloc));
   }
 }
 
@@ -334,7 +500,7 @@ int encode_window_map(CUtensorMap* map, const void* records, int heads, int reco
   if (!fn) return set_error(CXS_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {128, (cuuint64_t)heads, (cuuint64_t)records_n};
   cuuint64_t strides[2] = {256, (cuuint64_t)heads * 256};
-  cuuint32_t box[3] = {64, 1, (cuuint32_t)bs};
+  cuuint32_t box[3] = {64, 1, 64};  // window tiles are always 64 records
   cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(records), dims,
                   strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -346,7 +512,9 @@ int encode_window_map(CUtensorMap* map, const void* records, int heads, int reco
 template <int BS>
 size_t smem_bytes() {
   size_t io = ((size_t)BS * kTokenBytes + 1023) & ~(size_t)1023;
-  return 1024 + io + (size_t)kAttnWarps * 2 * BS * 128 + (kAttnWarps + 1) * 8;
+  size_t tiles = 2 * (size_t)cxs::tc::kRowTileBytes;
+  size_t warps = (size_t)kAttnWarps * cxs::tc::WarpSmem::kBytes;
+  return 1024 + io + tiles + warps + 128;
 }
 
 struct GridInfo {
@@ -401,8 +569,7 @@ int launch(const cxs_attend_geometry& g, const cxs_attend_buffers& b, cudaStream
   a.gate = g.gate;
   a.window_start = g.window_start;
   a.spin_limit = g.spin_limit > 0 ? g.spin_limit : (1ll << 31);
-  int rows = g.queries * g.heads;
-  a.consumers = rows < grid * kAttnWarps ? rows : grid * kAttnWarps;
+  a.consumers = grid * kAttnWarps;
   a.query = (const __nv_bfloat16*)b.query;
   a.kv = (__nv_bfloat16*)b.kv;
   a.all_ids = b.all_ids;
@@ -452,8 +619,12 @@ extern "C" int cxs_fetch_attend(const cxs_attend_geometry* geometry,
   const cxs_attend_buffers& b = *buffers;
   if (g.queries < 1 || g.heads < 1 || g.width < 1 || g.physical < 1)
     return set_error(CXS_ERR_INVALID, "nonempty attend geometry required");
+  if (g.width > 32)
+    return set_error(CXS_ERR_INVALID, "width (top-n) must be at most 32");
   if (g.window < 0 || (g.window > 0 && (!b.window_kv || g.window_len < 1)))
     return set_error(CXS_ERR_INVALID, "window branch needs a window buffer");
+  if (g.window > 0 && (g.window_start < 0 || g.window_start + g.window_len > INT32_MAX))
+    return set_error(CXS_ERR_INVALID, "window positions must fit int32");
   if (g.gate && (!b.compressed || !b.gates))
     return set_error(CXS_ERR_INVALID, "gate mix needs compressed output and gates");
   if (((uintptr_t)b.kv & 15) || ((uintptr_t)b.query & 15) || ((uintptr_t)b.out & 15))
