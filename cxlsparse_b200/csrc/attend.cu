@@ -122,14 +122,16 @@ __global__ void prepare_kernel(int P, int BS, const int64_t* __restrict__ addres
 // (duplicates attended again, as the reference does), on the tcgen05 engine
 // of tile_tc.cuh, and writes the (gate-mixed) output.
 //
-// Per tile t in stage st (K/V double-buffered; one mbarrier commit C_t per
-// tile covers P.V of tile t-1 and S of tile t):
-//   A  every lane waits C_t; lane 0 starts the copy of tile t+1 into the other
-//      stage (acquire-waiting on ready[b] for a selected block)
+// Tile t uses K buffer t % 2 and V buffer t % 2; one mbarrier commit C_t per
+// tile covers P.V of tile t-1 and S of tile t. Lane 0 keeps the copies ahead:
+// K of tile j may start once S of tile j-2 is done, V of tile j once P.V of
+// tile j-2 is, and a selected block only after its ready flag is set.
+//   A  every lane waits C_t; lane 0 starts what is free and known ready
 //   B  softmax of S(t) -> P, running max/denominator, O rescale in TMEM
-//   C  the warp agrees on the status of every wait; a failure ends the launch
-//      for this warp after its copies have landed
-//   D  lane 0 issues O += P.V(t), waits for tile t+1, issues S(t+1), commits
+//   C  lane 0 makes sure K of tile t+1 is under way (acquire-waiting on its
+//      ready flag); the warp agrees on every wait's status, and a failure
+//      ends the launch for this warp once its copies have landed
+//   D  lane 0 issues O += P.V(t) and S(t+1) as their copies land, commits
 template <int BS>
 __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
                                                const CUtensorMap& win_map, const AttendArgs& a,
@@ -145,22 +147,21 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
   const uint32_t s_addr = s_col + lane_off, o_addr = o_col + lane_off;
   const uint32_t id_s = tc::idesc_bf16(128, 64, 0, 0), id_o = tc::idesc_bf16(128, 64, 0, 1);
   const uint32_t q_addr = cxs::smem_addr(q_tile), p_addr = cxs::smem_addr(p_tile);
-  uint32_t tma_phases = 0, mma_phase = 0;  // bit s of tma_phases: phase of stage s
-  int stage = 0;
+  uint32_t k_phase = 0, v_phase = 0, mma_phase = 0;  // bit b: phase of buffer b
   const int rows = a.Q * a.H;
   if (leader) {
     cxs::tma_prefetch_desc(&kv_map);
     if (a.window) cxs::tma_prefetch_desc(&win_map);
   }
-  auto mma_scores = [&](int stg) {  // S = Q . K(stg)^T
-    const uint32_t ka = cxs::smem_addr(ws.k(stg));
+  auto mma_scores = [&](int b) {  // S = Q . K(b)^T
+    const uint32_t ka = cxs::smem_addr(ws.k(b));
 #pragma unroll
     for (int k = 0; k < 4; ++k)
       tc::mma(s_col, tc::desc_sw128(q_addr + 32 * k, 16, 1024),
               tc::desc_sw128(ka + 32 * k, 16, 1024), id_s, k);
   };
-  auto mma_output = [&](int stg, bool accumulate) {  // O (+)= P . V(stg)
-    const uint32_t va = cxs::smem_addr(ws.v(stg));
+  auto mma_output = [&](int b, bool accumulate) {  // O (+)= P . V(b)
+    const uint32_t va = cxs::smem_addr(ws.v(b));
 #pragma unroll
     for (int k = 0; k < 4; ++k)
       tc::mma(o_col, tc::desc_sw128(p_addr + 32 * k, 16, 1024),
@@ -186,28 +187,99 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
       my_block = a.all_ids[(long long)row * a.W + lane];
       if (my_block >= 0 && my_block < a.P) my_start = a.starts[my_block];
     }
+    // Block of tile j (all lanes; -1 for window tiles and past the end).
+    auto block_of = [&](int j) {
+      const int b = __shfl_sync(0xffffffffu, my_block, (j - n_win) & 31);
+      return (j >= n_win && j < total) ? b : -1;
+    };
     tc::write_query_row(q_tile, a.query, row, m, lane);
     cxs::fence_proxy_async_shared();
     __syncwarp();
-    // Lane 0: start the copy of tile t into stage stg (false: bad block or
-    // ready wait failed).
-    auto issue = [&](int t, int block, int stg) -> bool {
-      if (t < n_win) {
-        cxs::mbar_expect_tx(ws.tma_bar(stg), 2 * tc::kTileBytes);
-        tc::window_load(ws.k(stg), ws.v(stg), &win_map, h,
-                        w_lo + t * tc::kTileRows - (int)a.window_start, ws.tma_bar(stg));
-        return true;
+    // Lane 0's copy schedule for this row: K / V copies of tiles [0, kn) /
+    // [0, vn) started, [0, kw) / [0, vw) landed.
+    int kn = 0, vn = 0, kw = 0, vw = 0;
+    int pf_tile = -1, pf_ready = 0;  // ready flag of tile pf_tile, acquire-loaded earlier
+    bool failed = false;
+    auto start_copy = [&](int j, int blk, bool value) {
+      const int b = j & 1;
+      uint64_t* bar = value ? ws.vbar(b) : ws.kbar(b);
+      uint8_t* dst = value ? ws.v(b) : ws.k(b);
+      if (j < n_win) {
+        cxs::mbar_expect_tx(bar, tc::kTileBytes);
+        tc::window_load(dst, &win_map, value ? 64 : 0, h,
+                        w_lo + j * tc::kTileRows - (int)a.window_start, bar);
+      } else {
+        cxs::mbar_expect_tx(bar, BS * 128);
+        cxs::tma_load_2d(dst, &kv_map, value ? 64 : 0, blk * BS, bar);
       }
-      if (block < 0 || block >= a.P) {
-        atomicOr(a.error, cxs::kErrBadBlock);
-        return false;
+    };
+    // Start every copy that is free during step t (K of tiles <= t + 2, V of
+    // tiles <= t + 1 whose K is under way) and whose block is known ready;
+    // with `need_k`, K of tile t + 1 is started even if that means waiting
+    // for its ready flag. b1..b3: blocks of tiles t + 1 .. t + 3.
+    auto pump = [&](int t, int b1, int b2, int b3, bool need_k) {
+      while (!failed && kn < total && kn <= t + 2) {
+        const int j = kn, blk = j == t + 1 ? b1 : b2;
+        if (j >= n_win) {
+          if (j < t + 1 || blk < 0 || blk >= a.P) {
+            atomicOr(a.error, cxs::kErrBadBlock);
+            failed = true;
+            break;
+          }
+          if (!(pf_tile == j && pf_ready)) {
+            if (!(need_k && j == t + 1)) break;
+            if (!cxs::wait_ready_bounded(&a.ready[blk], a.spin_limit, a.error)) {
+              failed = true;
+              break;
+            }
+          }
+          cxs::fence_proxy_async_global();
+        }
+        start_copy(j, blk, false);
+        ++kn;
       }
-      if (!cxs::wait_ready_bounded(&a.ready[block], a.spin_limit, a.error)) return false;
-      cxs::fence_proxy_async_global();
-      cxs::mbar_expect_tx(ws.tma_bar(stg), 2 * BS * 128);
-      cxs::tma_load_2d(ws.k(stg), &kv_map, 0, block * BS, ws.tma_bar(stg));
-      cxs::tma_load_2d(ws.v(stg), &kv_map, 64, block * BS, ws.tma_bar(stg));
-      return true;
+      while (!failed && vn < kn && vn <= t + 1) {
+        const int blk = vn == t + 1 ? b1 : -1;
+        if (vn >= n_win && (blk < 0 || blk >= a.P)) {
+          atomicOr(a.error, cxs::kErrBadBlock);
+          failed = true;
+          break;
+        }
+        start_copy(vn, blk, true);
+        ++vn;
+      }
+      // Acquire-load the ready flag of the next K tile now; it is read at
+      // the next call, after its latency has passed.
+      if (!failed && kn < total && kn >= n_win && !(pf_tile == kn && pf_ready)) {
+        const int blk = kn == t + 1 ? b1 : (kn == t + 2 ? b2 : b3);
+        if (blk >= 0 && blk < a.P) {
+          pf_tile = kn;
+          pf_ready = cxs::ld_acquire(&a.ready[blk]);
+        }
+      }
+    };
+    // Lane 0: let every started copy land (bounded) before giving up the row.
+    auto drain = [&]() {
+      for (; kw < kn; ++kw) {
+        tc::bounded_wait(ws.kbar(kw & 1), (k_phase >> (kw & 1)) & 1u, a.spin_limit, a.error,
+                         cxs::kErrCopyTimeout);
+        k_phase ^= 1u << (kw & 1);
+      }
+      for (; vw < vn; ++vw) {
+        tc::bounded_wait(ws.vbar(vw & 1), (v_phase >> (vw & 1)) & 1u, a.spin_limit, a.error,
+                         cxs::kErrCopyTimeout);
+        v_phase ^= 1u << (vw & 1);
+      }
+    };
+    auto land = [&](bool value) -> bool {  // lane 0: wait for the next K or V copy
+      int& done = value ? vw : kw;
+      uint32_t& phase = value ? v_phase : k_phase;
+      const int b = done & 1;
+      const bool ok = tc::bounded_wait(value ? ws.vbar(b) : ws.kbar(b), (phase >> b) & 1u,
+                                       a.spin_limit, a.error, cxs::kErrCopyTimeout);
+      phase ^= 1u << b;
+      ++done;
+      return ok;
     };
     bool alive = true;
     float m_run = -INFINITY, l_run = 0.f;
@@ -215,24 +287,23 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
 #pragma unroll
     for (int i = 0; i < 16; ++i) win_packed[i] = 0;
     if (total > 0) {
-      bool step_ok = true;  // lane 0: every wait of the coming step succeeded
-      const int block0 = __shfl_sync(0xffffffffu, my_block, 0);
-      if (leader) {
-        step_ok = issue(0, n_win > 0 ? -1 : block0, stage);
-        if (step_ok) {
-          step_ok = tc::bounded_wait(ws.tma_bar(stage), (tma_phases >> stage) & 1u, a.spin_limit,
-                                     a.error, cxs::kErrCopyTimeout);
-          tma_phases ^= 1u << stage;
+      {
+        const int b0 = block_of(0), b1 = block_of(1), b2 = block_of(2);
+        if (leader) {
+          pump(-1, b0, b1, b2, true);
+          if (!failed) failed = !land(false);
+          if (!failed) {
+            tc::fence_after();
+            mma_scores(0);
+          }
+          tc::commit(ws.mma_bar());
         }
-        if (step_ok) {
-          tc::fence_after();
-          mma_scores(stage);
-        }
-        tc::commit(ws.mma_bar());
       }
       for (int t = 0; t < total; ++t) {
-        const int st = stage;
         const bool first_of_branch = t == 0 || t == n_win;
+        const int b1 = block_of(t + 1), b2 = block_of(t + 2), b3 = block_of(t + 3);
+        const int cur_block = __shfl_sync(0xffffffffu, my_block, (t - n_win) & 31);
+        const int cur_start = __shfl_sync(0xffffffffu, my_start, (t - n_win) & 31);
         // A
         const bool waited = tc::bounded_wait(ws.mma_bar(), mma_phase, a.spin_limit, a.error,
                                              cxs::kErrCopyTimeout);
@@ -244,24 +315,16 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
           tc::combine_o(o_addr, half, o);
           const float den = l_run > 0.f ? l_run : 1.f;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) win_packed[i] = cxs::pack_bf16(o[2 * i] / den, o[2 * i + 1] / den);
+          for (int i = 0; i < 16; ++i)
+            win_packed[i] = cxs::pack_bf16(o[2 * i] / den, o[2 * i + 1] / den);
           m_run = -INFINITY;
           l_run = 0.f;
         }
-        const int cur_block = __shfl_sync(0xffffffffu, my_block, (t - n_win) & 31);
-        const int cur_start = __shfl_sync(0xffffffffu, my_start, (t - n_win) & 31);
-        const int next_block = __shfl_sync(0xffffffffu, my_block, (t + 1 - n_win) & 31);
-        bool next_issued = false;
-        if (leader && t + 1 < total) {
-          next_issued = issue(t + 1, next_block, st ^ 1);
-          step_ok = step_ok && next_issued;
-        }
+        if (leader) pump(t, b1, b2, b3, false);
         // B
         int lo = 0, hi = -1;
         if (t < n_win) {
-          const int t0 = w_lo + t * tc::kTileRows;
-          lo = 0;
-          hi = min(w_hi - t0, tc::kTileRows - 1);
+          hi = min(w_hi - (w_lo + t * tc::kTileRows), tc::kTileRows - 1);
         } else if (cur_block >= 0 && cur_block < a.P) {
           hi = min(pos - cur_start, BS - 1);
         }
@@ -271,28 +334,34 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
         cxs::fence_proxy_async_shared();
         tc::fence_before();
         // C
-        const bool ok = __all_sync(0xffffffffu, waited) && __shfl_sync(0xffffffffu, step_ok, 0);
+        if (leader) pump(t, b1, b2, b3, true);
+        const bool ok = __all_sync(0xffffffffu, waited) && !__shfl_sync(0xffffffffu, failed, 0);
         if (!ok) {
-          if (leader && next_issued)  // let the copy land before shared memory is released
-            tc::bounded_wait(ws.tma_bar(st ^ 1), (tma_phases >> (st ^ 1)) & 1u, a.spin_limit,
-                             a.error, cxs::kErrCopyTimeout);
+          if (leader) drain();
           alive = false;
           break;
         }
         // D
         if (leader) {
           tc::fence_after();
-          mma_output(st, !first_of_branch);
-          if (t + 1 < total) {
-            step_ok = tc::bounded_wait(ws.tma_bar(st ^ 1), (tma_phases >> (st ^ 1)) & 1u,
-                                       a.spin_limit, a.error, cxs::kErrCopyTimeout);
-            tma_phases ^= 1u << (st ^ 1);
-            if (step_ok) mma_scores(st ^ 1);
+          if (land(true)) {
+            mma_output(t & 1, !first_of_branch);
+            if (t + 1 < total) {
+              if (land(false))
+                mma_scores((t + 1) & 1);
+              else
+                failed = true;
+            }
+          } else {
+            failed = true;
           }
           tc::commit(ws.mma_bar());
         }
         __syncwarp();
-        stage ^= 1;
+      }
+      if (alive && __shfl_sync(0xffffffffu, failed, 0)) {
+        if (leader) drain();
+        alive = false;
       }
       if (!alive) break;
       // E: the last P.V is complete.
@@ -304,7 +373,8 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
         tc::combine_o(o_addr, half, o);
         const float den = l_run > 0.f ? l_run : 1.f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) win_packed[i] = cxs::pack_bf16(o[2 * i] / den, o[2 * i + 1] / den);
+        for (int i = 0; i < 16; ++i)
+          win_packed[i] = cxs::pack_bf16(o[2 * i] / den, o[2 * i + 1] / den);
         l_run = 0.f;
       }
     }
@@ -381,8 +451,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     cxs::mbar_init(io_bar, 1);
     for (int w = 0; w < kAttnWarps; ++w) {
       tc::WarpSmem ws{warps_base + w * tc::WarpSmem::kBytes};
-      cxs::mbar_init(ws.tma_bar(0), 1);
-      cxs::mbar_init(ws.tma_bar(1), 1);
+      for (int b = 0; b < 2; ++b) {
+        cxs::mbar_init(ws.kbar(b), 1);
+        cxs::mbar_init(ws.vbar(b), 1);
+      }
       cxs::mbar_init(ws.mma_bar(), 1);
     }
     cxs::fence_mbar_init();

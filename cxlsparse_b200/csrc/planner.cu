@@ -484,21 +484,20 @@ __global__ void __launch_bounds__(kChunk) chunk_compact_kernel(Geo g, cxs_plan_b
 // Top-`hot` indices of a head's frequency table by (frequency desc, index asc)
 // (active.py:449-500; stable argsort fallback active.py:884-888): find the
 // threshold frequency by a radix select over the significant bytes of the
-// maximum, keep every larger frequency and the lowest-index ties, then sort
-// the `hot` winners. Histograms use warp-aggregated shared atomics because
-// most frequencies share a few small values.
+// maximum, keep every larger frequency and the lowest-index ties (an ordered
+// warp-segmented gather), then sort the `hot` winners (rank counting up to
+// 1024 of them, a block radix sort above). Histograms use warp-aggregated
+// shared atomics because most frequencies share a few small values.
 template <int ITEMS>
 __global__ void __launch_bounds__(1024) hot_select_kernel(Geo g, cxs_plan_buffers b) {
   typedef cub::BlockRadixSort<unsigned long long, 1024, ITEMS> Sort;
-  typedef cub::BlockScan<int, 1024> Scan;
   typedef cub::BlockReduce<unsigned int, 1024> Reduce;
   extern __shared__ __align__(16) unsigned char sort_mem[];
   auto& temp = *reinterpret_cast<typename Sort::TempStorage*>(sort_mem);
-  __shared__ typename Scan::TempStorage scan;
   __shared__ typename Reduce::TempStorage reduce;
   __shared__ int hist[256];
   __shared__ unsigned int prefix_s, mask_s, max_s;
-  __shared__ int remaining_s, greater_base, equal_base;
+  __shared__ int remaining_s;
   __shared__ unsigned long long cand[kMaxHot];
   int h = blockIdx.x;
   int lane = threadIdx.x & 31;
@@ -511,8 +510,6 @@ __global__ void __launch_bounds__(1024) hot_select_kernel(Geo g, cxs_plan_buffer
     max_s = fmax;
     prefix_s = 0;
     remaining_s = g.HOT;
-    greater_base = 0;
-    equal_base = 0;
     int top = 0;  // highest byte holding a set bit of the maximum
     while (top < 24 && (fmax >> (top + 8))) top += 8;
     mask_s = top >= 24 ? 0u : ~((1u << (top + 8)) - 1u);  // bytes above `top` are zero
@@ -550,24 +547,59 @@ __global__ void __launch_bounds__(1024) hot_select_kernel(Geo g, cxs_plan_buffer
   unsigned int threshold = prefix_s;
   int need_eq = remaining_s;                 // ties at the threshold, lowest indices first
   int greater_total = g.HOT - need_eq;       // every frequency above the threshold
-  // Ordered gather: one scan per chunk of (greater, equal) counts packed in an int.
-  for (int base = 0; base < n; base += blockDim.x) {
-    int i = base + threadIdx.x;
-    unsigned int f = i < n ? (unsigned)freq[i] : 0u;
-    bool greater = i < n && f > threshold;
-    bool equal = i < n && f == threshold;
-    int packed = (greater ? 1 : 0) + (equal ? (1 << 16) : 0), prefix, total;
-    Scan(scan).ExclusiveSum(packed, prefix, total);
-    unsigned long long key = ((unsigned long long)(0x7FFFFFFFu - f) << 32) | (unsigned int)i;
-    if (greater) cand[greater_base + (prefix & 0xFFFF)] = key;
-    int eq_rank = equal_base + (prefix >> 16);
-    if (equal && eq_rank < need_eq) cand[greater_total + eq_rank] = key;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      greater_base += total & 0xFFFF;
-      equal_base += total >> 16;
+  // Ordered gather: warp w owns the contiguous segment [s0, s1); a counting
+  // pass and a scan over the 32 warps give each warp its output offsets.
+  const int warp = threadIdx.x >> 5;
+  const int seg = (n + 31) / 32, s0 = min(n, warp * seg), s1 = min(n, s0 + seg);
+  const unsigned lower = (1u << lane) - 1u;
+  int count_g = 0, count_e = 0;
+  for (int i = s0 + lane; i < s1; i += 32) {
+    unsigned int f = (unsigned)freq[i];
+    count_g += f > threshold;
+    count_e += f == threshold;
+  }
+  for (int o = 16; o; o >>= 1) {
+    count_g += __shfl_xor_sync(0xffffffffu, count_g, o);
+    count_e += __shfl_xor_sync(0xffffffffu, count_e, o);
+  }
+  if (lane == 0) {
+    hist[warp] = count_g;
+    hist[32 + warp] = count_e;
+  }
+  __syncthreads();
+  if (warp < 2) {  // warp 0: greater offsets, warp 1: equal offsets (exclusive scans)
+    int own = hist[32 * warp + lane], inclusive = own;
+    for (int o = 1; o < 32; o <<= 1) {
+      int other = __shfl_up_sync(0xffffffffu, inclusive, o);
+      if (lane >= o) inclusive += other;
     }
-    __syncthreads();
+    hist[64 + 32 * warp + lane] = inclusive - own;
+  }
+  __syncthreads();
+  int g_at = hist[64 + warp], e_at = hist[96 + warp];
+  for (int i0 = s0; i0 < s1; i0 += 32) {
+    int i = i0 + lane;
+    unsigned int f = i < s1 ? (unsigned)freq[i] : 0u;
+    bool greater = i < s1 && f > threshold;
+    bool equal = i < s1 && f == threshold;
+    unsigned mg = __ballot_sync(0xffffffffu, greater), me = __ballot_sync(0xffffffffu, equal);
+    unsigned long long key = ((unsigned long long)(0x7FFFFFFFu - f) << 32) | (unsigned int)i;
+    if (greater) cand[g_at + __popc(mg & lower)] = key;
+    int eq_rank = e_at + __popc(me & lower);
+    if (equal && eq_rank < need_eq) cand[greater_total + eq_rank] = key;
+    g_at += __popc(mg);
+    e_at += __popc(me);
+  }
+  __syncthreads();
+  if (g.HOT <= 1024) {
+    // Rank sort of the (distinct) winner keys: rank = number of smaller keys.
+    if (threadIdx.x < g.HOT) {
+      unsigned long long key = cand[threadIdx.x];
+      int rank = 0;
+      for (int j = 0; j < g.HOT; ++j) rank += cand[j] < key;
+      b.chosen[(long long)h * g.HOT + rank] = (int)(key & 0xFFFFFFFFull);
+    }
+    return;
   }
   unsigned long long keys[ITEMS];
 #pragma unroll

@@ -145,18 +145,22 @@ __device__ __forceinline__ uint32_t sw128_chunk(int row, int chunk) {
   return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-// Per-warp shared memory: two K/V stages and the warp's mbarriers.
+// Per-warp shared memory: two K buffers, two V buffers and the mbarriers
+// (K and V copies of a tile land separately: K is needed one step before V).
 struct WarpSmem {
-  static constexpr int kBars = 4 * kTileBytes;  // tma_bar[2], mma_bar
+  static constexpr int kBars = 4 * kTileBytes;  // kbar[2], vbar[2], mma_bar
   static constexpr int kBytes = kBars + 1024;   // keeps the next warp 1024-aligned
   uint8_t* base;
-  __device__ __forceinline__ uint8_t* k(int stage) const { return base + stage * 2 * kTileBytes; }
-  __device__ __forceinline__ uint8_t* v(int stage) const { return k(stage) + kTileBytes; }
-  __device__ __forceinline__ uint64_t* tma_bar(int stage) const {
-    return reinterpret_cast<uint64_t*>(base + kBars) + stage;
+  __device__ __forceinline__ uint8_t* k(int b) const { return base + b * kTileBytes; }
+  __device__ __forceinline__ uint8_t* v(int b) const { return base + (2 + b) * kTileBytes; }
+  __device__ __forceinline__ uint64_t* kbar(int b) const {
+    return reinterpret_cast<uint64_t*>(base + kBars) + b;
+  }
+  __device__ __forceinline__ uint64_t* vbar(int b) const {
+    return reinterpret_cast<uint64_t*>(base + kBars) + 2 + b;
   }
   __device__ __forceinline__ uint64_t* mma_bar() const {
-    return reinterpret_cast<uint64_t*>(base + kBars) + 2;
+    return reinterpret_cast<uint64_t*>(base + kBars) + 4;
   }
 };
 
@@ -177,19 +181,15 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t phase, long
   return true;
 }
 
-// Window tile: 64 records of KV head `head` starting at record `record0`
-// (3-D map {channel, head, record}; out-of-range records are zero-filled).
-__device__ __forceinline__ void window_load(uint8_t* k, uint8_t* v, const void* map, int head,
+// Half (K: channels 0-63, V: 64-127) of a window tile: 64 records of KV head
+// `head` from record `record0` (3-D map {channel, head, record};
+// out-of-range records are zero-filled).
+__device__ __forceinline__ void window_load(uint8_t* dst, const void* map, int channel, int head,
                                             int record0, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(k)),
-      "l"(map), "r"(0), "r"(head), "r"(record0), "r"(smem_addr(bar))
-      : "memory");
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(v)),
-      "l"(map), "r"(64), "r"(head), "r"(record0), "r"(smem_addr(bar))
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(channel), "r"(head), "r"(record0), "r"(smem_addr(bar))
       : "memory");
 }
 
@@ -212,37 +212,75 @@ __device__ __forceinline__ void write_query_row(uint8_t* q_tile, const __nv_bflo
   }
 }
 
+// 2^x with the hardware approximation (flushes results below 2^-126 to 0,
+// far below what a bf16 probability or an fp32 denominator resolves here).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Online softmax over one tile for this lane's half (tokens 32 * half ..
 // 32 * half + 31) of its head's row; tokens outside [lo, hi] are masked. The
 // lane and its partner (lane ^ 16) agree on the tile max and sum. Writes the
 // lane's 32 bf16 probabilities into P row `m` and returns the factor the
-// running output must be scaled by.
+// running output must be scaled by. p = 2^(s log2e - m log2e), the exp2 form
+// of the reference's exp(s - m).
 __device__ __forceinline__ float softmax_half(uint8_t* p_tile, uint32_t s_addr, int lo, int hi,
                                               float& m_run, float& l_run, int m, int half) {
   float sv[32];
   {
-    float lo_cols[32], hi_cols[32];
-    ld32(s_addr, lo_cols);
-    ld32(s_addr + 32, hi_cols);
+    uint32_t r0[32], r1[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r0[0]), "=r"(r0[1]), "=r"(r0[2]), "=r"(r0[3]), "=r"(r0[4]), "=r"(r0[5]),
+          "=r"(r0[6]), "=r"(r0[7]), "=r"(r0[8]), "=r"(r0[9]), "=r"(r0[10]), "=r"(r0[11]),
+          "=r"(r0[12]), "=r"(r0[13]), "=r"(r0[14]), "=r"(r0[15]), "=r"(r0[16]), "=r"(r0[17]),
+          "=r"(r0[18]), "=r"(r0[19]), "=r"(r0[20]), "=r"(r0[21]), "=r"(r0[22]), "=r"(r0[23]),
+          "=r"(r0[24]), "=r"(r0[25]), "=r"(r0[26]), "=r"(r0[27]), "=r"(r0[28]), "=r"(r0[29]),
+          "=r"(r0[30]), "=r"(r0[31])
+        : "r"(s_addr));
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r1[0]), "=r"(r1[1]), "=r"(r1[2]), "=r"(r1[3]), "=r"(r1[4]), "=r"(r1[5]),
+          "=r"(r1[6]), "=r"(r1[7]), "=r"(r1[8]), "=r"(r1[9]), "=r"(r1[10]), "=r"(r1[11]),
+          "=r"(r1[12]), "=r"(r1[13]), "=r"(r1[14]), "=r"(r1[15]), "=r"(r1[16]), "=r"(r1[17]),
+          "=r"(r1[18]), "=r"(r1[19]), "=r"(r1[20]), "=r"(r1[21]), "=r"(r1[22]), "=r"(r1[23]),
+          "=r"(r1[24]), "=r"(r1[25]), "=r"(r1[26]), "=r"(r1[27]), "=r"(r1[28]), "=r"(r1[29]),
+          "=r"(r1[30]), "=r"(r1[31])
+        : "r"(s_addr + 32));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 32; ++i) sv[i] = half ? hi_cols[i] : lo_cols[i];
+    for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(half ? r1[i] : r0[i]);
   }
-  const int first = 32 * half;
-  float mt = -INFINITY;
+  // This lane's valid tokens: [lo_l, hi_l] within its 32.
+  const int lo_l = lo - 32 * half, hi_l = hi - 32 * half;
+  const bool whole = lo_l <= 0 && hi_l >= 31;
+  if (!__all_sync(0xffffffffu, whole)) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i)
-    if (first + i >= lo && first + i <= hi) mt = fmaxf(mt, sv[i]);
+    for (int i = 0; i < 32; ++i)
+      if (i < lo_l || i > hi_l) sv[i] = -INFINITY;
+  }
+  float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], sv[i]);
+  float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
   mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
   const float updated = fmaxf(m_run, mt);
-  const float factor = m_run == -INFINITY ? 0.f : exp2f((m_run - updated) * kLog2e);
+  const float factor = m_run == -INFINITY ? 0.f : ex2((m_run - updated) * kLog2e);
   m_run = updated;
-  float sum = 0.f;
+  // A fully masked row so far (updated = -inf) gets p = 0 everywhere.
+  const float offset = updated == -INFINITY ? 0.f : updated * kLog2e;
+  float sm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    const float v = (first + i >= lo && first + i <= hi) ? exp2f((sv[i] - updated) * kLog2e) : 0.f;
+    const float v = ex2(fmaf(sv[i], kLog2e, -offset));  // masked: 2^-inf = 0
     sv[i] = v;
-    sum += v;
+    sm[i & 3] += v;
   }
+  float sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
   sum += __shfl_xor_sync(0xffffffffu, sum, 16);
   l_run = l_run * factor + sum;
 #pragma unroll

@@ -13,12 +13,13 @@ def _stream():
     return torch.cuda.current_stream().cuda_stream
 
 
-def test_rms_norm_matches_torch_sequence(cuda):
+@pytest.mark.parametrize("dim", [2048, 8192, 1000, 9000])  # vector path, then scalar
+def test_rms_norm_matches_torch_sequence(cuda, dim):
     torch.manual_seed(0)
-    x = torch.randn(37, 2048, device=cuda).bfloat16()
-    w = (torch.rand(2048, device=cuda) + 0.5).bfloat16()
+    x = torch.randn(37, dim, device=cuda).bfloat16()
+    w = (torch.rand(dim, device=cuda) + 0.5).bfloat16()
     out = torch.empty_like(x)
-    _lib.check(_lib.lib().cxs_rms_norm(x.data_ptr(), w.data_ptr(), out.data_ptr(), 37, 2048,
+    _lib.check(_lib.lib().cxs_rms_norm(x.data_ptr(), w.data_ptr(), out.data_ptr(), 37, dim,
                                        1e-6, _stream()))
     torch.testing.assert_close(out.float(), rms_norm(x, w, 1e-6).float(), rtol=0.01, atol=0.01)
 
@@ -51,10 +52,11 @@ def test_qkv_rope_gates_and_packing(cuda):
     torch.testing.assert_close(gates.float(), g.float(), rtol=0.01, atol=0.01)
 
 
-def test_silu_mul(cuda):
+@pytest.mark.parametrize("ffn", [300, 5632])  # scalar path, vector path
+def test_silu_mul(cuda, ffn):
     torch.manual_seed(2)
-    gu = torch.randn(9, 2 * 300, device=cuda).bfloat16()
-    out = torch.empty(9, 300, dtype=torch.bfloat16, device=cuda)
-    _lib.check(_lib.lib().cxs_silu_mul(gu.data_ptr(), 9, 300, out.data_ptr(), _stream()))
-    expected = torch.nn.functional.silu(gu[:, :300]) * gu[:, 300:]
+    gu = torch.randn(9, 2 * ffn, device=cuda).bfloat16()
+    out = torch.empty(9, ffn, dtype=torch.bfloat16, device=cuda)
+    _lib.check(_lib.lib().cxs_silu_mul(gu.data_ptr(), 9, ffn, out.data_ptr(), _stream()))
+    expected = torch.nn.functional.silu(gu[:, :ffn]) * gu[:, ffn:]
     torch.testing.assert_close(out.float(), expected.float(), rtol=0.01, atol=0.01)
