@@ -29,6 +29,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "NSA-1B extend tok/s @H16K/E256 at 1–8 B200; KV-fetch GB/s vs PCIe5 peak"
 REFERENCE_TOK_S = 13503.0  # derived H100 worker tok/s @H16K/E256 (E / worker p50)
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
+# fetch_attend_kernel<64> launch of the H=16384/E=256 extend step, from an
+# ncu --set full capture (NVTX range profile_step). The staged and window KV
+# stay in L2, so DRAM sees far less than the algorithmic bytes.
+NCU_DRAM_BYTES_PER_LAUNCH = 2.94e6
 
 
 def parse():
@@ -325,7 +330,10 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "roofline": {"bound": "hbm", "kernel": "fetch_attend_kernel<64>",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None,
+                         "frac": achieved / hbm,
+                         "traffic": NCU_DRAM_BYTES_PER_LAUNCH
+                         if (args.history, args.extend) == (16384, 256) else None,
+                         "binding": "host link: see fetch.frac_of_pcie_in_kernel",
                          "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"
                          if peak_kind == "measured" else "fallback",
                          "algorithmic_bytes_per_launch": algorithmic,
