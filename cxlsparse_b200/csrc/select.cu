@@ -9,16 +9,20 @@
 //    score descending with ties to the lower block id; width =
 //    min(count, ceil(total / BS)); remaining entries -1.
 //
-// One CTA of 4 warps per (query row, KV head); the warps split the 64-summary
-// tiles (staged by 3-D tensor TMA). Pass 1: per-warp online softmax + PV,
-// merged across warps in shared memory (compressed branch output). Pass 2:
-// scores recomputed with the merged per-head max / normaliser, reduced over
-// heads; warp 0 selects the top-n.
+// Two kernels. compressed_select_tc_kernel (tcgen05 / TMEM, 8 query rows per
+// CTA, 16 warps) serves every geometry whose per-row scores fit in shared memory (up to
+// 2048 blocks); compressed_select_kernel (one CTA of 4 warps per query row,
+// mma.sync tiles) serves longer histories. In the latter the warps split the
+// 64-summary tiles (staged by 3-D tensor TMA). Pass 1: per-warp online
+// softmax + PV, merged across warps in shared memory (compressed branch
+// output). Pass 2: scores recomputed with the merged per-head max /
+// normaliser, reduced over heads; warp 0 selects the top-n.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include "cxs_common.cuh"
 #include "tile_attn.cuh"
+#include "tile_tc.cuh"
 
 using cxs_host::set_error;
 
@@ -28,9 +32,14 @@ constexpr int kWarps = 4;
 constexpr int kTileKeys = 64;
 constexpr int kTileBytes = kTileKeys * 128;
 
-// Error sink for the kernel's bounded copy waits (its copies read device
+// Error sink for the kernels' bounded copy waits (their copies read device
 // memory only, so a timeout indicates a broken launch, not a slow link).
 __device__ int g_select_error;
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxSmem = 227 * 1024;
+bool g_select_ready[kMaxDevices] = {false};
+int* g_select_error_address[kMaxDevices] = {nullptr};
 
 struct SelectArgs {
   int Q, H, C, BS, count, width, score_len;
@@ -214,6 +223,383 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+// ------------------------------------------------- tcgen05 / TMEM variant ---
+// One CTA of 16 warps per (8 query rows, KV head h). The 8 rows x 16 GQA
+// heads form the M = 128 rows of the A operand: TMEM lane m (warps m / 32,
+// m / 32 + 4, + 8, + 12, which may all read that lane group) is query row
+// q0 + m / 16, head m % 16. The four warps of a lane group split every
+// 256-record summary chunk by columns: column quarter cq = warp / 4 owns
+// columns 64 cq .. 64 cq + 63, i.e. P sub-tile cq. Summary chunks are staged
+// by 3-D tensor TMA (K: channels 0-63, V: 64-127, 128-byte swizzle).
+//   S[128 x 256] = Q . K^T             tcgen05.mma kind::f16, N = 64 x tiles
+//   pass 1: row max and normaliser from S (TMEM reads, online over chunks,
+//           the four column quarters combined through shared memory)
+//   pass 2: P = exp(S - max) -> bf16 shared tile; O[128 x 64] += P . V on
+//           tcgen05; block score = sum over the 16 heads of P / normaliser
+//           (shuffle reduce-scatter across the 16 lanes of a row)
+// then one warp per row picks the top-n from the scores in shared memory.
+// K and V stay resident across both passes when the summaries fit two
+// chunks (and shared memory); longer histories reload them per chunk.
+constexpr int kTcRows = 8;
+constexpr int kTcThreads = 512;
+constexpr int kTcChunk = 256;
+constexpr int kTcTileBytes = 64 * 128;              // one 64-record K or V box
+constexpr int kTcQBytes = 128 * 128;                // Q: 128 rows x 64 dims bf16
+constexpr int kTcChunkBytes = kTcChunk * 128;       // K or V of one chunk
+constexpr int kTcPBytes = 128 * kTcChunk * 2;       // P: 4 swizzled [128 x 64] sub-tiles
+constexpr int kTcMaxResident = 2;                   // K chunks kept for pass 2
+constexpr int kTcTmemCols = 512;                    // S (256) + O (64), power of two
+constexpr int kTcMaxScores = 2048;                  // per-row score slots in shared memory
+constexpr int kTcReduceBytes = 2 * 4 * 128 * 4;     // per-quarter row max / sum
+
+size_t tc_smem_bytes(int kres, int score_len) {
+  return 1024 + (size_t)kTcQBytes + 2 * (size_t)kres * kTcChunkBytes + kTcPBytes +
+         kTcReduceBytes + (size_t)kTcRows * score_len * 4 + 64;
+}
+
+// Top-n key of a score: non-negative scores order like their bit patterns;
+// taken (-1) and NaN entries get key 0 and are never picked.
+__device__ __forceinline__ uint32_t topn_key(float v) {
+  return v >= 0.f ? (__float_as_uint(v) & 0x7fffffffu) + 1u : 0u;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    compressed_select_tc_kernel(const __grid_constant__ CUtensorMap map, SelectArgs a,
+                                int kres) {
+  namespace tc = cxs::tc;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int H = a.H, C = a.C, score_len = a.score_len;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lg = warp & 3, cq = warp >> 2;  // TMEM lane group, column quarter
+  const int m = 32 * lg + lane;             // A row / TMEM lane of this thread
+  const int h = blockIdx.x % H;
+  const int q0 = (blockIdx.x / H) * kTcRows;
+  uint8_t* q_tile = smem;
+  uint8_t* k_base = q_tile + kTcQBytes;
+  uint8_t* v_base = k_base + kres * kTcChunkBytes;
+  uint8_t* p_tile = v_base + kres * kTcChunkBytes;
+  float* red_max = reinterpret_cast<float*>(p_tile + kTcPBytes);  // [4][128]
+  float* red_sum = red_max + 4 * 128;                               // [4][128]
+  float* scores = red_sum + 4 * 128;                                // [kTcRows][score_len]
+  uint64_t* tma_bar = reinterpret_cast<uint64_t*>(scores + kTcRows * score_len);
+  uint64_t* mma_bar = tma_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
+
+  // Every chunk of summaries is processed (rows mask what lies at or beyond
+  // their own complete-block count), so the copies can start at once.
+  const int chunks = (C + kTcChunk - 1) / kTcChunk;
+  const bool resident = chunks <= kres;  // K and V of every chunk stay in shared memory
+  auto tiles_of = [&](int j) { return min(4, (C - kTcChunk * j + 63) / 64); };
+  auto load_half = [&](int j, uint8_t* dst, int channel) {
+    for (int t = 0; t < tiles_of(j); ++t)
+      cxs::tma_load_3d(cxs::smem_addr(dst + t * kTcTileBytes), &map, channel, h,
+                       kTcChunk * j + 64 * t, tma_bar);
+  };
+  auto k_of = [&](int j) { return k_base + (resident ? j : 0) * kTcChunkBytes; };
+  auto v_of = [&](int j) { return v_base + (resident ? j : 0) * kTcChunkBytes; };
+
+  if (tid == 0) {
+    cxs::mbar_init(tma_bar, 1);
+    cxs::mbar_init(mma_bar, 1);
+    cxs::fence_mbar_init();
+    if (chunks > 0) {
+      const int first = resident ? chunks : 1;
+      uint32_t bytes = 0;
+      for (int j = 0; j < first; ++j) bytes += 2 * tiles_of(j) * kTcTileBytes;
+      cxs::mbar_expect_tx(tma_bar, bytes);
+      for (int j = 0; j < first; ++j) {
+        load_half(j, k_of(j), 0);
+        load_half(j, v_of(j), 64);
+      }
+    }
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     cxs::smem_addr(tmem_slot)),
+                 "r"(kTcTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  for (int i = tid; i < kTcRows * score_len; i += kTcThreads) scores[i] = 0.f;
+  // Row m of Q (pre-scaled by 1/8 and rounded to bf16); this thread writes
+  // 16-byte chunks 2 cq and 2 cq + 1 of it.
+  const int ql = m >> 4, g = m & 15, q = q0 + ql;
+  const bool row_ok = q < a.Q;
+  const int pos = row_ok ? a.positions[q] : -1;
+  const int nc = pos >= 0 ? min((pos + 1) / a.BS, C) : 0;
+  const long long qrow = ((long long)q * H + h) * cxs::kGroups + g;  // [Q, H, 16] row index
+#pragma unroll
+  for (int c = 2 * cq; c < 2 * cq + 2; ++c) {
+    uint4 out = make_uint4(0, 0, 0, 0);
+    if (row_ok) {
+      const uint4 in = reinterpret_cast<const uint4*>(a.query + qrow * cxs::kDim)[c];
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(&in);
+      uint32_t* o = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = cxs::unpack_bf16(w[e]);
+        o[e] = cxs::pack_bf16(f.x * 0.125f, f.y * 0.125f);
+      }
+    }
+    *reinterpret_cast<uint4*>(q_tile + tc::sw128_chunk(m, c)) = out;
+  }
+  cxs::fence_proxy_async_shared();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_off = (uint32_t)(32 * lg) << 16;
+  const uint32_t s_col = tmem, o_col = tmem + kTcChunk;
+  const uint32_t s_addr = s_col + lane_off, o_addr = o_col + lane_off;
+  const uint32_t q_addr = cxs::smem_addr(q_tile), p_addr = cxs::smem_addr(p_tile);
+  const long long spin = 1ll << 31;
+  uint32_t tph = 0, mph = 0;
+  bool ok = true;
+
+  // Every thread waits; the CTA then agrees on the outcome, so a timeout
+  // (a broken launch: these copies read device memory only) leaves all
+  // threads on the same path.
+  auto wait_tma = [&]() {
+    bool done = ok && tc::bounded_wait(tma_bar, tph, spin, a.error, cxs::kErrCopyTimeout);
+    tph ^= 1;
+    ok = __syncthreads_and(done);
+  };
+  auto wait_mma = [&]() {
+    bool done = ok && tc::bounded_wait(mma_bar, mph, spin, a.error, cxs::kErrCopyTimeout);
+    mph ^= 1;
+    ok = __syncthreads_and(done);
+    tc::fence_after();
+  };
+  auto mma_scores = [&](int j) {  // S = Q . K_j^T, N = 64 x tiles
+    if (tid == 0) {
+      tc::fence_after();
+      const uint32_t ka = cxs::smem_addr(k_of(j));
+      const uint32_t id = tc::idesc_bf16(128, 64 * tiles_of(j), 0, 0);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        tc::mma(s_col, tc::desc_sw128(q_addr + 32 * k, 16, 1024),
+                tc::desc_sw128(ka + 32 * k, 16, 1024), id, k);
+      tc::commit(mma_bar);
+    }
+    wait_mma();
+  };
+  auto cta_sync = [&]() {
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+  };
+
+  // Pass 1: per-row max and normaliser over every chunk.
+  float m_run = -INFINITY, l_run = 0.f;
+  for (int j = 0; j < chunks && ok; ++j) {
+    if (j > 0 && !resident) {
+      if (tid == 0) {
+        cxs::mbar_expect_tx(tma_bar, tiles_of(j) * kTcTileBytes);
+        load_half(j, k_base, 0);
+      }
+    }
+    if (j == 0 || !resident) wait_tma();
+    if (!ok) break;
+    mma_scores(j);
+    // This warp's column groups (32 columns each) of the chunk: 2 cq, 2 cq + 1.
+    const bool mine = cq < tiles_of(j);
+    const int col0 = kTcChunk * j + 64 * cq;
+    float v0[32], v1[32];
+    if (mine) {  // warp-uniform
+      tc::ld32(s_addr + 64 * cq, v0);
+      tc::ld32(s_addr + 64 * cq + 32, v1);
+    }
+    float mt = -INFINITY;
+    if (mine) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (col0 + i < nc) mt = fmaxf(mt, v0[i]);
+        if (col0 + 32 + i < nc) mt = fmaxf(mt, v1[i]);
+      }
+    }
+    red_max[cq * 128 + m] = mt;
+    cta_sync();  // every thread has read S (the next chunk overwrites it) and posted its max
+    const float m_new = fmaxf(m_run, fmaxf(fmaxf(red_max[m], red_max[128 + m]),
+                                           fmaxf(red_max[256 + m], red_max[384 + m])));
+    const float off = m_new == -INFINITY ? 0.f : m_new * tc::kLog2e;
+    float sum = 0.f;
+    if (mine) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (col0 + i < nc) sum += tc::ex2(fmaf(v0[i], tc::kLog2e, -off));
+        if (col0 + 32 + i < nc) sum += tc::ex2(fmaf(v1[i], tc::kLog2e, -off));
+      }
+    }
+    red_sum[cq * 128 + m] = sum;
+    __syncthreads();
+    if (m_new != -INFINITY) {
+      const float total = (red_sum[m] + red_sum[128 + m]) + (red_sum[256 + m] + red_sum[384 + m]);
+      l_run = (m_run == -INFINITY ? 0.f : l_run * tc::ex2((m_run - m_new) * tc::kLog2e)) + total;
+      m_run = m_new;
+    }
+    __syncthreads();  // red_max / red_sum are reused by the next chunk
+  }
+
+  // Pass 2: probabilities -> P . V and the per-block scores.
+  const float offset = m_run == -INFINITY ? 0.f : m_run * tc::kLog2e;
+  const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+  float* my_scores = scores + ql * score_len;
+  for (int j = 0; j < chunks && ok; ++j) {
+    if (chunks > 1) {
+      if (!resident) {
+        if (tid == 0) {
+          cxs::mbar_expect_tx(tma_bar, 2 * tiles_of(j) * kTcTileBytes);
+          load_half(j, k_base, 0);
+          load_half(j, v_base, 64);
+        }
+        wait_tma();
+        if (!ok) break;
+      }
+      mma_scores(j);
+    }
+    if (cq < tiles_of(j)) {  // warp-uniform
+      uint8_t* sub = p_tile + cq * (128 * 128);
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const int col0 = kTcChunk * j + 64 * cq + 32 * half;
+        float v[32];
+        tc::ld32(s_addr + 64 * cq + 32 * half, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          v[i] = col0 + i < nc ? tc::ex2(fmaf(v[i], tc::kLog2e, -offset)) : 0.f;
+        // P (bf16): 16-byte chunks 4 half .. 4 half + 3 of row m of sub-tile cq.
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint4 chunk = make_uint4(cxs::pack_bf16(v[8 * k + 0], v[8 * k + 1]),
+                                         cxs::pack_bf16(v[8 * k + 2], v[8 * k + 3]),
+                                         cxs::pack_bf16(v[8 * k + 4], v[8 * k + 5]),
+                                         cxs::pack_bf16(v[8 * k + 6], v[8 * k + 7]));
+          *reinterpret_cast<uint4*>(sub + tc::sw128_chunk(m, 4 * half + k)) = chunk;
+        }
+        // Normalised probabilities summed over the row's 16 heads: a
+        // reduce-scatter across lanes (xor 8, 4, 2, 1) leaves lane l of the
+        // half-warp with columns 2 (l % 16) and 2 (l % 16) + 1 of the group.
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= inv_l;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const bool up = lane & 8;
+          const float send = up ? v[i] : v[16 + i];
+          v[i] = (up ? v[16 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const bool up = lane & 4;
+          const float send = up ? v[i] : v[8 + i];
+          v[i] = (up ? v[8 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 4);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const bool up = lane & 2;
+          const float send = up ? v[i] : v[4 + i];
+          v[i] = (up ? v[4 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 2);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const bool up = lane & 1;
+          const float send = up ? v[i] : v[2 + i];
+          v[i] = (up ? v[2 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 1);
+        }
+        const int col = col0 + 2 * g;
+        if (col < C) my_scores[col] = v[0];
+        if (col + 1 < C) my_scores[col + 1] = v[1];
+      }
+    }
+    cxs::fence_proxy_async_shared();
+    cta_sync();
+    if (tid == 0) {
+      const uint32_t id = tc::idesc_bf16(128, 64, 0, 1);
+      const uint32_t v_addr = cxs::smem_addr(v_of(j));
+      for (int kk = 0; kk < 4 * tiles_of(j); ++kk)
+        tc::mma(o_col, tc::desc_sw128(p_addr + (kk >> 2) * (128 * 128) + 32 * (kk & 3), 16, 1024),
+                tc::desc_sw128(v_addr + (kk >> 2) * kTcTileBytes + 2048 * (kk & 3), 16, 1024), id,
+                j > 0 || kk > 0);
+      tc::commit(mma_bar);
+    }
+    wait_mma();
+  }
+
+  // Compressed-branch output: O / normaliser, bf16; this thread writes dims
+  // 16 cq .. 16 cq + 15 of row m.
+  if (row_ok) {
+    uint4* dst = reinterpret_cast<uint4*>(a.out + qrow * cxs::kDim + 16 * cq);
+    dst[0] = make_uint4(0, 0, 0, 0);
+    dst[1] = make_uint4(0, 0, 0, 0);
+  }
+  if (chunks > 0 && ok) {
+    float o[16];
+    tc::ld16(o_addr + 16 * cq, o);
+    if (row_ok) {
+      uint4* dst = reinterpret_cast<uint4*>(a.out + qrow * cxs::kDim + 16 * cq);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        uint32_t r[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          r[e] = cxs::pack_bf16(l_run > 0.f ? o[8 * k + 2 * e] / l_run : 0.f,
+                                l_run > 0.f ? o[8 * k + 2 * e + 1] / l_run : 0.f);
+        dst[k] = make_uint4(r[0], r[1], r[2], r[3]);
+      }
+    }
+  }
+  __syncthreads();
+  if (a.scores) {
+    for (int r = 0; r < kTcRows; ++r) {
+      if (q0 + r >= a.Q) break;
+      float* srow = a.scores + ((long long)(q0 + r) * H + h) * C;
+      for (int i = tid; i < C; i += kTcThreads) srow[i] = scores[r * score_len + i];
+    }
+    __syncthreads();
+  }
+  // Top-n, warp r for row r: the current block first, then earlier blocks by
+  // (score descending, block ascending). Lane l owns candidates l, l + 32, ...
+  // and keeps its best key; each pick is two warp reductions (max key, then
+  // min block id among the lanes holding it) and one rescan by the owner.
+  if (warp < kTcRows && q0 + warp < a.Q) {
+    const int qq = q0 + warp;
+    const int p = a.positions[qq];
+    const int current = p >= 0 ? p / a.BS : -1;
+    const int limit = min(current, score_len);
+    float* sc = scores + warp * score_len;
+    int32_t* brow = a.blocks + ((long long)qq * H + h) * a.width;
+    if (lane == 0) brow[0] = current >= 0 ? current : -1;
+    uint32_t best = 0, best_idx = 0xffffffffu;
+    auto rescan = [&]() {
+      best = 0;
+      best_idx = 0xffffffffu;
+      for (int i = lane; i < limit; i += 32) {
+        const uint32_t key = topn_key(sc[i]);
+        if (key > best) {
+          best = key;
+          best_idx = i;
+        }
+      }
+    };
+    rescan();
+    for (int k = 1; k < a.width; ++k) {
+      const uint32_t top = __reduce_max_sync(0xffffffffu, best);
+      const uint32_t idx = __reduce_min_sync(0xffffffffu, best == top ? best_idx : 0xffffffffu);
+      if (lane == 0) brow[k] = top ? (int32_t)idx : -1;
+      if (top && (int)(idx & 31) == lane) {
+        sc[idx] = -1.f;  // taken
+        rescan();
+      }
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTcTmemCols));
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -239,8 +625,8 @@ extern "C" int cxs_compressed_select(const void* query, const void* compressed, 
     return set_error(CXS_ERR_INVALID, "invalid compressed-select geometry");
   if (!query || !out || !blocks || !positions || (summaries > 0 && !compressed))
     return set_error(CXS_ERR_INVALID, "null compressed-select argument");
-  if (((uintptr_t)compressed & 15) || ((uintptr_t)query & 15) || ((uintptr_t)out & 3))
-    return set_error(CXS_ERR_INVALID, "query/compressed must be 16-byte aligned");
+  if (((uintptr_t)compressed & 15) || ((uintptr_t)query & 15) || ((uintptr_t)out & 15))
+    return set_error(CXS_ERR_INVALID, "query/compressed/out must be 16-byte aligned");
   long long blocks_total = (total + block_size - 1) / block_size;
   int width = (int)(count < blocks_total ? count : blocks_total);
   if (summaries > (1 << 20)) return set_error(CXS_ERR_CAPACITY, "too many summaries");
@@ -272,18 +658,38 @@ extern "C" int cxs_compressed_select(const void* query, const void* compressed, 
   a.out = (__nv_bfloat16*)out;
   a.blocks = blocks;
   a.scores = scores;
-  int* error_word = nullptr;
-  CXS_CUDA(cudaGetSymbolAddress((void**)&error_word, g_select_error));
-  a.error = error_word;
+  int device = 0;
+  CXS_CUDA(cudaGetDevice(&device));
+  if (device < 0 || device >= kMaxDevices)
+    return set_error(CXS_ERR_UNSUPPORTED, "device index %d beyond %d", device, kMaxDevices);
+  if (!g_select_ready[device]) {
+    // Once per device: the error sink's device address and the shared-memory
+    // opt-in for both kernels (up to the per-block maximum).
+    CXS_CUDA(cudaGetSymbolAddress((void**)&g_select_error_address[device], g_select_error));
+    CXS_CUDA(cudaFuncSetAttribute(compressed_select_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+    CXS_CUDA(cudaFuncSetAttribute(compressed_select_tc_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+    g_select_ready[device] = true;
+  }
+  a.error = g_select_error_address[device];
   long long longest = summaries > blocks_total ? summaries : blocks_total;
   if (longest > (1 << 20)) return set_error(CXS_ERR_CAPACITY, "too many blocks");
   int score_len = (int)((longest + 3) & ~3ll);
   a.score_len = score_len;
+  int chunks = (summaries + kTcChunk - 1) / kTcChunk;
+  int kres = chunks <= kTcMaxResident ? (chunks > 0 ? chunks : 1) : 1;
+  if (kres > 1 && tc_smem_bytes(kres, score_len) > (size_t)kMaxSmem) kres = 1;
+  size_t tc_smem = tc_smem_bytes(kres, score_len);
+  if (score_len <= kTcMaxScores && tc_smem <= (size_t)kMaxSmem) {
+    int grid = ((queries + kTcRows - 1) / kTcRows) * heads;
+    compressed_select_tc_kernel<<<grid, kTcThreads, tc_smem, (cudaStream_t)stream>>>(map, a, kres);
+    CXS_LAUNCH_CHECK("compressed_select_tc_kernel");
+    return CXS_OK;
+  }
   size_t smem = 1024 + (size_t)kWarps * 2 * kTileBytes + (size_t)score_len * 4 +
                 (size_t)kWarps * (32 + 16 * 64) * 4 + kWarps * 8;
-  if (smem > 227 * 1024) return set_error(CXS_ERR_CAPACITY, "too many summaries for one warp");
-  CXS_CUDA(cudaFuncSetAttribute(compressed_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)smem));
+  if (smem > (size_t)kMaxSmem) return set_error(CXS_ERR_CAPACITY, "too many summaries for one warp");
   int rows = queries * heads;
   compressed_select_kernel<<<rows, kWarps * 32, smem, (cudaStream_t)stream>>>(
       map, a);

@@ -77,3 +77,29 @@ def test_block_summaries_match_mean_pooling(cuda):
     out = ops.block_summaries(values.cuda(), 16)
     expected = values[:192].reshape(-1, 16, 2, 128).float().mean(1).bfloat16()
     torch.testing.assert_close(out.cpu().float(), expected.float(), rtol=0.01, atol=0.01)
+
+
+@pytest.mark.parametrize("summaries,bs", [(260, 64), (300, 16), (700, 16), (2100, 16)])
+def test_long_histories_match_reference(cuda, summaries, bs):
+    """Summary counts past one 256-record chunk: two resident K chunks (260,
+    300), K reloaded per chunk and pass (700), and the per-row kernel for
+    more blocks than the shared-memory score table holds (2100)."""
+    g = torch.Generator().manual_seed(summaries)
+    heads, count = 2, 16
+    total = summaries * bs + bs // 2
+    positions = torch.cat([torch.randint(0, total, (16,), generator=g),
+                           torch.tensor([total - 1, bs * 5 - 1, 0])]).to(torch.int32)
+    query = torch.randn(len(positions), heads, 16, 64, generator=g).bfloat16()
+    key = torch.randn(summaries, heads, 64, generator=g).bfloat16()
+    value = torch.randn(summaries, heads, 64, generator=g).bfloat16()
+    compressed = torch.cat((key, value), -1).cuda()
+    scores = torch.empty((len(query), heads, summaries), dtype=torch.float32, device="cuda")
+    out, blocks = ops.compressed_attention_select(query.cuda(), compressed, positions.cuda(),
+                                                  total, bs, count, scores=scores)
+    torch.cuda.synchronize()
+    ref_out, _, ref_scores = A.compressed_attention_select(
+        query.float(), key.float(), value.float(), positions.long(), total, bs, count)
+    torch.testing.assert_close(out.cpu().float(), ref_out, rtol=0.03, atol=0.03)
+    torch.testing.assert_close(scores.cpu(), ref_scores, rtol=1e-4, atol=1e-5)
+    exact = A.topn_from_scores(scores.cpu(), positions.long(), bs, count, total)
+    assert torch.equal(blocks.cpu().long(), exact)
