@@ -82,7 +82,7 @@ class NSAExtendModel:
 
     def __init__(self, cfg=None, *, device="cuda", seed=0, max_users=1, max_history=16384,
                  hot_policy="frequency", read_order="consumption_depth",
-                 cross_query_dedup=True, pool_regions=1, chunk=1024):
+                 cross_query_dedup=True, pool_regions=1, chunk=1024, workspaces=None):
         self.cfg = cfg = cfg or NSAConfig()
         self.device = torch.device(device)
         self.max_history, self.chunk = max_history, chunk
@@ -112,8 +112,9 @@ class NSAExtendModel:
                                    topk=min(cfg.hot, 256), dim=128)
         self.transport = GRSelectedTransport(
             self.cache, read_order=read_order, cross_query_dedup=cross_query_dedup,
-            hot_policy=hot_policy, capacity=cfg.layers + 4, async_hot=True)
-        self.fast = None
+            hot_policy=hot_policy, capacity=workspaces or cfg.layers + 4, async_hot=True)
+        self.fast = None          # fused-glue buffers of the user being served
+        self.fast_states = {}     # user -> its fused-glue buffers (prepare_fast)
         self.probe, self.probe_counters = None, []
         self.users = {}
         self.counters = []
@@ -240,7 +241,7 @@ class NSAExtendModel:
             layers.append(dict(kept=kept, tail=tail, c_hist=c_hist, new=new,
                                window_buf=window_buf, summaries=summaries, current=current,
                                fetches=fetches, window_start=st.length - kept))
-        self.fast = dict(
+        self.fast = self.fast_states[user] = dict(
             E=E, user=user, layers=layers,
             positions=torch.arange(st.length, st.length + E, device=d, dtype=torch.int32),
             x=torch.empty((E, cfg.hidden), dtype=torch.bfloat16, device=d),
@@ -288,11 +289,16 @@ class NSAExtendModel:
         _lib.check(lib.cxs_silu_mul(gate_up.data_ptr(), E, cfg.ffn, f["mlp"].data_ptr(), stream))
         return torch.addmm(hidden, f["mlp"], w["down"].t())
 
-    def extend_fast(self, token_ids, hidden=None):
+    def extend_fast(self, token_ids, hidden=None, user=None):
         """Extend step through the fused glue (after ``prepare_fast``).
 
         ``hidden`` optionally replaces the token embeddings (synthetic
-        candidate hidden states)."""
+        candidate hidden states); ``user`` selects whose prepared buffers
+        serve the step (default: the most recently prepared user)."""
+        if user is not None:
+            if user not in self.fast_states:
+                raise ValueError(f"prepare_fast(..., user={user!r}) first")
+            self.fast = self.fast_states[user]
         if self.fast is None or len(token_ids) != self.fast["E"]:
             raise ValueError("prepare_fast(len(token_ids)) first")
         if hidden is None:
@@ -307,7 +313,11 @@ class NSAExtendModel:
         return out
 
     def capture_extend(self, extend_tokens, user="user", warmup=2):
-        """Capture one extend forward in a CUDA graph with static input/output."""
+        """Capture one extend forward of ``user`` in a CUDA graph with static
+        input/output. Graphs of several users may be replayed one after
+        another on one stream: they share the transport's per-layer
+        workspaces, which the transport keeps (pins) once a captured graph
+        holds them."""
         self.prepare_fast(extend_tokens, user)
         static_ids = torch.zeros(extend_tokens, dtype=torch.int64, device=self.device)
         stream = torch.cuda.Stream(self.device)
@@ -328,6 +338,9 @@ class NSAExtendModel:
         self.captured_launches = _lib.lib().cxs_launch_count() - before
         graph_counters = list(self.counters)
         self.counters.clear()
+        # The graph reads static_ids and writes static_out in place: keep both
+        # alive for as long as the graph is, whatever the caller keeps.
+        graph.static_buffers = (static_ids, static_out)
         return graph, static_ids, static_out, graph_counters
 
     def compare_private_plan(self, token_ids, hidden=None):

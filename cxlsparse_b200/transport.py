@@ -177,9 +177,14 @@ class GRSelectedTransport:
         resident = sum(w["allocated_bytes"] for w in self.workspaces.values())
         while self.workspaces and (len(self.workspaces) >= self.capacity
                                    or resident + estimate > self.workspace_budget):
+            # Least recently used first; a workspace bound into a caller's
+            # captured graph stays (its buffers are baked into the graph).
+            victim = next((k for k, v in self.workspaces.items() if not v.get("pinned")), None)
+            if victim is None:
+                raise GRWorkspaceLimit("every cached workspace is bound into a captured graph")
             if self.submitted:
                 self.last_done.synchronize()
-            _, old = self.workspaces.popitem(last=False)
+            old = self.workspaces.pop(victim)
             old.pop("graph", None)
             resident -= old["allocated_bytes"]
             self.workspace_evictions += 1
@@ -313,6 +318,8 @@ class GRSelectedTransport:
         qb = query_bucket(q_count)
         window_shape = (len(window_kv), window) if fused else None
         w = self._workspace(qb, heads, width, fetches, block_size, window_shape, workspace_id)
+        if capturing:
+            w["pinned"] = True  # the caller's graph now holds this workspace's buffers
         # Direct binding: without the transport's own graphs, the kernels read
         # the caller's tensors in place (no staging copies) when they already
         # have the bucket's shape, dtype and layout.
