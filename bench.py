@@ -48,11 +48,15 @@ def parse():
     p.add_argument("--layers", type=int, default=16)
     p.add_argument("--read-order", default="consumption_depth")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", default="extend", choices=("extend", "dedup", "serving"),
+    p.add_argument("--workload", default="extend",
+                   choices=("extend", "dedup", "serving", "headsplit"),
                    help="dedup: BASELINE configs[2] stress (16 candidates x 128 tokens, "
                         "all history cold); serving: BASELINE configs[3] (users per GPU "
-                        "with jittered ~32K histories, 4 queries x E per user); each "
-                        "prints its own JSON line")
+                        "with jittered ~32K histories, 4 queries x E per user); "
+                        "headsplit: BASELINE configs[4] (the KV heads of each user split "
+                        "over a GPU pair, H=128K, 8 queries x E per user); each prints "
+                        "its own JSON line")
+    p.add_argument("--users-per-pair", type=int, default=4)
     p.add_argument("--users-per-gpu", type=int, default=8)
     p.add_argument("--queries", type=int, default=4)
     p.add_argument("--jitter", type=int, default=1000)
@@ -63,7 +67,7 @@ def parse():
                         "'profile_step' and exit (for ncu --nvtx-include profile_step/)")
     args = p.parse_args()
     if args.history is None:
-        args.history = 32768 if args.workload == "serving" else 16384
+        args.history = {"serving": 32768, "headsplit": 131072}.get(args.workload, 16384)
     return args
 
 
@@ -566,17 +570,155 @@ def _reserve_stdout():
     sys.stdout = json_out
 
 
+def run_headsplit(args):
+    """ranks (2p, 2p + 1) form pair p; rank 2p + i owns KV head i
+    of every layer for the pair's users (its 16 query heads, pool slice,
+    planner, fetch and attention) and the pair all-gathers the attention
+    outputs once per layer before o_proj. Users are round-robin over pairs;
+    each gets H history tokens and `queries` candidates of E tokens packed
+    into one suffix. On one GPU the same user set runs with both heads local
+    (the reference point for the split). A step serves every user of the pair
+    once (one captured graph per user, collectives inside)."""
+    import torch
+
+    from cxlsparse_b200.model import NSAConfig, NSAExtendModel
+    from cxlsparse_b200.sharding import gather_scores, head_exchange, head_pair_groups
+    from cxlsparse_b200.sharding import users_for_rank
+
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    world, rank, local = dist_setup(torch)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    group, shard, shards, pair, pairs = head_pair_groups(world)
+    cfg = NSAConfig(layers=args.layers)
+    users_total = args.users_per_pair * pairs
+    mine = users_for_rank(list(range(users_total)), pair, pairs)
+    suffix = args.queries * args.extend
+    model = NSAExtendModel(cfg, device=device, seed=0, max_users=len(mine),
+                           max_history=args.history + suffix, read_order=args.read_order,
+                           workspaces=cfg.layers * len(mine) + 4, head_shard=(shard, shards),
+                           exchange=head_exchange(group, shards) if shards > 1 else None)
+    t0 = time.perf_counter()
+    candidates = {}
+    for u in mine:
+        g = torch.Generator().manual_seed(4000 + u)
+        model.prefill(torch.randint(0, cfg.vocab, (args.history,), generator=g).to(device),
+                      user=f"u{u}")
+        candidates[u] = torch.randint(0, cfg.vocab, (suffix,), generator=g)
+    prefill_s = time.perf_counter() - t0
+    captured, launches = {}, 0
+    for u in mine:
+        graph, static_ids, static_out, counters = model.capture_extend(suffix, user=f"u{u}")
+        static_ids.copy_(candidates[u].to(device))
+        captured[u] = (graph, static_ids, static_out, counters)
+        launches += model.captured_launches
+    pcie = measure_pcie(torch, device)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    def serve_all():
+        for u in mine:
+            captured[u][0].replay()
+
+    for _ in range(args.warmup):
+        serve_all()
+    serve_all()
+    torch.cuda.synchronize(device)
+    stats = torch.stack([c.statistics for u in mine for c in captured[u][3]]).cpu()
+    errors = [int(c.device_error.item()) for u in mine for c in captured[u][3]]
+    if any(errors) or stats[..., 6].any():
+        raise RuntimeError(f"device plan/attend errors: {errors}")
+    fetched = int(stats[..., 3].sum()) * 256
+    sampler = ClockSampler(local)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        serve_all()
+    end.record(stream)
+    barrier()
+    device_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    host_ids = {u: candidates[u].pin_memory() for u in mine}
+    local_out = torch.empty((len(mine), cfg.hidden), dtype=torch.bfloat16, device=device)
+    host_out = torch.empty((world, len(mine), cfg.hidden), dtype=torch.bfloat16,
+                           pin_memory=True)
+    barrier()
+    start.record(stream)
+    for _ in range(args.steps):
+        for i, u in enumerate(mine):
+            graph, static_ids, static_out, _ = captured[u]
+            static_ids.copy_(host_ids[u], non_blocking=True)
+            graph.replay()
+            local_out[i].copy_(static_out[-1])
+        gathered = gather_scores(local_out) if dist is not None else local_out[None]
+        host_out.copy_(gathered, non_blocking=True)
+    end.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    clocks = sampler.stop()
+    if rank == 0:
+        tokens = users_total * suffix
+        print(json.dumps({
+            "metric": METRIC, "workload": "headsplit", "value": tokens / (device_ms / 1e3),
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": device_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded random token ids per user, random N(0,0.02) weights, "
+                    "history KV computed by the model (chunked prefill)",
+            "config": {"workload": f"BASELINE configs[4]: KV heads split over GPU pairs, "
+                                   f"{args.users_per_pair} users per pair, H={args.history}, "
+                                   f"{args.queries} queries x E={args.extend} per user",
+                       "users": users_total, "pairs": pairs, "kv_heads_per_gpu": model.kv_local,
+                       "layers": args.layers, "block_size": 64, "top_n": 16, "window": 512,
+                       "hot": "256 tokens per (layer, kv head), reference frequency policy",
+                       "exchange": "NCCL all-gather of the [E, 16, 64] attention output per "
+                                   "layer within the pair (inside the captured graph)",
+                       "parallelism": f"{pairs} pair(s) x 2 KV-head shards" if shards > 1
+                       else "1 GPU, both KV heads local"},
+            "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s",
+                    "h2d_bytes_per_step": len(mine) * suffix * 8,
+                    "d2h_bytes_per_step": world * len(mine) * cfg.hidden * 2},
+            "gpu_launches": launches * args.steps,
+            "fetch": {"bytes_per_step_rank0": fetched,
+                      "gb_s_over_step_rank0": fetched / (device_ms / 1e3) / 1e9,
+                      "pcie_h2d_peak_gb_s": pcie},
+            "clocks": clocks, "prefill_s_rank0": prefill_s,
+        }))
+    if dist is not None:
+        captured.clear()
+        dist.barrier()
+        dist.destroy_process_group()
+    model.close()
+
+
 def main():
     _reserve_stdout()
     args = parse()
     if args.workload == "dedup":
         run_dedup(args)
         return
-    if args.workload == "serving":
+    if args.workload in ("serving", "headsplit"):
         if args.impl == "reference":
             run_reference(args)
-        else:
+        elif args.workload == "serving":
             run_serving(args)
+        else:
+            run_headsplit(args)
         return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -41,7 +41,7 @@ class PlanGeometry(ctypes.Structure):
     _fields_ = [(name, c_i32) for name in (
         "queries", "heads", "width", "block_size", "map_blocks", "per_head",
         "sort_extent", "hot", "max_history", "regions", "page_size",
-        "consumer_ctas", "read_order", "private_plan")] + [("pool_tokens", c_i64)]
+        "consumer_ctas", "read_order", "private_plan", "launch_mode")] + [("pool_tokens", c_i64)]
 
 
 PLAN_BUFFER_FIELDS = (

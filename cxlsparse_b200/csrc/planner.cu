@@ -25,10 +25,37 @@ constexpr int kMaxPhysical = 16384;     // single-CTA publish sort limit
 constexpr int kMaxHot = 4096;           // shared-memory hot hash / hot sort limit
 
 struct Geo {
-  int Q, H, W, BS, MAP, CAP, SORT, HOT, MAXH, REGIONS, PAGE, CONSUMERS, ORDER, PRIVATE;
+  int Q, H, W, BS, MAP, CAP, SORT, HOT, MAXH, REGIONS, PAGE, CONSUMERS, ORDER, PRIVATE, MODE;
   int HASH, P, R;
+  int PAGE_SHIFT, REGION_SHIFT;  // log2 of PAGE / REGIONS when powers of two, else -1
   long long POOL;
 };
+
+// Backing-pool address of token slot `source` (>= 0): page source / PAGE,
+// pages striped round-robin over the regions (mempool/cxl.py:110-113).
+// Shifts and masks replace the 64-bit division when PAGE / REGIONS are
+// powers of two; the values are the same.
+__device__ __forceinline__ long long pool_address(const Geo& g, const int64_t* bases,
+                                                  long long source, int* region_out) {
+  long long page, offset, local_page;
+  int region;
+  if (g.PAGE_SHIFT >= 0) {
+    page = source >> g.PAGE_SHIFT;
+    offset = source & (g.PAGE - 1);
+  } else {
+    page = source / g.PAGE;
+    offset = source % g.PAGE;
+  }
+  if (g.REGION_SHIFT >= 0) {
+    region = (int)(page & (g.REGIONS - 1));
+    local_page = page >> g.REGION_SHIFT;
+  } else {
+    region = (int)(page % g.REGIONS);
+    local_page = page / g.REGIONS;
+  }
+  *region_out = region;
+  return bases[region] + (local_page * g.PAGE + offset) * kTokenBytes;
+}
 
 __device__ __forceinline__ bool occurrence_valid(int block, int pos, int total, const Geo& g) {
   return pos >= 0 && block >= 0 && block < g.MAP && (long long)block * g.BS <= pos &&
@@ -258,10 +285,8 @@ __global__ void addresses_kernel(Geo g, cxs_plan_buffers b) {
                      : pointer + (token - old) * kTokenBytes;
     long long address = hbm;
     if (safe) {
-      long long page = source / g.PAGE;
-      int region = (int)(page % g.REGIONS);
-      long long local = (page / g.REGIONS) * g.PAGE + source % g.PAGE;
-      address = b.bases[region] + local * kTokenBytes;
+      int region;
+      address = pool_address(g, b.bases, source, &region);
       if (region < 8) region_mask_counts[region] += 1;
       else atomicAdd(&b.region_counts[region], 1);
     }
@@ -749,6 +774,530 @@ __global__ void commit_kernel(Geo g, cxs_plan_buffers b, const uint4* __restrict
   }
 }
 
+// -------------------------------------------------------------- fused plan ---
+// The deduplicating plan in one launch of a single thread-block cluster
+// (16 CTAs of 512 threads where the GPU allows, else 8), its phases
+// separated by the cluster's hardware barrier instead of kernel boundaries.
+// Same arrays, same values as the kernels above:
+//   0 reset                                   (reset_kernel)
+//   1 dedup insert                            (insert_kernel)
+//   2 compact ranks + references: every CTA rebuilds the per-head bitmap of
+//     inserted blocks and its word prefix counts in shared memory, so a
+//     block's compact index (its rank among the head's keys) is known without
+//     waiting for the mapping; CTA h writes head h's active_keys / mapping
+//                                             (compact_kernel, references_kernel)
+//   3 source resolution, missing count        (addresses_kernel)
+//   4 occurrence rows, consumption depth: a row's depth recounts the valid
+//     occurrences of the earlier rows of its consumer (at most 8 of them),
+//     so both fit one phase; longer consumer chains take two
+//                                             (occurrences_kernel, depth_kernel)
+//   5 near consumers (shared order only)      (near_kernel)
+//   6 IOIDs / Ranks: each missing block's rank is the number of missing
+//     blocks with a smaller unique key, counted against all keys staged in
+//     shared memory                           (publish_kernel)
+constexpr int kFusedThreads = 512;
+constexpr int kFusedWarps = kFusedThreads / 32;
+constexpr int kFusedMaxPhysical = 8192;
+constexpr int kFusedMaxMap = 65536;
+constexpr int kFusedMaxChain = 8;  // earlier rows per consumer recounted in phase 4
+constexpr int kFusedMaxHeads = 8;
+
+// Hardware barrier over the CTAs of the cluster, ordering their memory
+// accesses (shared and global) at cluster scope.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Distributed shared memory: the address of the same shared-memory offset
+// in CTA `cta` of the cluster, a fire-and-forget OR into it and a load.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local, uint32_t cta) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(cta));
+  return remote;
+}
+__device__ __forceinline__ void cluster_or(uint32_t remote, uint32_t value) {
+  asm volatile("red.shared::cluster.or.b32 [%0], %1;" ::"r"(remote), "r"(value) : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ld(uint32_t remote) {
+  uint32_t value;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(value) : "r"(remote) : "memory");
+  return value;
+}
+
+// Valid, mapped occurrences of row r (warp-collective): the occurrence-row
+// length of occurrences_kernel for a deduplicating plan; compact(h, block)
+// gives the compact index or -1.
+template <typename Compact>
+__device__ __forceinline__ int row_occurrences(const Geo& g, const cxs_plan_buffers& b, int r,
+                                               int lane, Compact compact, int32_t* out) {
+  const int q = r / g.H, h = r % g.H;
+  const int pos = b.positions[q];
+  const bool head_ok = b.stats[h * 7 + 6] == 0;
+  int count = 0;
+  for (int i0 = 0; i0 < g.W; i0 += 32) {
+    const int i = i0 + lane;
+    bool valid = false;
+    int physical = 0;
+    if (i < g.W && head_ok) {
+      const int block = b.blocks[(long long)r * g.W + i];
+      valid = pos >= 0 && block >= 0 && block < g.MAP && (long long)block * g.BS <= pos;
+      if (valid) {
+        const int c = compact(h, block);
+        valid = c >= 0 && c < g.CAP;
+        physical = h * g.CAP + c;
+      }
+    }
+    const unsigned mask = __ballot_sync(0xffffffffu, valid);
+    if (out && valid) out[count + __popc(mask & ((1u << lane) - 1))] = physical;
+    count += __popc(mask);
+  }
+  return count;
+}
+
+__global__ void __launch_bounds__(kFusedThreads, 1)
+    plan_fused_kernel(Geo g, cxs_plan_buffers b, int max_depth, int merged_depth) {
+  extern __shared__ __align__(16) unsigned char fused_mem[];
+  typedef cub::BlockScan<int, kFusedThreads> Scan;
+  __shared__ typename Scan::TempStorage scan;
+  const int ctas = gridDim.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long gtid = (long long)blockIdx.x * kFusedThreads + threadIdx.x;
+  const long long gthreads = (long long)ctas * kFusedThreads;
+  const int gwarp = blockIdx.x * kFusedWarps + warp, gwarps = ctas * kFusedWarps;
+
+  // Per-CTA counters: phases add into shared memory and flush one global
+  // atomic per counter per CTA (the stats words are shared by every block
+  // and row of a head, so direct global atomics would serialise at L2).
+  __shared__ int cta_stats[kFusedMaxHeads * 7];
+  __shared__ int cta_regions[8];
+  __shared__ int cta_missing;
+  auto clear_counters = [&]() {
+    for (int i = threadIdx.x; i < kFusedMaxHeads * 7; i += kFusedThreads) cta_stats[i] = 0;
+    if (threadIdx.x < 8) cta_regions[threadIdx.x] = 0;
+    if (threadIdx.x == 0) cta_missing = 0;
+  };
+  auto flush_counters = [&]() {  // after a __syncthreads
+    for (int i = threadIdx.x; i < g.H * 7; i += kFusedThreads)
+      if (cta_stats[i]) atomicAdd(&b.stats[i], cta_stats[i]);
+    if (threadIdx.x < min(g.REGIONS, 8) && cta_regions[threadIdx.x])
+      atomicAdd(&b.region_counts[threadIdx.x], cta_regions[threadIdx.x]);
+    if (threadIdx.x == 0 && cta_missing) atomicAdd(b.missing, cta_missing);
+  };
+  // CTA h (h < H) keeps head h's claim bitmap at the start of its shared
+  // memory; every CTA reaches it through distributed shared memory.
+  const int words = (g.MAP + 31) / 32;
+  uint32_t* claim = reinterpret_cast<uint32_t*>(fused_mem);
+  unsigned char* scratch = fused_mem + (((size_t)words * 4 + 15) & ~(size_t)15);
+
+  // ---- 0: reset
+  {
+    clear_counters();
+    if ((int)blockIdx.x < g.H)
+      for (int i = threadIdx.x; i < words; i += kFusedThreads) claim[i] = 0;
+    const long long hc = (long long)g.H * g.CAP, hs = (long long)g.H * g.SORT;
+    const long long rw = (long long)g.R * g.W;
+    for (long long i = gtid; i < hc; i += gthreads) {
+      b.required[i] = 0;
+      b.insert_keys[i] = kInt32Max;
+    }
+    for (long long i = gtid; i < hs; i += gthreads) b.frequencies[i] = 0;
+    for (long long i = gtid; i < rw; i += gthreads) b.all_ids[i] = -1;
+    for (long long i = gtid; i < g.R; i += gthreads) b.all_counts[i] = 0;
+    for (long long i = gtid; i < g.P; i += gthreads) {
+      b.ioids[i] = -1;
+      b.ranks[i] = -1;
+      b.first_depth[i] = max_depth;
+      b.near_consumers[i] = 0;
+    }
+    for (long long i = gtid; i < g.H; i += gthreads) b.active_counts[i] = 0;
+    for (long long i = gtid; i < (long long)g.H * 7; i += gthreads) b.stats[i] = 0;
+    for (long long i = gtid; i < g.REGIONS; i += gthreads) b.region_counts[i] = 0;
+    if (gtid == 0) b.missing[0] = 0;
+    // Every mapping entry of a valid selection is rewritten in phase 2 (all
+    // valid blocks are claimed), so only the sentinel is set here.
+    for (long long i = gtid; i < g.H; i += gthreads) b.mapping[i * (g.MAP + 1) + g.MAP] = -2;
+  }
+  cluster_sync();
+
+  // ---- 1: dedup claims: each valid occurrence sets its block's bit in the
+  // head's claim bitmap (CTA h's shared memory); duplicates set it again.
+  for (int r = gwarp; r < g.R; r += gwarps) {
+    const int q = r / g.H, h = r % g.H;
+    const int pos = b.positions[q];
+    const int total = (int)(b.desc[h * 5 + 1] + b.desc[h * 5 + 4]);
+    const uint32_t remote = cluster_map(cxs::smem_addr(claim), h);
+    int errors = 0;
+    for (int i = lane; i < g.W; i += 32) {
+      const int block = b.blocks[(long long)r * g.W + i];
+      if (occurrence_valid(block, pos, total, g))
+        cluster_or(remote + (uint32_t)(block >> 5) * 4, 1u << (block & 31));
+      else if (block >= 0 && pos >= 0)
+        ++errors;
+    }
+    errors = cxs::warp_sum(errors);
+    if (lane == 0 && errors) atomicAdd(&cta_stats[h * 7 + 6], errors);
+  }
+  __syncthreads();
+  flush_counters();
+  __syncthreads();
+  clear_counters();
+  cluster_sync();
+
+  // ---- 2: claim bitmaps copied into every CTA with word prefix counts, so
+  // a block's compact index (its rank among the head's claimed blocks) is
+  // known locally; CTA h publishes head h's compact layout; references.
+  uint32_t* bits = reinterpret_cast<uint32_t*>(scratch);                // [H][words]
+  int* prefix = reinterpret_cast<int*>(bits + (long long)g.H * words);  // [H][words]
+  for (int h = 0; h < g.H; ++h) {
+    const uint32_t remote = cluster_map(cxs::smem_addr(claim), h);
+    for (int i = threadIdx.x; i < words; i += kFusedThreads)
+      bits[h * words + i] = cluster_ld(remote + (uint32_t)i * 4);
+  }
+  __syncthreads();
+  const int per = (words + kFusedThreads - 1) / kFusedThreads;
+  for (int h = 0; h < g.H; ++h) {
+    const int begin = threadIdx.x * per, end = min(words, begin + per);
+    int local = 0;
+    for (int w = begin; w < end; ++w) local += __popc(bits[h * words + w]);
+    int offset;
+    Scan(scan).ExclusiveSum(local, offset);
+    for (int w = begin; w < end; ++w) {
+      prefix[h * words + w] = offset;
+      offset += __popc(bits[h * words + w]);
+    }
+    __syncthreads();
+  }
+  auto rank_of = [&](int h, int block) -> int {
+    const uint32_t word = bits[h * words + (block >> 5)];
+    const uint32_t bit = 1u << (block & 31);
+    if (!(word & bit)) return -1;
+    return prefix[h * words + (block >> 5)] + __popc(word & (bit - 1));
+  };
+  if ((int)blockIdx.x < g.H) {  // CTA h publishes head h's compact layout
+    const int h = blockIdx.x;
+    const int count = prefix[h * words + words - 1] + __popc(bits[h * words + words - 1]);
+    if (threadIdx.x == 0) {
+      b.active_counts[h] = count;
+      if (count > g.CAP) atomicAdd(&b.stats[h * 7 + 6], count - g.CAP);  // no slot left
+    }
+    const int begin = threadIdx.x * per, end = min(words, begin + per);
+    for (int w = begin; w < end; ++w) {
+      uint32_t word = bits[h * words + w];
+      int offset = prefix[h * words + w];
+      while (word) {
+        const int block = w * 32 + __ffs(word) - 1;
+        word &= word - 1;
+        if (offset < g.CAP) {
+          b.active_keys[(long long)h * g.CAP + offset] = block;
+          b.insert_keys[(long long)h * g.CAP + offset] = block;
+          b.mapping[(long long)h * (g.MAP + 1) + block] = offset;
+        } else {
+          b.mapping[(long long)h * (g.MAP + 1) + block] = -2;
+        }
+        ++offset;
+      }
+    }
+    for (int c = min(count, g.CAP) + threadIdx.x; c < g.CAP; c += kFusedThreads)
+      b.active_keys[(long long)h * g.CAP + c] = kInt32Max;
+  }
+  // References, one occurrence per lane (required = causal prefix maximum,
+  // old / local token counts, one frequency-run count per occurrence).
+  for (int r = gwarp; r < g.R; r += gwarps) {
+    const int q = r / g.H, h = r % g.H;
+    const int pos = b.positions[q];
+    const int old = (int)b.desc[h * 5 + 1];
+    const int history = (int)b.desc[h * 5 + 2];
+    const int total = old + (int)b.desc[h * 5 + 4];
+    int old_refs = 0, local_refs = 0;
+    for (int i = lane; i < g.W; i += 32) {
+      const int block = b.blocks[(long long)r * g.W + i];
+      if (!occurrence_valid(block, pos, total, g)) continue;
+      const int compact = rank_of(h, block);
+      if (compact < 0 || compact >= g.CAP) continue;
+      const int start = block * g.BS;
+      const int req = min(g.BS, min(pos + 1, total) - start);
+      atomicMax(&b.required[(long long)h * g.CAP + compact], req);
+      const int olds = min(max(old - start, 0), req);
+      old_refs += olds;
+      local_refs += req - olds;
+      // One count per occurrence at slot (historical - 1) of the block's
+      // frequency run; phase 3 turns the run into per-token frequencies
+      // (token o is counted by every occurrence covering more than o
+      // historical tokens: a suffix sum).
+      const int historical = min(max(history - start, 0), req);
+      if (historical > 0)
+        atomicAdd(&b.frequencies[(long long)h * g.SORT + (long long)compact * g.BS +
+                                 historical - 1], 1);
+    }
+    old_refs = cxs::warp_sum(old_refs);
+    local_refs = cxs::warp_sum(local_refs);
+    if (lane == 0) {
+      if (old_refs) atomicAdd(&cta_stats[h * 7 + 4], old_refs);
+      if (local_refs) atomicAdd(&cta_stats[h * 7 + 5], local_refs);
+    }
+  }
+  __syncthreads();
+  flush_counters();
+  __syncthreads();
+  clear_counters();
+  cluster_sync();
+
+  // ---- 3: source resolution; CTAs split by head, each with its hot hash
+  {
+    const int per_head = ctas / g.H;
+    if ((int)blockIdx.x < per_head * g.H) {
+      const int h = blockIdx.x % g.H, k = blockIdx.x / g.H;
+      int* hkeys = reinterpret_cast<int*>(scratch);
+      int* hvals = hkeys + g.HASH;
+      const int row = (int)b.desc[h * 5];
+      const int old = (int)b.desc[h * 5 + 1];
+      const long long pointer = b.desc[h * 5 + 3];
+      for (int i = threadIdx.x; i < g.HASH; i += kFusedThreads) hkeys[i] = -1;
+      __syncthreads();
+      const int32_t* tags = b.tags + (long long)row * (g.HOT + 1);
+      const int32_t* locs = b.locs + (long long)row * (g.HOT + 1);
+      for (int i = threadIdx.x; i < g.HOT; i += kFusedThreads) {
+        const int token = tags[i];
+        if (token < 0 || token >= old) continue;
+        uint32_t s = hash_slot(token, g.HASH - 1);
+        for (int probe = 0; probe < g.HASH; ++probe) {
+          const int prev = atomicCAS(&hkeys[s], -1, token);
+          if (prev == -1) {
+            hvals[s] = locs[i];
+            break;
+          }
+          if (prev == token) break;  // duplicate tag: keep the first location
+          s = (s + 1) & (g.HASH - 1);
+        }
+      }
+      __syncthreads();
+      const char* hot_data = static_cast<const char*>(b.hot_data);
+      const int count = b.active_counts[h];
+      // Four compact blocks per warp, eight lanes per block; lane `sub` of a
+      // group owns tokens sub, sub + 8, ... and frequency slots
+      // sub * per .. sub * per + per - 1 (per = BS / 8, BS <= 64). Every
+      // load of a block is issued before its first store.
+      const int sub = lane & 7, group = lane >> 3;
+      const int per = g.BS / 8;
+      for (int c0 = (k * kFusedWarps + warp) * 4; c0 < g.CAP;
+           c0 += per_head * kFusedWarps * 4) {
+        const int c = c0 + group;
+        const bool in_range = c < g.CAP;
+        const bool active = in_range && c < count;
+        const long long p = (long long)h * g.CAP + c;
+        int32_t* run = b.frequencies + (long long)h * g.SORT + (long long)c * g.BS;
+        int fv[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) fv[t] = (in_range && t < per) ? run[sub * per + t] : 0;
+        const int block = active ? b.active_keys[p] : -1;
+        const int req = active ? b.required[p] : 0;
+        // Hot lookups and pool-slot loads for this lane's tokens.
+        long long source[8];
+        int location[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int o = sub + 8 * t;
+          const long long token = (long long)block * g.BS + o;
+          const bool valid = active && o < req && t < per;
+          const bool previous = valid && token < old;
+          location[t] = -1;
+          source[t] = -1;
+          if (previous) {
+            uint32_t s = hash_slot((int)token, g.HASH - 1);
+            for (int probe = 0; probe < g.HASH; ++probe) {
+              const int key = hkeys[s];
+              if (key == (int)token) {
+                location[t] = hvals[s];
+                break;
+              }
+              if (key == -1) break;
+              s = (s + 1) & (g.HASH - 1);
+            }
+            if (location[t] < 0 && token < g.MAXH)
+              source[t] = b.host_locs[(long long)row * g.MAXH + token];
+          }
+        }
+        // Frequency run: suffix sums of the per-length counts.
+        {
+          int chunk = 0;
+#pragma unroll
+          for (int t = 0; t < 8; ++t) chunk += fv[t];
+          int after = chunk;  // inclusive suffix over this group's lanes >= sub
+#pragma unroll
+          for (int o = 1; o < 8; o <<= 1) {
+            const int other = __shfl_down_sync(0xffffffffu, after, o, 8);
+            if (sub + o < 8) after += other;
+          }
+          after -= chunk;
+#pragma unroll
+          for (int t = 7; t >= 0; --t) {
+            after += fv[t];
+            if (in_range && t < per) run[sub * per + t] = after;
+          }
+        }
+        unsigned packed = 0;  // n_valid | n_prev << 8 | n_hot << 16 | n_ext << 24
+        int n_err = 0;
+        int region_mask_counts[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int o = sub + 8 * t;
+          if (!in_range || t >= per) continue;
+          const long long token = (long long)block * g.BS + o;
+          const bool valid = active && o < req;
+          const bool previous = valid && token < old;
+          const bool external = previous && location[t] < 0;
+          const bool error = external && (source[t] < 0 || source[t] >= g.POOL);
+          const bool safe = external && !error;
+          long long hbm = 0;
+          if (valid && !external)
+            hbm = previous ? (long long)(hot_data + (long long)location[t] * kTokenBytes)
+                           : pointer + (token - old) * kTokenBytes;
+          long long address = hbm;
+          if (safe) {
+            int region;
+            address = pool_address(g, b.bases, source[t], &region);
+            if (region < 8) region_mask_counts[region] += 1;
+            else atomicAdd(&b.region_counts[region], 1);
+          }
+          const long long idx = p * g.BS + o;
+          b.address[idx] = address;
+          b.hbm[idx] = hbm;
+          b.slots[idx] = safe ? source[t] : -1;
+          packed += (unsigned)valid | ((unsigned)previous << 8) |
+                    ((unsigned)(previous && !external) << 16) | ((unsigned)external << 24);
+          n_err += error;
+        }
+        // Sums over the 8 lanes of the group (every count is at most 64).
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+          packed += __shfl_xor_sync(0xffffffffu, packed, o, 8);
+          n_err += __shfl_xor_sync(0xffffffffu, n_err, o, 8);
+        }
+        const int regions8 = min(g.REGIONS, 8);
+        for (int r = 0; r < regions8; ++r) {
+          int cnt = region_mask_counts[r];
+#pragma unroll
+          for (int o = 1; o < 8; o <<= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o, 8);
+          if (sub == 0 && cnt) atomicAdd(&cta_regions[r], cnt);
+        }
+        if (sub == 0 && in_range) {
+          const int n_valid = packed & 255u, n_prev = (packed >> 8) & 255u;
+          const int n_hot = (packed >> 16) & 255u, n_ext = packed >> 24;
+          b.valid[p] = (active && n_err == 0) ? req : 0;
+          b.starts[p] = active ? block * g.BS : 0;
+          b.flags[p] = n_ext > 0;
+          if (n_ext > 0) atomicAdd(&cta_missing, 1);
+          if (n_valid) atomicAdd(&cta_stats[h * 7 + 0], n_valid);
+          if (n_prev) atomicAdd(&cta_stats[h * 7 + 1], n_prev);
+          if (n_hot) atomicAdd(&cta_stats[h * 7 + 2], n_hot);
+          if (n_ext) atomicAdd(&cta_stats[h * 7 + 3], n_ext);
+          if (n_err) atomicAdd(&cta_stats[h * 7 + 6], n_err);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  flush_counters();
+  cluster_sync();
+
+  // ---- 4: occurrence rows (+ consumption depth)
+  auto mapped = [&](int h, int block) { return b.mapping[(long long)h * (g.MAP + 1) + block]; };
+  const bool by_depth = g.ORDER != CXS_ORDER_PHYSICAL;
+  for (int r = gwarp; r < g.R; r += gwarps) {
+    int32_t* ids = b.all_ids + (long long)r * g.W;
+    const int count = row_occurrences(g, b, r, lane, mapped, ids);
+    const int pos = b.positions[r / g.H];
+    if (lane == 0) {
+      b.all_counts[r] = count;
+      b.row_positions[r] = pos;
+    }
+    if (!by_depth || !merged_depth) continue;
+    int depth = 0;
+    for (int prev = r % g.CONSUMERS; prev < r; prev += g.CONSUMERS)
+      depth += row_occurrences(g, b, prev, lane, mapped, nullptr);
+    if (lane == 0) b.row_depth[r] = depth;
+    __syncwarp();
+    if (pos < 0) continue;
+    for (int col = lane; col < min(g.W, count); col += 32) {
+      const int block = ids[col];
+      if (block >= 0 && block < g.P && b.flags[block]) atomicMin(&b.first_depth[block], depth + col);
+    }
+  }
+  if (by_depth && !merged_depth) {
+    cluster_sync();
+    for (int r = gwarp; r < g.R; r += gwarps) {
+      int depth = 0;
+      for (int prev = r % g.CONSUMERS + lane * g.CONSUMERS; prev < r; prev += 32 * g.CONSUMERS)
+        if (b.row_positions[prev] >= 0) depth += b.all_counts[prev];
+      depth = cxs::warp_sum(depth);
+      if (lane == 0) b.row_depth[r] = depth;
+      if (b.row_positions[r] < 0) continue;
+      const int count = min(g.W, b.all_counts[r]);
+      for (int col = lane; col < count; col += 32) {
+        const int block = b.all_ids[(long long)r * g.W + col];
+        if (block >= 0 && block < g.P && b.flags[block]) atomicMin(&b.first_depth[block], depth + col);
+      }
+    }
+  }
+  cluster_sync();
+
+  // ---- 5: near consumers (shared consumption-depth order)
+  if (g.ORDER == CXS_ORDER_DEPTH_SHARED) {
+    for (int r = gwarp; r < g.R; r += gwarps) {
+      if (b.row_positions[r] < 0) continue;
+      const int count = min(g.W, b.all_counts[r]);
+      const int depth0 = b.row_depth[r];
+      const int32_t* ids = b.all_ids + (long long)r * g.W;
+      for (int col = lane; col < count; col += 32) {
+        const int block = ids[col];
+        if (block < 0 || block >= g.P || !b.flags[block]) continue;
+        const int first = b.first_depth[block];
+        const int depth = depth0 + col;
+        if (depth < first || depth >= first + kNearWindow) continue;
+        bool unique = true;
+        for (int back = 1; back < kNearWindow; ++back)
+          if (col >= back && ids[col - back] == block) unique = false;
+        if (unique) atomicAdd(&b.near_consumers[block], 1);
+      }
+    }
+    cluster_sync();
+  }
+
+  // ---- 6: IOIDs / Ranks by counting smaller unique keys
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(scratch);
+  const unsigned long long P = (unsigned long long)g.P, rows = (unsigned long long)g.R;
+  for (int p = threadIdx.x; p < g.P; p += kFusedThreads) {
+    unsigned long long key = ~0ull;
+    if (b.flags[p]) {
+      if (g.ORDER == CXS_ORDER_PHYSICAL) {
+        key = (unsigned long long)p;
+      } else {
+        const unsigned long long first = (unsigned long long)b.first_depth[p];
+        const unsigned long long near =
+            g.ORDER == CXS_ORDER_DEPTH_SHARED ? (unsigned long long)b.near_consumers[p] : 0ull;
+        key = (first * (rows + 1) + rows - near) * P + (unsigned long long)p;
+      }
+    }
+    keys[p] = key;
+  }
+  __syncthreads();
+  // One warp per missing block (blocks spread over the CTAs); the lanes
+  // split the keys and the warp sums their counts.
+  for (int p = warp * ctas + blockIdx.x; p < g.P; p += gwarps) {
+    const unsigned long long key = keys[p];
+    if (key == ~0ull) continue;
+    int rank = 0;
+    for (int j = lane; j < g.P; j += 32) rank += keys[j] < key;
+    rank = cxs::warp_sum(rank);
+    if (lane == 0) {
+      b.ioids[rank] = p;
+      b.ranks[p] = rank;
+    }
+  }
+}
+
 int sort_items(int n) {
   int items = 1;
   while (items * 1024 < n) items *= 2;
@@ -775,10 +1324,12 @@ int check_geometry(const cxs_plan_geometry* geo, Geo* out) {
   g.CONSUMERS = geo->consumer_ctas;
   g.ORDER = geo->read_order;
   g.PRIVATE = geo->private_plan;
+  g.MODE = geo->launch_mode;
   g.POOL = geo->pool_tokens;
   if (g.Q < 1 || g.H < 1 || g.W < 1 || g.BS < 1 || (g.BS & (g.BS - 1)) || g.MAP < 1 ||
       g.CAP < 1 || g.HOT < 1 || g.REGIONS < 1 || g.PAGE < 1 || g.CONSUMERS < 1)
     return set_error(CXS_ERR_INVALID, "nonempty plan geometry and power-of-two BS required");
+  if (g.MODE < 0 || g.MODE > 1) return set_error(CXS_ERR_INVALID, "launch_mode must be 0 or 1");
   if (g.ORDER < CXS_ORDER_PHYSICAL || g.ORDER > CXS_ORDER_DEPTH_SHARED)
     return set_error(CXS_ERR_INVALID, "unknown read order %d", g.ORDER);
   if ((long long)g.MAP * g.BS > kInt32Max)
@@ -786,6 +1337,14 @@ int check_geometry(const cxs_plan_geometry* geo, Geo* out) {
   if (g.SORT < g.HOT) return set_error(CXS_ERR_INVALID, "sort_extent must cover hot");
   g.P = g.H * g.CAP;
   g.R = g.Q * g.H;
+  auto log2_or_minus = [](int v) {
+    if (v < 1 || (v & (v - 1))) return -1;
+    int shift = 0;
+    while ((1 << shift) < v) ++shift;
+    return shift;
+  };
+  g.PAGE_SHIFT = log2_or_minus(g.PAGE);
+  g.REGION_SHIFT = log2_or_minus(g.REGIONS);
   g.HASH = 1;
   while (g.HASH < 2 * g.HOT) g.HASH *= 2;
   if (g.MAP + 1 > kMaxMapBlocks)
@@ -830,6 +1389,71 @@ int launch_hot(const Geo& g, const cxs_plan_buffers& b, cudaStream_t stream) {
   return CXS_OK;
 }
 
+// The single-cluster plan when the geometry allows it (deduplicating plan,
+// launch_mode 0, at most kFusedMaxPhysical blocks, BS <= 64, shared-memory
+// tables within bounds); *launched reports whether it ran.
+int launch_fused(const Geo& g, const cxs_plan_buffers& b, int max_depth, cudaStream_t stream,
+                 int* launched) {
+  *launched = 0;
+  if (g.PRIVATE || g.MODE != 0 || g.P > kFusedMaxPhysical || g.MAP + 1 > kFusedMaxMap ||
+      g.BS > 64)
+    return CXS_OK;
+  if (g.H > kFusedMaxHeads) return CXS_OK;
+  const size_t words = (size_t)(g.MAP + 31) / 32;
+  size_t smem = 2 * (size_t)g.H * words * 4;
+  smem = smem > (size_t)g.HASH * 8 ? smem : (size_t)g.HASH * 8;
+  smem = smem > (size_t)g.P * 8 ? smem : (size_t)g.P * 8;
+  smem += ((words * 4 + 15) & ~(size_t)15) + 16;  // the claim bitmap in front
+  constexpr size_t kMaxFusedSmem = 160 * 1024;
+  if (smem > kMaxFusedSmem) return CXS_OK;
+  static int cluster_cache[64] = {0};  // CTAs per cluster for this device (-1: none)
+  int device = 0;
+  CXS_CUDA(cudaGetDevice(&device));
+  if (device < 0 || device >= 64) return CXS_OK;
+  cudaLaunchConfig_t config = {};
+  config.blockDim = dim3(kFusedThreads);
+  config.dynamicSmemBytes = kMaxFusedSmem;
+  config.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  if (!cluster_cache[device]) {
+    CXS_CUDA(cudaFuncSetAttribute(plan_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kMaxFusedSmem));
+    if (cudaFuncSetAttribute(plan_fused_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                             1) != cudaSuccess)
+      cudaGetLastError();
+    cluster_cache[device] = -1;
+    for (int size : {16, 8}) {
+      config.gridDim = dim3(size);
+      attr[0].val.clusterDim.x = size;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, plan_fused_kernel, &config) == cudaSuccess &&
+          clusters >= 1) {
+        cluster_cache[device] = size;
+        break;
+      }
+      cudaGetLastError();
+    }
+  }
+  const int ctas = cluster_cache[device];
+  if (ctas < g.H) return CXS_OK;
+  const int chain = (g.R + g.CONSUMERS - 1) / g.CONSUMERS - 1;  // earlier rows per consumer
+  const int merged = chain <= kFusedMaxChain;
+  config.gridDim = dim3(ctas);
+  config.dynamicSmemBytes = smem;
+  attr[0].val.clusterDim.x = ctas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  CXS_CUDA(cudaLaunchKernelEx(&config, plan_fused_kernel, g, b, max_depth, merged));
+  cxs_host::count_launch();
+  *launched = 1;
+  return CXS_OK;
+}
+
 }  // namespace
 
 extern "C" int cxs_plan_check(const cxs_plan_geometry* geometry) {
@@ -861,6 +1485,17 @@ static int plan_impl(const cxs_plan_geometry* geometry, const cxs_plan_buffers* 
     return set_error(CXS_ERR_INVALID, "query-private plan buffers missing");
   cudaStream_t stream = (cudaStream_t)stream_ptr;
   int max_depth = ((g.R + g.CONSUMERS - 1) / g.CONSUMERS) * g.W;
+  int fused = 0;
+  status = launch_fused(g, b, max_depth, stream, &fused);
+  if (status != CXS_OK) return status;
+  if (fused) {
+    if (!hot) return CXS_OK;
+    switch (sort_items(g.HOT)) {
+      case 1: return launch_hot<1>(g, b, stream);
+      case 2: return launch_hot<2>(g, b, stream);
+      default: return launch_hot<4>(g, b, stream);
+    }
+  }
   int warps_per_cta = 8;
   int row_grid = (g.Q * g.H + warps_per_cta - 1) / warps_per_cta;
   int r_grid = (g.R + warps_per_cta - 1) / warps_per_cta;

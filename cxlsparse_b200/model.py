@@ -82,9 +82,23 @@ class NSAExtendModel:
 
     def __init__(self, cfg=None, *, device="cuda", seed=0, max_users=1, max_history=16384,
                  hot_policy="frequency", read_order="consumption_depth",
-                 cross_query_dedup=True, pool_regions=1, chunk=1024, workspaces=None):
+                 cross_query_dedup=True, pool_regions=1, chunk=1024, workspaces=None,
+                 head_shard=(0, 1), exchange=None):
         self.cfg = cfg = cfg or NSAConfig()
         self.device = torch.device(device)
+        # KV-head sharding: this instance owns KV heads
+        # [head0, head0 + kv_local) of every layer (their query heads, pool
+        # slice, cache rows, planner and attention); `exchange` turns the
+        # local attention output [E, kv_local, 16, 64] into all heads'
+        # [E, kv_heads, 16, 64] (an all-gather across the shard group).
+        shard, shards = head_shard
+        if shards < 1 or cfg.kv_heads % shards or not 0 <= shard < shards:
+            raise ValueError("head_shard must split the KV heads evenly")
+        if shards > 1 and exchange is None:
+            raise ValueError("a head-sharded model needs an exchange")
+        self.kv_local = cfg.kv_heads // shards
+        self.head0 = shard * self.kv_local
+        self.exchange = exchange
         self.max_history, self.chunk = max_history, chunk
         g = torch.Generator(device="cpu").manual_seed(seed)
 
@@ -104,10 +118,10 @@ class NSAExtendModel:
                 gate=normal(cfg.ffn, d), up=normal(cfg.ffn, d), down=normal(d, cfg.ffn)))
         self.inv_freq = 1.0 / (cfg.rope_theta ** (
             torch.arange(0, cfg.head_dim, 2, device=self.device).float() / cfg.head_dim))
-        pages_per_user = cfg.layers * cfg.kv_heads * math.ceil(max_history / 64)
+        pages_per_user = cfg.layers * self.kv_local * math.ceil(max_history / 64)
         self.pool = MemoryPool(pages_per_user * max_users, 128, "host", page_size=64,
                                regions=pool_regions, device=self.device)
-        self.cache = HiSparseCache(self.pool, rows=max_users * cfg.layers * cfg.kv_heads,
+        self.cache = HiSparseCache(self.pool, rows=max_users * cfg.layers * self.kv_local,
                                    max_history=max_history, hot=cfg.hot,
                                    topk=min(cfg.hot, 256), dim=128)
         self.transport = GRSelectedTransport(
@@ -123,11 +137,11 @@ class NSAExtendModel:
     def user(self, name):
         if name not in self.users:
             cfg = self.cfg
-            empty = torch.empty((0, cfg.kv_heads, 128), dtype=torch.bfloat16, device=self.device)
+            empty = torch.empty((0, self.kv_local, 128), dtype=torch.bfloat16, device=self.device)
             pages_needed = math.ceil(self.max_history / 64)
             self.users[name] = UserState(
-                row=len(self.users) * cfg.layers * cfg.kv_heads,
-                pages=[[self.pool.allocate(pages_needed) for _ in range(cfg.kv_heads)]
+                row=len(self.users) * cfg.layers * self.kv_local,
+                pages=[[self.pool.allocate(pages_needed) for _ in range(self.kv_local)]
                        for _ in range(cfg.layers)],
                 summaries=[empty] * cfg.layers, tails=[empty] * cfg.layers,
                 windows=[empty] * cfg.layers)
@@ -143,8 +157,10 @@ class NSAExtendModel:
         v = F.linear(x, w["v"]).view(-1, cfg.kv_heads, cfg.head_dim)
         gates = torch.sigmoid(F.linear(x, w["g"])).view(-1, cfg.kv_heads, cfg.groups, 3)
         q, k = rotary(q, k, positions, self.inv_freq)
-        query = q.reshape(-1, cfg.kv_heads, cfg.groups, cfg.head_dim)
-        records = torch.cat((k, v), -1).contiguous()
+        own = slice(self.head0, self.head0 + self.kv_local)
+        query = q.reshape(-1, cfg.kv_heads, cfg.groups, cfg.head_dim)[:, own].contiguous()
+        gates = gates[:, own].contiguous()
+        records = torch.cat((k[:, own], v[:, own]), -1).contiguous()
         total = old + len(records)
         compressed, tail = ops.append_compressed(st.summaries[index], st.tails[index], records,
                                                  cfg.block_size)
@@ -152,13 +168,15 @@ class NSAExtendModel:
             query, compressed, positions, total, cfg.block_size, cfg.block_counts)
         window_kv = torch.cat((st.windows[index], records))
         window_start = old - len(st.windows[index])
-        base = st.row + index * cfg.kv_heads
+        base = st.row + index * self.kv_local
         fetches = [dict(row=base + h, cached_length=old, history_length=old,
-                        current_kv=records[:, h].contiguous()) for h in range(cfg.kv_heads)]
+                        current_kv=records[:, h].contiguous()) for h in range(self.kv_local)]
         mixed, counters = self.transport.run(
             query, blocks, positions, fetches, cfg.block_size, window=cfg.window,
             window_kv=window_kv, window_start=window_start, compressed=cmp_out, gates=gates)
         self.counters.append(counters)
+        if self.exchange is not None:
+            mixed = self.exchange(mixed)
         hidden = hidden + F.linear(mixed.reshape(len(hidden), -1), w["o"])
         x = rms_norm(hidden, w["post_norm"], cfg.rms_eps)
         hidden = hidden + F.linear(F.silu(F.linear(x, w["gate"])) * F.linear(x, w["up"]),
@@ -171,10 +189,10 @@ class NSAExtendModel:
         """Persist this chunk as history: pool write, slot table, summaries, window."""
         cfg = self.cfg
         old = st.length
-        for h in range(cfg.kv_heads):
+        for h in range(self.kv_local):
             slots = self.pool.token_slots(st.pages[index][h], old, old + len(records))
             self.pool.write_many(slots, records[:, h].contiguous(), asynchronous=True)
-            self.cache.append_slots(st.row + index * cfg.kv_heads + h, old, slots)
+            self.cache.append_slots(st.row + index * self.kv_local + h, old, slots)
         st.summaries[index], st.tails[index] = compressed, tail
         st.windows[index] = window_kv[max(0, len(window_kv) - cfg.window + 1):].clone()
 
@@ -217,9 +235,15 @@ class NSAExtendModel:
         """
         cfg, st, d = self.cfg, self.user(user), self.device
         E = extend_tokens
+        kl, h0, gd = self.kv_local, self.head0, cfg.groups * cfg.head_dim
         for w in self.layers:
             if "qkvg" not in w:
-                w["qkvg"] = torch.cat([w["q"], w["k"], w["v"], w["g"]]).contiguous()
+                # Projection rows of the owned heads only: q, k, v, gate logits.
+                w["qkvg"] = torch.cat([w["q"][h0 * gd:(h0 + kl) * gd],
+                                       w["k"][h0 * cfg.head_dim:(h0 + kl) * cfg.head_dim],
+                                       w["v"][h0 * cfg.head_dim:(h0 + kl) * cfg.head_dim],
+                                       w["g"][h0 * cfg.groups * 3:(h0 + kl) * cfg.groups * 3]]
+                                      ).contiguous()
                 w["gate_up"] = torch.cat([w["gate"], w["up"]]).contiguous()
         layers = []
         for index in range(cfg.layers):
@@ -229,15 +253,14 @@ class NSAExtendModel:
                 raise ValueError("window must retain the summary tail")
             c_hist = len(st.summaries[index])
             new = (tail + E) // cfg.block_size
-            window_buf = torch.empty((kept + E, cfg.kv_heads, 128), dtype=torch.bfloat16, device=d)
+            window_buf = torch.empty((kept + E, kl, 128), dtype=torch.bfloat16, device=d)
             window_buf[:kept] = st.windows[index]
-            summaries = torch.empty((c_hist + new, cfg.kv_heads, 128), dtype=torch.bfloat16,
-                                    device=d)
+            summaries = torch.empty((c_hist + new, kl, 128), dtype=torch.bfloat16, device=d)
             summaries[:c_hist] = st.summaries[index]
-            current = torch.empty((cfg.kv_heads, E, 128), dtype=torch.bfloat16, device=d)
-            base = st.row + index * cfg.kv_heads
+            current = torch.empty((kl, E, 128), dtype=torch.bfloat16, device=d)
+            base = st.row + index * kl
             fetches = [dict(row=base + h, cached_length=st.length, history_length=st.length,
-                            current_kv=current[h]) for h in range(cfg.kv_heads)]
+                            current_kv=current[h]) for h in range(kl)]
             layers.append(dict(kept=kept, tail=tail, c_hist=c_hist, new=new,
                                window_buf=window_buf, summaries=summaries, current=current,
                                fetches=fetches, window_start=st.length - kept))
@@ -245,9 +268,8 @@ class NSAExtendModel:
             E=E, user=user, layers=layers,
             positions=torch.arange(st.length, st.length + E, device=d, dtype=torch.int32),
             x=torch.empty((E, cfg.hidden), dtype=torch.bfloat16, device=d),
-            query=torch.empty((E, cfg.kv_heads, cfg.groups, cfg.head_dim), dtype=torch.bfloat16,
-                              device=d),
-            gates=torch.empty((E, cfg.kv_heads, cfg.groups, 3), dtype=torch.bfloat16, device=d),
+            query=torch.empty((E, kl, cfg.groups, cfg.head_dim), dtype=torch.bfloat16, device=d),
+            gates=torch.empty((E, kl, cfg.groups, 3), dtype=torch.bfloat16, device=d),
             mlp=torch.empty((E, cfg.ffn), dtype=torch.bfloat16, device=d))
         return self.fast
 
@@ -262,14 +284,15 @@ class NSAExtendModel:
                                     cfg.hidden, cfg.rms_eps, stream))
         proj = F.linear(x, w["qkvg"])
         records = L["window_buf"][L["kept"]:]
+        kl = self.kv_local
         _lib.check(lib.cxs_qkv_rope(
             proj.data_ptr(), proj.shape[1], positions.data_ptr(), self.inv_freq.data_ptr(), E,
-            cfg.q_heads, cfg.kv_heads, query.data_ptr(), records.data_ptr(),
-            cfg.kv_heads * 128, L["current"].data_ptr(), E * 128, gates.data_ptr(), stream))
+            kl * cfg.groups, kl, query.data_ptr(), records.data_ptr(),
+            kl * 128, L["current"].data_ptr(), E * 128, gates.data_ptr(), stream))
         if L["new"]:
             start = L["window_buf"][L["kept"] - L["tail"]:]
             _lib.check(lib.cxs_block_summaries(
-                start.data_ptr(), L["tail"] + E, cfg.kv_heads, cfg.block_size,
+                start.data_ptr(), L["tail"] + E, kl, cfg.block_size,
                 L["summaries"][L["c_hist"]:].data_ptr(), stream))
         total = L["window_start"] + L["kept"] + E
         cmp_out, blocks = ops.compressed_attention_select(
@@ -282,6 +305,8 @@ class NSAExtendModel:
             window_kv=L["window_buf"], window_start=L["window_start"], compressed=cmp_out,
             gates=gates, workspace_id=index)
         self.counters.append(counters)
+        if self.exchange is not None:
+            mixed = self.exchange(mixed)
         hidden = torch.addmm(hidden, mixed.reshape(E, -1), w["o"].t())
         _lib.check(lib.cxs_rms_norm(hidden.data_ptr(), w["post_norm"].data_ptr(), x.data_ptr(),
                                     E, cfg.hidden, cfg.rms_eps, stream))

@@ -110,6 +110,9 @@ typedef struct cxs_plan_geometry {
   int32_t consumer_ctas; /* consumers assumed by the depth order */
   int32_t read_order;    /* CXS_ORDER_* */
   int32_t private_plan;  /* 0 = dedup across rows, 1 = query-private */
+  int32_t launch_mode;   /* 0: a deduplicating plan runs as one launch of a
+                            single thread-block cluster when its tables fit
+                            (otherwise, and for 1, one launch per phase) */
   int64_t pool_tokens;   /* pool capacity in token slots */
 } cxs_plan_geometry;
 
@@ -154,6 +157,7 @@ typedef struct cxs_plan_buffers {
   int32_t* private_occurrences; /* [R, W] */
   int32_t* canonical;           /* [H, sort_extent] */
 } cxs_plan_buffers;
+
 
 /* Bytes of dynamic shared memory / limits check for a geometry; returns
  * CXS_ERR_CAPACITY for geometries the kernels refuse (before any launch). */

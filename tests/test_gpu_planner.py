@@ -20,7 +20,8 @@ from oracle import plan as P
 pytestmark = pytest.mark.gpu
 
 
-def run_device_plan(z, device, *, private=None, read_order=None, consumer_ctas=None):
+def run_device_plan(z, device, *, private=None, read_order=None, consumer_ctas=None,
+                    single_launch=True):
     private = bool(int(z["private"])) if private is None else private
     read_order = read_order or str(z["read_order"])
     tags = torch.from_numpy(z["tags"]).to(device, torch.int32)
@@ -46,6 +47,8 @@ def run_device_plan(z, device, *, private=None, read_order=None, consumer_ctas=N
     # The plan reads these on every (graph) replay: keep them alive with w.
     w["_inputs"] = (blocks, positions, desc, bases, tags, locs, host_locs, cache)
     buffers.hot_data = int(z["hot_data"])
+    if not single_launch:
+        w["c_geometry"].launch_mode = 1  # one launch per planner phase
     # Stale scratch from an earlier call must not leak into the next plan.
     for key in ("address", "hbm", "slots", "valid", "all_ids", "chosen"):
         w[key].fill_(77)
@@ -54,10 +57,11 @@ def run_device_plan(z, device, *, private=None, read_order=None, consumer_ctas=N
     return w
 
 
+@pytest.mark.parametrize("single_launch", [True, False], ids=["fused", "per_phase"])
 @pytest.mark.parametrize("path", plan_fixtures(), ids=lambda p: p.stem)
-def test_device_plan_matches_reference_bit_exact(cuda, path):
+def test_device_plan_matches_reference_bit_exact(cuda, path, single_launch):
     z = load(path)
-    w = run_device_plan(z, cuda)
+    w = run_device_plan(z, cuda, single_launch=single_launch)
     cpu = {k: v.cpu().numpy() for k, v in w.items() if isinstance(v, torch.Tensor)}
     for key in EXACT_KEYS:
         assert np.array_equal(cpu[key].astype(np.int64), z["ref_" + key].astype(np.int64)), key
@@ -74,11 +78,13 @@ def test_device_plan_matches_reference_bit_exact(cuda, path):
     assert np.array_equal(cpu["chosen"], z["chosen"][:, :hot].astype(np.int64))
 
 
+@pytest.mark.parametrize("single_launch", [True, False], ids=["fused", "per_phase"])
 @pytest.mark.parametrize("order", ["physical", "consumption_depth", "consumption_depth_shared"])
 @pytest.mark.parametrize("consumers", [1, 3, 256])
-def test_device_read_orders_match_oracle(cuda, order, consumers):
+def test_device_read_orders_match_oracle(cuda, order, consumers, single_launch):
     z = load(plan_fixtures()[3])  # miss_bs64_shared_regions
-    w = run_device_plan(z, cuda, read_order=order, consumer_ctas=consumers)
+    w = run_device_plan(z, cuda, read_order=order, consumer_ctas=consumers,
+                        single_launch=single_launch)
     args = oracle_args(z)
     args.update(read_order=order, consumer_ctas=min(consumers, w["rows"]))
     ref = P.active_plan(**args)

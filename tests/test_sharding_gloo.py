@@ -7,7 +7,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from cxlsparse_b200.sharding import gather_scores, users_for_rank
+from cxlsparse_b200.sharding import (gather_scores, head_exchange, head_pair_groups,
+                                     users_for_rank)
 
 
 def _free_port():
@@ -44,3 +45,32 @@ def test_assignment_covers_every_user_once():
     for world in (1, 2, 4, 8):
         seen = sorted(u for r in range(world) for u in users_for_rank(users, r, world))
         assert seen == users
+
+
+def _head_worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        group, shard, shards, pair, pairs = head_pair_groups(world)
+        exchange = head_exchange(group, shards)
+        # [E=3, kv_local=1, 16, 64]: head value = 100 * (global head) + token
+        local = torch.zeros(3, 1, 16, 64)
+        for e in range(3):
+            local[e] = 100 * (shard + 0) + e + 1000 * pair
+        full = exchange(local)
+        results[rank] = (shard, shards, pair, pairs, full[:, :, 0, 0].tolist())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_head_pairs_exchange_attention_outputs():
+    world = 4
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_head_worker, args=(world, _free_port(), results), nprocs=world,
+                       start_method="spawn")
+    for rank in range(world):
+        shard, shards, pair, pairs, heads = results[rank]
+        assert (shard, shards, pair, pairs) == (rank % 2, 2, rank // 2, 2)
+        # token e: [head 0 of the pair, head 1 of the pair]
+        assert heads == [[1000 * pair + e, 1000 * pair + 100 + e] for e in range(3)]
