@@ -62,6 +62,9 @@ def parse():
     p.add_argument("--jitter", type=int, default=1000)
     p.add_argument("--sigma", type=float, default=0.5)
     p.add_argument("--candidates", type=int, default=16)
+    p.add_argument("--packed", action="store_true",
+                   help="pack several candidates into one suffix, as the reference does "
+                        "(worker/prompt.py:24-55), instead of one segment per candidate")
     p.add_argument("--profile-step", action="store_true",
                    help="after prefill, run one eager extend inside the NVTX range "
                         "'profile_step' and exit (for ncu --nvtx-include profile_step/)")
@@ -378,7 +381,9 @@ def run_ours(args):
 def run_dedup(args):
     """16 candidate queries of E=128 sharing one H=16K history,
     all history cold; candidate hidden states = shared base + N(0, sigma).
-    The candidates are packed into one suffix (worker/prompt.py:24-55)."""
+    Each candidate sees the history and its own suffix (candidate segments);
+    with --packed they share one suffix as the reference packs them
+    (worker/prompt.py:24-55)."""
     import torch
 
     from cxlsparse_b200.model import NSAConfig, NSAExtendModel
@@ -387,7 +392,9 @@ def run_dedup(args):
     torch.cuda.set_device(device)
     cfg = NSAConfig(layers=args.layers)
     E = args.candidates * 128
-    model = NSAExtendModel(cfg, device=device, seed=0, max_history=args.history + E,
+    segments = 1 if args.packed else args.candidates
+    model = NSAExtendModel(cfg, device=device, seed=0,
+                           max_history=args.history + E + 64 * args.candidates,
                            hot_policy="static")
     g = torch.Generator().manual_seed(2000)
     history = torch.randint(0, cfg.vocab, (args.history,), generator=g).to(device)
@@ -397,7 +404,7 @@ def run_dedup(args):
     hidden = torch.cat([base + args.sigma * torch.randn(128, cfg.hidden, generator=g)
                         for _ in range(args.candidates)]).to(device, torch.bfloat16)
     ids = torch.zeros(E, dtype=torch.int64, device=device)
-    model.prepare_fast(E)
+    model.prepare_fast(E // segments, candidates=segments)
     for _ in range(args.warmup):
         model.extend_fast(ids, hidden)
     torch.cuda.synchronize(device)
@@ -413,6 +420,7 @@ def run_dedup(args):
     print(json.dumps({
         "workload": "BASELINE configs[2] dedup stress", "sigma": args.sigma,
         "candidates": args.candidates, "extend_rows": E, "history": args.history,
+        "suffix": "one packed suffix" if args.packed else "one segment per candidate",
         "ms_per_step": ms, "tok_s": E / (ms / 1e3),
         "shared_bytes_per_step": shared * 256, "private_bytes_per_step": private * 256,
         "fetched_byte_reduction": 1 - shared / max(private, 1)}))
@@ -423,10 +431,12 @@ def run_serving(args):
     """users_per_gpu users per GPU (users round-robin over ranks),
     each with its own jittered history (H +- jitter tokens, so most tails are
     partial 64-token blocks) in this GPU's pinned pool slice, and one extend
-    request per user per step: `queries` candidates of E tokens packed into
-    one suffix (worker/prompt.py:24-55). A step serves every local user once,
-    back to back (one captured graph per user); per-user final hidden states
-    are all-gathered with NCCL (the only collective)."""
+    request per user per step: `queries` candidates of E tokens, each seeing
+    the history and its own suffix (candidate segments; --packed packs them
+    into one suffix as worker/prompt.py:24-55 does). A step serves every
+    local user once, back to back (one captured graph per user); the final
+    hidden state of every candidate is all-gathered with NCCL (the only
+    collective)."""
     import torch
 
     from cxlsparse_b200.model import NSAConfig, NSAExtendModel
@@ -445,8 +455,9 @@ def run_serving(args):
                for _ in range(users_total)]
     mine = users_for_rank(list(range(users_total)), rank, world)
     suffix = args.queries * args.extend
+    segments = 1 if args.packed else args.queries
     model = NSAExtendModel(cfg, device=device, seed=0, max_users=len(mine),
-                           max_history=max(lengths[u] for u in mine) + suffix,
+                           max_history=max(lengths[u] for u in mine) + suffix + 64 * segments,
                            read_order=args.read_order,
                            workspaces=cfg.layers * len(mine) + 4)
     t0 = time.perf_counter()
@@ -460,7 +471,8 @@ def run_serving(args):
     captured = {}
     launches = 0
     for u in mine:
-        graph, static_ids, static_out, counters = model.capture_extend(suffix, user=f"u{u}")
+        graph, static_ids, static_out, counters = model.capture_extend(
+            suffix // segments, user=f"u{u}", candidates=segments)
         static_ids.copy_(candidates[u].to(device))
         captured[u] = (graph, static_ids, static_out, counters)
         launches += model.captured_launches
@@ -507,8 +519,10 @@ def run_serving(args):
     device_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
 
     host_ids = {u: candidates[u].pin_memory() for u in mine}
-    local_out = torch.empty((len(mine), cfg.hidden), dtype=torch.bfloat16, device=device)
-    host_out = torch.empty((world, len(mine), cfg.hidden), dtype=torch.bfloat16,
+    # Result per user: the final hidden state of each candidate's last token.
+    local_out = torch.empty((len(mine), segments, cfg.hidden), dtype=torch.bfloat16,
+                            device=device)
+    host_out = torch.empty((world, len(mine), segments, cfg.hidden), dtype=torch.bfloat16,
                            pin_memory=True)
     barrier()
     start.record(stream)
@@ -517,7 +531,7 @@ def run_serving(args):
             graph, static_ids, static_out, _ = captured[u]
             static_ids.copy_(host_ids[u], non_blocking=True)
             graph.replay()
-            local_out[i].copy_(static_out[-1])
+            local_out[i].copy_(static_out.view(segments, -1, cfg.hidden)[:, -1])
         gathered = gather_scores(local_out) if dist is not None else local_out[None]
         host_out.copy_(gathered, non_blocking=True)
     end.record(stream)
@@ -536,7 +550,9 @@ def run_serving(args):
                     "history KV computed by the model (chunked prefill)",
             "config": {"workload": f"BASELINE configs[3]: {args.users_per_gpu} users per GPU, "
                                    f"H={args.history}+-{args.jitter}, {args.queries} queries x "
-                                   f"E={args.extend} per user (one packed suffix)",
+                                   f"E={args.extend} per user",
+                       "suffix": "one packed suffix" if args.packed
+                       else "one segment per candidate (history + own suffix)",
                        "users": users_total, "users_per_gpu": args.users_per_gpu,
                        "history_lengths_rank0": [lengths[u] for u in mine],
                        "layers": args.layers, "block_size": 64, "top_n": 16, "window": 512,
@@ -545,7 +561,7 @@ def run_serving(args):
                        "parallelism": f"users round-robin over {world} GPU(s)"},
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s",
                     "h2d_bytes_per_step": len(mine) * suffix * 8,
-                    "d2h_bytes_per_step": world * len(mine) * cfg.hidden * 2},
+                    "d2h_bytes_per_step": world * len(mine) * segments * cfg.hidden * 2},
             "gpu_launches": launches * args.steps,
             "fetch": {"bytes_per_step_rank0": fetched,
                       "gb_s_over_step_rank0": fetched / (device_ms / 1e3) / 1e9,
@@ -575,8 +591,9 @@ def run_headsplit(args):
     of every layer for the pair's users (its 16 query heads, pool slice,
     planner, fetch and attention) and the pair all-gathers the attention
     outputs once per layer before o_proj. Users are round-robin over pairs;
-    each gets H history tokens and `queries` candidates of E tokens packed
-    into one suffix. On one GPU the same user set runs with both heads local
+    each gets H history tokens and `queries` candidates of E tokens, one
+    segment per candidate (--packed: one packed suffix). On one GPU the same
+    user set runs with both heads local
     (the reference point for the split). A step serves every user of the pair
     once (one captured graph per user, collectives inside)."""
     import torch
@@ -595,8 +612,10 @@ def run_headsplit(args):
     users_total = args.users_per_pair * pairs
     mine = users_for_rank(list(range(users_total)), pair, pairs)
     suffix = args.queries * args.extend
+    segments = 1 if args.packed else args.queries
     model = NSAExtendModel(cfg, device=device, seed=0, max_users=len(mine),
-                           max_history=args.history + suffix, read_order=args.read_order,
+                           max_history=args.history + suffix + 64 * segments,
+                           read_order=args.read_order,
                            workspaces=cfg.layers * len(mine) + 4, head_shard=(shard, shards),
                            exchange=head_exchange(group, shards) if shards > 1 else None)
     t0 = time.perf_counter()
@@ -609,7 +628,8 @@ def run_headsplit(args):
     prefill_s = time.perf_counter() - t0
     captured, launches = {}, 0
     for u in mine:
-        graph, static_ids, static_out, counters = model.capture_extend(suffix, user=f"u{u}")
+        graph, static_ids, static_out, counters = model.capture_extend(
+            suffix // segments, user=f"u{u}", candidates=segments)
         static_ids.copy_(candidates[u].to(device))
         captured[u] = (graph, static_ids, static_out, counters)
         launches += model.captured_launches
@@ -654,8 +674,10 @@ def run_headsplit(args):
     barrier()
     device_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
     host_ids = {u: candidates[u].pin_memory() for u in mine}
-    local_out = torch.empty((len(mine), cfg.hidden), dtype=torch.bfloat16, device=device)
-    host_out = torch.empty((world, len(mine), cfg.hidden), dtype=torch.bfloat16,
+    # Result per user: the final hidden state of each candidate's last token.
+    local_out = torch.empty((len(mine), segments, cfg.hidden), dtype=torch.bfloat16,
+                            device=device)
+    host_out = torch.empty((world, len(mine), segments, cfg.hidden), dtype=torch.bfloat16,
                            pin_memory=True)
     barrier()
     start.record(stream)
@@ -664,7 +686,7 @@ def run_headsplit(args):
             graph, static_ids, static_out, _ = captured[u]
             static_ids.copy_(host_ids[u], non_blocking=True)
             graph.replay()
-            local_out[i].copy_(static_out[-1])
+            local_out[i].copy_(static_out.view(segments, -1, cfg.hidden)[:, -1])
         gathered = gather_scores(local_out) if dist is not None else local_out[None]
         host_out.copy_(gathered, non_blocking=True)
     end.record(stream)
@@ -692,7 +714,7 @@ def run_headsplit(args):
                        else "1 GPU, both KV heads local"},
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s",
                     "h2d_bytes_per_step": len(mine) * suffix * 8,
-                    "d2h_bytes_per_step": world * len(mine) * cfg.hidden * 2},
+                    "d2h_bytes_per_step": world * len(mine) * segments * cfg.hidden * 2},
             "gpu_launches": launches * args.steps,
             "fetch": {"bytes_per_step_rank0": fetched,
                       "gb_s_over_step_rank0": fetched / (device_ms / 1e3) / 1e9,

@@ -23,6 +23,7 @@ READ_ORDERS = {
 }
 
 c_i32, c_i64, c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
+ABI_VERSION = 2  # CXS_ABI_VERSION
 
 
 class CxsError(RuntimeError):
@@ -61,7 +62,8 @@ class PlanBuffers(ctypes.Structure):
 class AttendGeometry(ctypes.Structure):
     _fields_ = [(name, c_i32) for name in (
         "queries", "heads", "width", "block_size", "physical", "window", "window_len",
-        "gate")] + [("window_start", c_i64), ("spin_limit", c_i64)]
+        "gate")] + [(name, c_i64) for name in (
+            "window_start", "spin_limit", "segment_start", "segment_tokens")]
 
 
 ATTEND_BUFFER_FIELDS = (
@@ -116,16 +118,24 @@ def lib():
                                                  ctypes.POINTER(AttendBuffers), c_vp]),
             "cxs_compressed_select": (c_i32, [c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_i32,
                                               c_i32, c_i64, c_vp, c_vp, c_vp, c_vp]),
+            "cxs_compressed_select_segments": (c_i32, [c_vp, c_vp, c_i32, c_vp, c_i32, c_i32,
+                                                       c_i32, c_i32, c_i64, c_i64, c_i64, c_vp,
+                                                       c_vp, c_vp, c_vp]),
             "cxs_block_summaries": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
+            "cxs_block_summaries_segments": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_i32,
+                                                     c_i64, c_i64, c_vp]),
             "cxs_rms_norm": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, ctypes.c_float, c_vp]),
             "cxs_qkv_rope": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp,
                                      c_i32, c_vp, c_i32, c_vp, c_vp]),
+            "cxs_qkv_rope_segments": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_i32, c_i32, c_i32,
+                                              c_vp, c_vp, c_i32, c_vp, c_i32, c_vp, c_i32,
+                                              c_i32, c_vp]),
             "cxs_silu_mul": (c_i32, [c_vp, c_i32, c_i32, c_vp, c_vp]),
         }
         for name, (restype, argtypes) in sigs.items():
             fn = getattr(handle, name)
             fn.restype, fn.argtypes = restype, argtypes
-        if handle.cxs_abi_version() != 1:
+        if handle.cxs_abi_version() != ABI_VERSION:
             raise ImportError("cxlsparse_b200 ABI version mismatch")
         _lib = handle
     return _lib
@@ -161,5 +171,6 @@ def exported_symbols():
             "cxs_pool_write", "cxs_plan_check", "cxs_plan", "cxs_plan_core",
             "cxs_plan_select_commit_hot", "cxs_plan_commit_hot",
             "cxs_fetch_attend", "cxs_attend_capacity", "cxs_fetch_attend_noalloc",
-            "cxs_compressed_select",
-            "cxs_block_summaries", "cxs_rms_norm", "cxs_qkv_rope", "cxs_silu_mul")
+            "cxs_compressed_select", "cxs_compressed_select_segments",
+            "cxs_block_summaries", "cxs_block_summaries_segments", "cxs_rms_norm",
+            "cxs_qkv_rope", "cxs_qkv_rope_segments", "cxs_silu_mul")

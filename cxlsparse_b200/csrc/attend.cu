@@ -29,6 +29,7 @@ constexpr int kThreads = 32 * (1 + kAttnWarps);
 struct AttendArgs {
   int Q, H, W, BS, P, window, window_len, gate;
   long long window_start, spin_limit;
+  int seg_start, seg_tokens;  // candidate segments (seg_tokens 0: one suffix)
   int consumers;  // attention warps of the launch: grid * kAttnWarps
   const __nv_bfloat16* query;
   __nv_bfloat16* kv;
@@ -170,15 +171,38 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
   for (int row = w * gridDim.x + blockIdx.x; row < rows; row += a.consumers) {
     const int h = row % a.H;
     const int pos = a.row_positions[row];
-    // Window: logical positions [w_lo, w_hi] (positions and window bounds fit
-    // int32: host-checked), in tiles of 64 from w_lo.
-    int w_lo = 1, w_hi = 0;
+    // Window: positions [w_lo, w_hi], then [o_lo, o_hi] (positions and window
+    // bounds fit int32: host-checked), each in tiles of 64 from its start.
+    // With candidate segments, a row of segment s sees the history below
+    // seg_start, then its own segment, which starts at seg_start + s *
+    // seg_tokens (true position = seg_start + offset into the segment); every
+    // segment row splits its window there, whatever s, so that a candidate's
+    // tiles (and roundings) do not depend on its segment index. Without
+    // segments the window is one contiguous range.
+    int w_lo = 1, w_hi = 0, o_lo = 1, o_hi = 0;
     if (a.window > 0 && pos >= 0) {
       const int w_first = (int)a.window_start, w_last = w_first + a.window_len - 1;
-      w_lo = max(max(pos - a.window + 1, 0), w_first);
-      w_hi = min(pos, w_last);
+      int own = -1, real = pos;
+      if (a.seg_tokens > 0 && pos >= a.seg_start) {
+        own = a.seg_start + (pos - a.seg_start) / a.seg_tokens * a.seg_tokens;
+        real = a.seg_start + (pos - own);
+      }
+      w_lo = max(max(real - a.window + 1, 0), w_first);
+      if (own < 0) {
+        w_hi = min(pos, w_last);
+      } else {
+        w_hi = min(a.seg_start - 1, w_last);
+        o_lo = max(own + max(real - a.window + 1 - a.seg_start, 0), w_first);
+        o_hi = min(pos, w_last);
+      }
     }
-    const int n_win = w_lo <= w_hi ? (w_hi - w_lo) / tc::kTileRows + 1 : 0;
+    const int n_hist = w_lo <= w_hi ? (w_hi - w_lo) / tc::kTileRows + 1 : 0;
+    const int n_win = n_hist + (o_lo <= o_hi ? (o_hi - o_lo) / tc::kTileRows + 1 : 0);
+    // First position and last position of window tile j.
+    auto win_first = [&](int j) {
+      return j < n_hist ? w_lo + j * tc::kTileRows : o_lo + (j - n_hist) * tc::kTileRows;
+    };
+    auto win_last = [&](int j) { return j < n_hist ? w_hi : o_hi; };
     const int count = pos >= 0 ? min(a.all_counts[row], a.W) : 0;
     const int total = n_win + count;
     // Lane i holds selected occurrence i (block id and first position).
@@ -206,8 +230,8 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
       uint8_t* dst = value ? ws.v(b) : ws.k(b);
       if (j < n_win) {
         cxs::mbar_expect_tx(bar, tc::kTileBytes);
-        tc::window_load(dst, &win_map, value ? 64 : 0, h,
-                        w_lo + j * tc::kTileRows - (int)a.window_start, bar);
+        tc::window_load(dst, &win_map, value ? 64 : 0, h, win_first(j) - (int)a.window_start,
+                        bar);
       } else {
         cxs::mbar_expect_tx(bar, BS * 128);
         cxs::tma_load_2d(dst, &kv_map, value ? 64 : 0, blk * BS, bar);
@@ -324,7 +348,7 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
         // B
         int lo = 0, hi = -1;
         if (t < n_win) {
-          hi = min(w_hi - (w_lo + t * tc::kTileRows), tc::kTileRows - 1);
+          hi = min(win_last(t) - win_first(t), tc::kTileRows - 1);
         } else if (cur_block >= 0 && cur_block < a.P) {
           hi = min(pos - cur_start, BS - 1);
         }
@@ -640,6 +664,8 @@ int launch(const cxs_attend_geometry& g, const cxs_attend_buffers& b, cudaStream
   a.window_len = g.window_len;
   a.gate = g.gate;
   a.window_start = g.window_start;
+  a.seg_start = (int)g.segment_start;
+  a.seg_tokens = (int)g.segment_tokens;
   a.spin_limit = g.spin_limit > 0 ? g.spin_limit : (1ll << 31);
   a.consumers = grid * kAttnWarps;
   a.query = (const __nv_bfloat16*)b.query;
@@ -695,8 +721,17 @@ extern "C" int cxs_fetch_attend(const cxs_attend_geometry* geometry,
     return set_error(CXS_ERR_INVALID, "width (top-n) must be at most 32");
   if (g.window < 0 || (g.window > 0 && (!b.window_kv || g.window_len < 1)))
     return set_error(CXS_ERR_INVALID, "window branch needs a window buffer");
-  if (g.window > 0 && (g.window_start < 0 || g.window_start + g.window_len > INT32_MAX))
+  // window_start may be negative: records before position 0 are padding that
+  // no window reaches (a window never starts below position 0).
+  if (g.window > 0 && (g.window_start < -(long long)g.window_len ||
+                       g.window_start + g.window_len > INT32_MAX))
     return set_error(CXS_ERR_INVALID, "window positions must fit int32");
+  if (g.segment_tokens < 0 || g.segment_start < 0 ||
+      (g.segment_tokens > 0 &&
+       (g.segment_start % g.block_size || g.segment_tokens % g.block_size ||
+        g.segment_start + (long long)g.segment_tokens * g.queries > INT32_MAX)))
+    return set_error(CXS_ERR_INVALID,
+                     "segment_start / segment_tokens must be block multiples and fit int32");
   if (g.gate && (!b.compressed || !b.gates))
     return set_error(CXS_ERR_INVALID, "gate mix needs compressed output and gates");
   if (((uintptr_t)b.kv & 15) || ((uintptr_t)b.query & 15) || ((uintptr_t)b.out & 15))

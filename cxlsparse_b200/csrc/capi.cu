@@ -163,10 +163,15 @@ extern "C" int cxs_pool_write(const void* records, const int64_t* slots, int64_t
 
 // Mean of BS consecutive tokens per (summary, head, channel), fp32 accumulate.
 // 128 channels x 8 token groups per CTA; partial sums reduced in shared memory.
+// Grid (summary, head, run): run z reads tokens + z * token_stride records and
+// writes out + z * summary_stride records.
 __global__ void block_summaries_kernel(const __nv_bfloat16* __restrict__ tokens, int heads,
-                                       int bs, __nv_bfloat16* __restrict__ out) {
+                                       int bs, __nv_bfloat16* __restrict__ out,
+                                       int64_t token_stride, int64_t summary_stride) {
   __shared__ float partial[8][128];
   int summary = blockIdx.x, head = blockIdx.y;
+  tokens += (int64_t)blockIdx.z * token_stride * heads * 128;
+  out += (int64_t)blockIdx.z * summary_stride * heads * 128;
   int c = threadIdx.x & 127, group = threadIdx.x >> 7;
   const __nv_bfloat16* base = tokens + ((int64_t)summary * bs * heads + head) * 128 + c;
   float acc = 0.f;
@@ -181,15 +186,27 @@ __global__ void block_summaries_kernel(const __nv_bfloat16* __restrict__ tokens,
   }
 }
 
-extern "C" int cxs_block_summaries(const void* tokens, int64_t count, int32_t heads,
-                                   int32_t block_size, void* summaries, void* stream) {
-  if (count < 0 || heads < 1 || block_size < 1)
+extern "C" int cxs_block_summaries_segments(const void* tokens, int64_t count, int32_t heads,
+                                            int32_t block_size, void* summaries,
+                                            int32_t segments, int64_t token_stride,
+                                            int64_t summary_stride, void* stream) {
+  if (count < 0 || heads < 1 || block_size < 1 || segments < 1 || segments > 65535 ||
+      token_stride < 0 || summary_stride < 0)
     return set_error(CXS_ERR_INVALID, "invalid summary geometry");
   int64_t n = count / block_size;
   if (!n) return CXS_OK;
-  dim3 grid((unsigned)n, heads);
+  if (segments > 1 && (token_stride < count || summary_stride < n))
+    return set_error(CXS_ERR_INVALID, "summary runs overlap");
+  dim3 grid((unsigned)n, heads, segments);
   block_summaries_kernel<<<grid, 1024, 0, (cudaStream_t)stream>>>(
-      (const __nv_bfloat16*)tokens, heads, block_size, (__nv_bfloat16*)summaries);
+      (const __nv_bfloat16*)tokens, heads, block_size, (__nv_bfloat16*)summaries, token_stride,
+      summary_stride);
   CXS_LAUNCH_CHECK("block_summaries_kernel");
   return CXS_OK;
+}
+
+extern "C" int cxs_block_summaries(const void* tokens, int64_t count, int32_t heads,
+                                   int32_t block_size, void* summaries, void* stream) {
+  return cxs_block_summaries_segments(tokens, count, heads, block_size, summaries, 1, 0, 0,
+                                      stream);
 }

@@ -100,9 +100,13 @@ __global__ void qkv_rope_kernel(const __nv_bfloat16* __restrict__ proj, int proj
                                 const float* __restrict__ inv_freq, int q_heads, int kv_heads,
                                 __nv_bfloat16* __restrict__ query, __nv_bfloat16* __restrict__ records,
                                 int records_stride, __nv_bfloat16* __restrict__ current,
-                                int current_stride, __nv_bfloat16* __restrict__ gates) {
+                                int current_stride, __nv_bfloat16* __restrict__ gates,
+                                int segment_rows, int segment_stride) {
   __shared__ float cos_s[32], sin_s[32];
   int t = blockIdx.x;
+  // Destination row of this token's record / current KV (candidate segments).
+  const long long d =
+      segment_rows > 0 ? (long long)(t / segment_rows) * segment_stride + t % segment_rows : t;
   const __nv_bfloat16* p = proj + (long long)t * proj_stride;
   if (threadIdx.x < 32) {
     const float angle = (float)positions[t] * inv_freq[threadIdx.x];
@@ -126,10 +130,10 @@ __global__ void qkv_rope_kernel(const __nv_bfloat16* __restrict__ proj, int proj
       dst[i + 32] = __float2bfloat16_rn(out_right);
     } else {
       int kh = head - q_heads;
-      __nv_bfloat16* rec = records + (long long)t * records_stride + kh * 128;
+      __nv_bfloat16* rec = records + d * records_stride + kh * 128;
       rec[i] = __float2bfloat16_rn(out_left);
       rec[i + 32] = __float2bfloat16_rn(out_right);
-      __nv_bfloat16* cur = current + (long long)kh * current_stride + (long long)t * 128;
+      __nv_bfloat16* cur = current + (long long)kh * current_stride + d * 128;
       cur[i] = __float2bfloat16_rn(out_left);
       cur[i + 32] = __float2bfloat16_rn(out_right);
     }
@@ -138,8 +142,8 @@ __global__ void qkv_rope_kernel(const __nv_bfloat16* __restrict__ proj, int proj
   for (int idx = threadIdx.x; idx < kv_cols; idx += blockDim.x) {
     int kh = idx / 64, i = idx % 64;
     __nv_bfloat16 v = p[q_cols + kv_cols + idx];
-    records[(long long)t * records_stride + kh * 128 + 64 + i] = v;
-    current[(long long)kh * current_stride + (long long)t * 128 + 64 + i] = v;
+    records[d * records_stride + kh * 128 + 64 + i] = v;
+    current[(long long)kh * current_stride + d * 128 + 64 + i] = v;
   }
   // gates: sigmoid, [Hkv, Hq/Hkv, 3] per token.
   for (int idx = threadIdx.x; idx < q_heads * 3; idx += blockDim.x) {
@@ -192,19 +196,31 @@ extern "C" int cxs_rms_norm(const void* x, const void* weight, void* out, int32_
   return CXS_OK;
 }
 
-extern "C" int cxs_qkv_rope(const void* proj, int32_t proj_stride, const int32_t* positions,
-                            const float* inv_freq, int32_t tokens, int32_t q_heads,
-                            int32_t kv_heads, void* query, void* records, int32_t records_stride,
-                            void* current, int32_t current_stride, void* gates, void* stream) {
-  if (tokens < 0 || q_heads < 1 || kv_heads < 1)
+extern "C" int cxs_qkv_rope_segments(const void* proj, int32_t proj_stride,
+                                     const int32_t* positions, const float* inv_freq,
+                                     int32_t tokens, int32_t q_heads, int32_t kv_heads,
+                                     void* query, void* records, int32_t records_stride,
+                                     void* current, int32_t current_stride, void* gates,
+                                     int32_t segment_rows, int32_t segment_stride, void* stream) {
+  if (tokens < 0 || q_heads < 1 || kv_heads < 1 || segment_rows < 0 ||
+      (segment_rows > 0 && segment_stride < segment_rows))
     return set_error(CXS_ERR_INVALID, "invalid qkv_rope geometry");
   if (!tokens) return CXS_OK;
   qkv_rope_kernel<<<tokens, 256, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)proj, proj_stride, positions, inv_freq, q_heads, kv_heads,
       (__nv_bfloat16*)query, (__nv_bfloat16*)records, records_stride, (__nv_bfloat16*)current,
-      current_stride, (__nv_bfloat16*)gates);
+      current_stride, (__nv_bfloat16*)gates, segment_rows, segment_stride);
   CXS_LAUNCH_CHECK("qkv_rope_kernel");
   return CXS_OK;
+}
+
+extern "C" int cxs_qkv_rope(const void* proj, int32_t proj_stride, const int32_t* positions,
+                            const float* inv_freq, int32_t tokens, int32_t q_heads,
+                            int32_t kv_heads, void* query, void* records, int32_t records_stride,
+                            void* current, int32_t current_stride, void* gates, void* stream) {
+  return cxs_qkv_rope_segments(proj, proj_stride, positions, inv_freq, tokens, q_heads,
+                               kv_heads, query, records, records_stride, current, current_stride,
+                               gates, 0, 0, stream);
 }
 
 extern "C" int cxs_silu_mul(const void* gate_up, int32_t rows, int32_t ffn, void* out,

@@ -43,6 +43,7 @@ int* g_select_error_address[kMaxDevices] = {nullptr};
 
 struct SelectArgs {
   int Q, H, C, BS, count, width, score_len;
+  int seg_block, seg_blocks;  // candidate segments in blocks (seg_blocks 0: one suffix)
   long long total;
   const __nv_bfloat16* query;
   const int32_t* positions;
@@ -51,6 +52,26 @@ struct SelectArgs {
   float* scores;
   int* error;
 };
+
+// Blocks [lo, hi) a row at `pos` never sees: for a row of candidate segment
+// s > 0, the segments before its own (and the part of segment 0 past the
+// history); empty otherwise.
+struct Gap {
+  int lo = 0, hi = 0;
+  __device__ __forceinline__ bool hides(int c) const { return c >= lo && c < hi; }
+};
+
+__device__ __forceinline__ Gap segment_gap(const SelectArgs& a, int pos) {
+  Gap gap;
+  if (a.seg_blocks > 0 && pos >= 0) {
+    const int s = (pos / a.BS - a.seg_block) / a.seg_blocks;
+    if (pos / a.BS >= a.seg_block && s > 0) {
+      gap.lo = a.seg_block;
+      gap.hi = a.seg_block + s * a.seg_blocks;
+    }
+  }
+  return gap;
+}
 
 __global__ void __launch_bounds__(kWarps * 32)
     compressed_select_kernel(const __grid_constant__ CUtensorMap map, SelectArgs a) {
@@ -77,6 +98,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   int pos = a.positions[q];
   int g = lane >> 2, c = lane & 3;
   int nc = pos >= 0 ? min((pos + 1) / a.BS, a.C) : 0;  // complete summaries
+  const Gap gap = segment_gap(a, pos);
   int tiles = (nc + kTileKeys - 1) / kTileKeys;
   long long spin = 1ll << 31;
   for (int i = threadIdx.x; i < score_len; i += blockDim.x) scores[i] = 0.f;
@@ -101,7 +123,8 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
     phase ^= 1;
     int base = t * kTileKeys;
-    sm.step(qa, k_addr, v_addr, lane, [&](int k) { return base + k < nc; });
+    sm.step(qa, k_addr, v_addr, lane,
+            [&](int k) { return base + k < nc && !gap.hides(base + k); });
     __syncwarp();
   }
   // Merge the warps' (max, sum, accumulator) per head through shared memory.
@@ -174,7 +197,7 @@ __global__ void __launch_bounds__(kWarps * 32)
       for (int e = 0; e < 2; ++e) {
         int key = t * kTileKeys + nt * 8 + 2 * c + e;
         float p = 0.f;
-        if (key < nc)
+        if (key < nc && !gap.hides(key))
           p = expf(sc[nt][e] - gm[0]) * inv[0] + expf(sc[nt][e + 2] - gm[1]) * inv[1];
         p += __shfl_xor_sync(0xffffffffu, p, 4);
         p += __shfl_xor_sync(0xffffffffu, p, 8);
@@ -200,6 +223,7 @@ __global__ void __launch_bounds__(kWarps * 32)
     float best = -1.f;
     int best_idx = 0x7fffffff;
     for (int i = lane; i < limit; i += 32) {
+      if (gap.hides(i)) continue;
       float v = scores[i];
       if (v > best || (v == best && i < best_idx)) {
         best = v;
@@ -327,6 +351,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const bool row_ok = q < a.Q;
   const int pos = row_ok ? a.positions[q] : -1;
   const int nc = pos >= 0 ? min((pos + 1) / a.BS, C) : 0;
+  const Gap gap = segment_gap(a, pos);
+  auto visible = [&](int c) { return c < nc && !gap.hides(c); };
   const long long qrow = ((long long)q * H + h) * cxs::kGroups + g;  // [Q, H, 16] row index
 #pragma unroll
   for (int c = 2 * cq; c < 2 * cq + 2; ++c) {
@@ -413,8 +439,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (mine) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        if (col0 + i < nc) mt = fmaxf(mt, v0[i]);
-        if (col0 + 32 + i < nc) mt = fmaxf(mt, v1[i]);
+        if (visible(col0 + i)) mt = fmaxf(mt, v0[i]);
+        if (visible(col0 + 32 + i)) mt = fmaxf(mt, v1[i]);
       }
     }
     red_max[cq * 128 + m] = mt;
@@ -426,8 +452,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (mine) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        if (col0 + i < nc) sum += tc::ex2(fmaf(v0[i], tc::kLog2e, -off));
-        if (col0 + 32 + i < nc) sum += tc::ex2(fmaf(v1[i], tc::kLog2e, -off));
+        if (visible(col0 + i)) sum += tc::ex2(fmaf(v0[i], tc::kLog2e, -off));
+        if (visible(col0 + 32 + i)) sum += tc::ex2(fmaf(v1[i], tc::kLog2e, -off));
       }
     }
     red_sum[cq * 128 + m] = sum;
@@ -466,7 +492,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc::ld32(s_addr + 64 * cq + 32 * half, v);
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          v[i] = col0 + i < nc ? tc::ex2(fmaf(v[i], tc::kLog2e, -offset)) : 0.f;
+          v[i] = visible(col0 + i) ? tc::ex2(fmaf(v[i], tc::kLog2e, -offset)) : 0.f;
         // P (bf16): 16-byte chunks 4 half .. 4 half + 3 of row m of sub-tile cq.
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -565,6 +591,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int p = a.positions[qq];
     const int current = p >= 0 ? p / a.BS : -1;
     const int limit = min(current, score_len);
+    const Gap row_gap = segment_gap(a, p);
     float* sc = scores + warp * score_len;
     int32_t* brow = a.blocks + ((long long)qq * H + h) * a.width;
     if (lane == 0) brow[0] = current >= 0 ? current : -1;
@@ -573,7 +600,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       best = 0;
       best_idx = 0xffffffffu;
       for (int i = lane; i < limit; i += 32) {
-        const uint32_t key = topn_key(sc[i]);
+        const uint32_t key = row_gap.hides(i) ? 0u : topn_key(sc[i]);
         if (key > best) {
           best = key;
           best_idx = i;
@@ -617,12 +644,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
-extern "C" int cxs_compressed_select(const void* query, const void* compressed, int32_t summaries,
-                                     const int32_t* positions, int32_t queries, int32_t heads,
-                                     int32_t block_size, int32_t count, int64_t total, void* out,
-                                     int32_t* blocks, float* scores, void* stream) {
+extern "C" int cxs_compressed_select_segments(
+    const void* query, const void* compressed, int32_t summaries, const int32_t* positions,
+    int32_t queries, int32_t heads, int32_t block_size, int32_t count, int64_t total,
+    int64_t segment_start, int64_t segment_tokens, void* out, int32_t* blocks, float* scores,
+    void* stream) {
   if (queries < 1 || heads < 1 || block_size < 1 || count < 1 || total < 1 || summaries < 0)
     return set_error(CXS_ERR_INVALID, "invalid compressed-select geometry");
+  if (segment_tokens < 0 || segment_start < 0 ||
+      (segment_tokens > 0 && (segment_start % block_size || segment_tokens % block_size ||
+                              segment_start + segment_tokens * (long long)queries > INT32_MAX)))
+    return set_error(CXS_ERR_INVALID,
+                     "segment_start / segment_tokens must be block multiples and fit int32");
   if (!query || !out || !blocks || !positions || (summaries > 0 && !compressed))
     return set_error(CXS_ERR_INVALID, "null compressed-select argument");
   if (((uintptr_t)compressed & 15) || ((uintptr_t)query & 15) || ((uintptr_t)out & 15))
@@ -653,6 +686,8 @@ extern "C" int cxs_compressed_select(const void* query, const void* compressed, 
   a.count = count;
   a.width = width;
   a.total = total;
+  a.seg_block = segment_tokens > 0 ? (int)(segment_start / block_size) : 0;
+  a.seg_blocks = (int)(segment_tokens / block_size);
   a.query = (const __nv_bfloat16*)query;
   a.positions = positions;
   a.out = (__nv_bfloat16*)out;
@@ -695,4 +730,13 @@ extern "C" int cxs_compressed_select(const void* query, const void* compressed, 
       map, a);
   CXS_LAUNCH_CHECK("compressed_select_kernel");
   return CXS_OK;
+}
+
+extern "C" int cxs_compressed_select(const void* query, const void* compressed, int32_t summaries,
+                                     const int32_t* positions, int32_t queries, int32_t heads,
+                                     int32_t block_size, int32_t count, int64_t total, void* out,
+                                     int32_t* blocks, float* scores, void* stream) {
+  return cxs_compressed_select_segments(query, compressed, summaries, positions, queries, heads,
+                                        block_size, count, total, 0, 0, out, blocks, scores,
+                                        stream);
 }

@@ -24,6 +24,7 @@ import torch.nn.functional as F
 
 from . import _lib, ops
 from .mempool import HiSparseCache, MemoryPool
+from .segments import SegmentLayout
 from .transport import GRSelectedTransport
 
 
@@ -130,6 +131,7 @@ class NSAExtendModel:
         self.fast = None          # fused-glue buffers of the user being served
         self.fast_states = {}     # user -> its fused-glue buffers (prepare_fast)
         self.probe, self.probe_counters = None, []
+        self.selections = None    # a list: eager fast steps append each layer's blocks
         self.users = {}
         self.counters = []
 
@@ -225,16 +227,28 @@ class NSAExtendModel:
         return self.forward(token_ids, positions, user, append=False)
 
     # -- fused-glue extend path (what the benchmark graph captures) ------------
-    def prepare_fast(self, extend_tokens, user="user"):
+    def prepare_fast(self, extend_tokens, user="user", candidates=1):
         """Persistent per-layer buffers for extend steps of ``extend_tokens`` tokens.
 
         Each layer gets a window buffer [kept + E, H, 128] whose first rows hold
         the retained history window and whose tail receives this step's K/V, a
         summaries buffer [C_hist + new, H, 128] and per-head current-KV buffers
         [H, E, 128]; the transport binds them in place (no staging copies).
+
+        ``candidates`` > 1 serves that many GR candidates of ``extend_tokens``
+        tokens each over the shared history in one step, each seeing only the
+        history and its own suffix (the candidate-segment layout of
+        ``cxs_attend_geometry``). The shared history ends at the last block
+        boundary; the history tail past it (fewer than BS tokens) is copied
+        once into the front of every candidate's segment, so each segment
+        holds tail + suffix, padded to whole blocks. History blocks are then
+        deduplicated across candidates, suffix blocks are candidate-private.
         """
         cfg, st, d = self.cfg, self.user(user), self.device
-        E = extend_tokens
+        E, n_cand, bs = extend_tokens, candidates, cfg.block_size
+        if n_cand < 1:
+            raise ValueError("candidates must be >= 1")
+        rows = E * n_cand
         kl, h0, gd = self.kv_local, self.head0, cfg.groups * cfg.head_dim
         for w in self.layers:
             if "qkvg" not in w:
@@ -245,6 +259,9 @@ class NSAExtendModel:
                                        w["g"][h0 * cfg.groups * 3:(h0 + kl) * cfg.groups * 3]]
                                       ).contiguous()
                 w["gate_up"] = torch.cat([w["gate"], w["up"]]).contiguous()
+        old = st.length
+        layout = SegmentLayout(old, E, n_cand, bs)
+        tail_len, start, seg_tokens = layout.tail, layout.start, layout.tokens
         layers = []
         for index in range(cfg.layers):
             kept = len(st.windows[index])
@@ -252,25 +269,61 @@ class NSAExtendModel:
             if tail > kept:
                 raise ValueError("window must retain the summary tail")
             c_hist = len(st.summaries[index])
-            new = (tail + E) // cfg.block_size
-            window_buf = torch.empty((kept + E, kl, 128), dtype=torch.bfloat16, device=d)
-            window_buf[:kept] = st.windows[index]
-            summaries = torch.empty((c_hist + new, kl, 128), dtype=torch.bfloat16, device=d)
-            summaries[:c_hist] = st.summaries[index]
-            current = torch.empty((kl, E, 128), dtype=torch.bfloat16, device=d)
+            new = (tail + E) // bs
             base = st.row + index * kl
-            fetches = [dict(row=base + h, cached_length=st.length, history_length=st.length,
+            if n_cand == 1:
+                window_buf = torch.empty((kept + E, kl, 128), dtype=torch.bfloat16, device=d)
+                window_buf[:kept] = st.windows[index]
+                summaries = torch.empty((c_hist + new, kl, 128), dtype=torch.bfloat16, device=d)
+                summaries[:c_hist] = st.summaries[index]
+                current = torch.empty((kl, E, 128), dtype=torch.bfloat16, device=d)
+                fetches = [dict(row=base + h, cached_length=old, history_length=old,
+                                current_kv=current[h]) for h in range(kl)]
+                layers.append(dict(kept=kept, tail=tail, c_hist=c_hist, new=new,
+                                   window_buf=window_buf, summaries=summaries, current=current,
+                                   fetches=fetches, window_start=old - kept))
+                continue
+            if tail != tail_len or c_hist * bs != start:
+                raise ValueError("layer state does not match the history length")
+            # Window buffer of a fixed length (W - 1 history records + the
+            # segments), the history right-aligned against the segments: users
+            # with different history lengths share workspace shapes. Records
+            # before the first kept one are never inside a window.
+            shared = kept - tail                            # window records below `start`
+            lead = cfg.window - 1
+            window_buf = torch.zeros((lead + n_cand * seg_tokens, kl, 128),
+                                     dtype=torch.bfloat16, device=d)
+            window_buf[lead - shared:lead] = st.windows[index][:shared]
+            segs = window_buf[lead:].view(n_cand, seg_tokens, kl, 128)
+            segs[:, :tail] = st.tails[index]
+            nsb = seg_tokens // bs
+            summaries = torch.zeros((c_hist + n_cand * nsb, kl, 128), dtype=torch.bfloat16,
+                                    device=d)
+            summaries[:c_hist] = st.summaries[index]
+            current = torch.zeros((kl, n_cand * seg_tokens, 128), dtype=torch.bfloat16,
+                                  device=d)
+            current.view(kl, n_cand, seg_tokens, 128)[:, :, :tail] = (
+                st.tails[index].permute(1, 0, 2)[:, None])
+            fetches = [dict(row=base + h, cached_length=start, history_length=start,
                             current_kv=current[h]) for h in range(kl)]
-            layers.append(dict(kept=kept, tail=tail, c_hist=c_hist, new=new,
+            layers.append(dict(kept=lead, tail=tail, c_hist=c_hist, new=new, nsb=nsb,
                                window_buf=window_buf, summaries=summaries, current=current,
-                               fetches=fetches, window_start=st.length - kept))
+                               fetches=fetches, window_start=start - lead))
+        r = torch.arange(rows, device=d)
+        true_positions = (old + r % E).to(torch.int32)
+        if n_cand == 1:
+            positions = true_positions
+        else:
+            positions = torch.tensor(layout.positions(), dtype=torch.int32, device=d)
         self.fast = self.fast_states[user] = dict(
-            E=E, user=user, layers=layers,
-            positions=torch.arange(st.length, st.length + E, device=d, dtype=torch.int32),
-            x=torch.empty((E, cfg.hidden), dtype=torch.bfloat16, device=d),
-            query=torch.empty((E, kl, cfg.groups, cfg.head_dim), dtype=torch.bfloat16, device=d),
-            gates=torch.empty((E, kl, cfg.groups, 3), dtype=torch.bfloat16, device=d),
-            mlp=torch.empty((E, cfg.ffn), dtype=torch.bfloat16, device=d))
+            E=rows, per_candidate=E, candidates=n_cand, user=user, layers=layers,
+            positions=positions, true_positions=true_positions, total=layout.total,
+            segments=layout.segments() if n_cand > 1 else None, layout=layout,
+            x=torch.empty((rows, cfg.hidden), dtype=torch.bfloat16, device=d),
+            query=torch.empty((rows, kl, cfg.groups, cfg.head_dim), dtype=torch.bfloat16,
+                              device=d),
+            gates=torch.empty((rows, kl, cfg.groups, 3), dtype=torch.bfloat16, device=d),
+            mlp=torch.empty((rows, cfg.ffn), dtype=torch.bfloat16, device=d))
         return self.fast
 
     def _layer_fast(self, index, hidden):
@@ -283,27 +336,45 @@ class NSAExtendModel:
         _lib.check(lib.cxs_rms_norm(hidden.data_ptr(), w["in_norm"].data_ptr(), x.data_ptr(), E,
                                     cfg.hidden, cfg.rms_eps, stream))
         proj = F.linear(x, w["qkvg"])
-        records = L["window_buf"][L["kept"]:]
         kl = self.kv_local
-        _lib.check(lib.cxs_qkv_rope(
-            proj.data_ptr(), proj.shape[1], positions.data_ptr(), self.inv_freq.data_ptr(), E,
-            kl * cfg.groups, kl, query.data_ptr(), records.data_ptr(),
-            kl * 128, L["current"].data_ptr(), E * 128, gates.data_ptr(), stream))
-        if L["new"]:
-            start = L["window_buf"][L["kept"] - L["tail"]:]
-            _lib.check(lib.cxs_block_summaries(
-                start.data_ptr(), L["tail"] + E, kl, cfg.block_size,
-                L["summaries"][L["c_hist"]:].data_ptr(), stream))
-        total = L["window_start"] + L["kept"] + E
+        segments = f["segments"]
+        if segments is None:
+            records = L["window_buf"][L["kept"]:]
+            _lib.check(lib.cxs_qkv_rope(
+                proj.data_ptr(), proj.shape[1], positions.data_ptr(), self.inv_freq.data_ptr(),
+                E, kl * cfg.groups, kl, query.data_ptr(), records.data_ptr(),
+                kl * 128, L["current"].data_ptr(), E * 128, gates.data_ptr(), stream))
+            if L["new"]:
+                start = L["window_buf"][L["kept"] - L["tail"]:]
+                _lib.check(lib.cxs_block_summaries(
+                    start.data_ptr(), L["tail"] + E, kl, cfg.block_size,
+                    L["summaries"][L["c_hist"]:].data_ptr(), stream))
+        else:
+            # Candidate c's suffix token i goes to row tail + i of segment c.
+            seg_tokens, tail, per = segments[1], L["tail"], f["per_candidate"]
+            records = L["window_buf"][L["kept"] + tail:]
+            current = L["current"][:, tail:]
+            _lib.check(lib.cxs_qkv_rope_segments(
+                proj.data_ptr(), proj.shape[1], f["true_positions"].data_ptr(),
+                self.inv_freq.data_ptr(), E, kl * cfg.groups, kl, query.data_ptr(),
+                records.data_ptr(), kl * 128, current.data_ptr(), L["current"].shape[1] * 128,
+                gates.data_ptr(), per, seg_tokens, stream))
+            if L["new"]:
+                ops.block_summaries_segments(
+                    L["window_buf"][L["kept"]:], tail + per, cfg.block_size,
+                    L["summaries"][L["c_hist"]:], f["candidates"], seg_tokens, L["nsb"])
         cmp_out, blocks = ops.compressed_attention_select(
-            query, L["summaries"], positions, total, cfg.block_size, cfg.block_counts)
+            query, L["summaries"], positions, f["total"], cfg.block_size, cfg.block_counts,
+            segments=segments)
+        if self.selections is not None:
+            self.selections.append(blocks)
         if self.probe is not None:  # comparison plan on the same selections / cache state
             self.probe_counters.append(self.probe.plan_only(
                 query, blocks, positions, L["fetches"], cfg.block_size, workspace_id=index))
         mixed, counters = self.transport.run(
             query, blocks, positions, L["fetches"], cfg.block_size, window=cfg.window,
             window_kv=L["window_buf"], window_start=L["window_start"], compressed=cmp_out,
-            gates=gates, workspace_id=index)
+            gates=gates, workspace_id=index, segments=segments)
         self.counters.append(counters)
         if self.exchange is not None:
             mixed = self.exchange(mixed)
@@ -337,14 +408,16 @@ class NSAExtendModel:
             self.cfg.hidden, self.cfg.rms_eps, torch.cuda.current_stream(self.device).cuda_stream))
         return out
 
-    def capture_extend(self, extend_tokens, user="user", warmup=2):
+    def capture_extend(self, extend_tokens, user="user", warmup=2, candidates=1):
         """Capture one extend forward of ``user`` in a CUDA graph with static
-        input/output. Graphs of several users may be replayed one after
+        input/output (``candidates`` x ``extend_tokens`` token rows, see
+        ``prepare_fast``). Graphs of several users may be replayed one after
         another on one stream: they share the transport's per-layer
         workspaces, which the transport keeps (pins) once a captured graph
         holds them."""
-        self.prepare_fast(extend_tokens, user)
-        static_ids = torch.zeros(extend_tokens, dtype=torch.int64, device=self.device)
+        self.prepare_fast(extend_tokens, user, candidates)
+        static_ids = torch.zeros(extend_tokens * candidates, dtype=torch.int64,
+                                 device=self.device)
         stream = torch.cuda.Stream(self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(stream):

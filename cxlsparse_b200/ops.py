@@ -14,9 +14,13 @@ from . import _lib
 
 
 def compressed_attention_select(query, compressed, positions, total, block_size, count, *,
-                                scores=None):
+                                scores=None, segments=None):
     """Compressed-token attention and top-n block ids; ``scores`` optionally
-    receives the [Q, H, C] fp32 block scores the selection was made from."""
+    receives the [Q, H, C] fp32 block scores the selection was made from.
+    ``segments=(segment_start, segment_tokens)`` selects over candidate
+    segments (positions, summaries and returned block ids in the segment
+    layout of ``cxs_attend_geometry``; ``total`` is one candidate's true
+    history + suffix length)."""
     queries, heads, groups, dim = query.shape
     if groups != 16 or dim != 64 or query.dtype != torch.bfloat16:
         raise ValueError("query must be bf16 [Q, H, 16, 64]")
@@ -31,10 +35,12 @@ def compressed_attention_select(query, compressed, positions, total, block_size,
     if scores is not None and scores.shape != (queries, heads, len(compressed)):
         raise ValueError("scores must be [Q, H, C] fp32")
     stream = torch.cuda.current_stream(query.device)
-    _lib.check(_lib.lib().cxs_compressed_select(
+    segment_start, segment_tokens = segments or (0, 0)
+    _lib.check(_lib.lib().cxs_compressed_select_segments(
         query.data_ptr(), compressed.data_ptr() if len(compressed) else None, len(compressed),
-        positions.data_ptr(), queries, heads, block_size, count, total, output.data_ptr(),
-        blocks.data_ptr(), _lib.ptr(scores), stream.cuda_stream))
+        positions.data_ptr(), queries, heads, block_size, count, total, segment_start,
+        segment_tokens, output.data_ptr(), blocks.data_ptr(), _lib.ptr(scores),
+        stream.cuda_stream))
     return output, blocks
 
 
@@ -49,6 +55,18 @@ def block_summaries(tokens, block_size):
                                                   tokens.shape[1], block_size, out.data_ptr(),
                                                   stream.cuda_stream))
     return out
+
+
+def block_summaries_segments(tokens, count, block_size, out, segments, token_stride,
+                             summary_stride):
+    """Summaries of ``segments`` runs of ``count`` records in one launch: run s
+    pools tokens[s * token_stride :][:count] into out[s * summary_stride :]
+    (tokens / out are [n, H, 128] bf16 buffers, written in place)."""
+    if count // block_size:
+        stream = torch.cuda.current_stream(tokens.device)
+        _lib.check(_lib.lib().cxs_block_summaries_segments(
+            tokens.data_ptr(), count, tokens.shape[1], block_size, out.data_ptr(), segments,
+            token_stride, summary_stride, stream.cuda_stream))
 
 
 def append_compressed(compressed, tail, current, block_size):

@@ -163,7 +163,8 @@ class GRSelectedTransport:
         return self._capacity_cache[bs]
 
     def _workspace(self, qb, heads, width, fetches, bs, window_shape, workspace_id=None):
-        logical = max(f["cached_length"] + qb for f in fetches)
+        # Candidate segments place suffix tokens up to cached + len(current_kv).
+        logical = max(f["cached_length"] + max(qb, len(f["current_kv"])) for f in fetches)
         map_blocks = max(64, math.ceil(logical / (64 * bs)) * 64)
         key = (qb, heads, width, bs, map_blocks, window_shape, workspace_id)
         if key in self.workspaces:
@@ -261,7 +262,7 @@ class GRSelectedTransport:
         b.gates = _lib.ptr(gates)
         w["binding"] = "direct"
 
-    def _execute(self, w, window_start, window, defer_hot=False):
+    def _execute(self, w, window_start, window, defer_hot=False, segments=(0, 0)):
         stream = torch.cuda.current_stream(self.cache.data.device)
         self.active_plan.plan(w, stream, defer_hot=defer_hot)
         geometry = _lib.AttendGeometry(
@@ -269,7 +270,8 @@ class GRSelectedTransport:
             physical=w["physical"], window=window if w["window_shape"] else 0,
             window_len=w["window_shape"][0] if w["window_shape"] else 0,
             gate=1 if w["window_shape"] else 0, window_start=window_start,
-            spin_limit=self.spin_limit)
+            spin_limit=self.spin_limit, segment_start=segments[0],
+            segment_tokens=segments[1])
         timing = self.kernel_timing is not None and not torch.cuda.is_current_stream_capturing()
         if timing:
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -283,9 +285,26 @@ class GRSelectedTransport:
     # -- main entry --------------------------------------------------------
     def run(self, query, blocks, positions, fetches, block_size, *, trace=False,
             window=None, window_kv=None, window_start=0, compressed=None, gates=None,
-            workspace_id=None):
+            workspace_id=None, segments=None):
+        """Reference ``run`` plus the fused branches and, optionally, candidate
+        segments: ``segments=(segment_start, segment_tokens)`` says that
+        ``positions``, ``blocks``, the window buffer and each fetch's
+        ``current_kv`` use the candidate-segment layout of
+        ``cxs_attend_geometry`` (every candidate sees the history below
+        ``segment_start`` and its own suffix only). The plan needs nothing
+        else: history blocks deduplicate across candidates, suffix blocks
+        stay private to their candidate. ``fetches[h]["cached_length"]`` and
+        ``history_length`` must then equal ``segment_start``."""
         if trace:
             raise ValueError("Collect device activity separately from GR timing")
+        segments = tuple(int(x) for x in segments) if segments else (0, 0)
+        if segments[1]:
+            if (segments[0] % block_size or segments[1] % block_size or segments[0] < 0
+                    or segments[1] < 0):
+                raise ValueError("segments must be (start, tokens) in whole blocks")
+            if any(f["cached_length"] != segments[0] or f["history_length"] != segments[0]
+                   for f in fetches):
+                raise ValueError("segmented fetches must cache exactly the shared history")
         if (query.ndim != 4 or blocks.ndim != 3 or query.shape[:2] != blocks.shape[:2]
                 or len(fetches) != query.shape[1] or positions.shape != (len(query),)
                 or blocks.dtype != torch.int32
@@ -363,23 +382,23 @@ class GRSelectedTransport:
         for f in fetches:
             f["current_kv"].record_stream(stream)
         if self.cuda_graphs:
-            graph_key = (window_start, window)
+            graph_key = (window_start, window, segments)
             if w.get("graph_key") != graph_key:
                 w.pop("graph", None)
-                self._execute(w, window_start, window)  # warm-up, then capture
+                self._execute(w, window_start, window, segments=segments)  # warm-up
                 graph = torch.cuda.CUDAGraph()
                 if self._capture_stream is None:
                     self._capture_stream = torch.cuda.Stream(device)
                 self._capture_stream.wait_stream(stream)
                 with torch.cuda.graph(graph, stream=self._capture_stream):
-                    self._execute(w, window_start, window)
+                    self._execute(w, window_start, window, segments=segments)
                 stream.wait_stream(self._capture_stream)
                 w["graph"], w["graph_key"] = graph, graph_key
                 self.captures += 1
             w["graph"].replay()
             self.replays += 1
         else:
-            self._execute(w, window_start, window, defer_hot=async_hot)
+            self._execute(w, window_start, window, defer_hot=async_hot, segments=segments)
         if workspace_id is None:
             counters = DeferredLayerCounters(w["stats"].clone(), 1, self.pool.backend,
                                              w["error"].clone())
@@ -410,7 +429,7 @@ class GRSelectedTransport:
             consumer="tma_bounded_rows", consumer_ctas=w["consumer_ctas"],
             io_policy="tma_block_ready", tma_copy="bulk_1d",
             partial_block_policy="external_token_gather", cpu_selection_downloads=0,
-            fused_branches=fused, workspace_allocations=self.workspace_allocations,
+            fused_branches=fused, segments=segments, workspace_allocations=self.workspace_allocations,
             workspace_evictions=self.workspace_evictions,
             workspace_bytes=sum(x["allocated_bytes"] for x in self.workspaces.values()),
             logical_block_capacity=w["map_blocks"], active_block_capacity=w["physical"],

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define CXS_ABI_VERSION 1
+#define CXS_ABI_VERSION 2
 
 enum cxs_status {
   CXS_OK = 0,
@@ -203,6 +203,22 @@ int cxs_plan_commit_hot(const cxs_plan_geometry* geometry, const cxs_plan_buffer
  * A preceding prepare kernel (same call) classifies block sources, gathers
  * resident blocks into the staging buffer and initialises ready flags.
  */
+/* Candidate segments. The reference packs every GR candidate into one suffix
+ * (worker/prompt.py:24-55), so candidates attend to each other's tokens.
+ * With segment_tokens > 0 several candidates instead share one history and
+ * each sees only the history and its own suffix:
+ *  - positions below segment_start (a multiple of the block size) are
+ *    history, shared by all candidates;
+ *  - candidate s's suffix token with true position segment_start + i sits at
+ *    position segment_start + s * segment_tokens + i (segment_tokens is a
+ *    multiple of the block size, at least the candidate's suffix length);
+ *  - a row whose position p lies in segment s > 0 sees history positions
+ *    below segment_start and its own segment up to p; segments 1..s-1 and
+ *    the start of segment 0 beyond the history are a gap it never reads.
+ * Blocks, summaries, window records and current KV use these positions,
+ * so the planner deduplicates history blocks across candidates and keeps
+ * each candidate's suffix blocks private without knowing about segments.
+ * The window branch covers the true positions (p_true - window, p_true]. */
 typedef struct cxs_attend_geometry {
   int32_t queries;      /* Q token rows */
   int32_t heads;        /* H */
@@ -212,8 +228,11 @@ typedef struct cxs_attend_geometry {
   int32_t window;       /* sliding window W_s (0: no window branch) */
   int32_t window_len;   /* records in the window buffer */
   int32_t gate;         /* 1: write the gate mix instead of the selected output */
-  int64_t window_start; /* absolute position of window record 0 */
+  int64_t window_start; /* absolute position of window record 0 (may be negative:
+                           records before position 0 are never in a window) */
   int64_t spin_limit;   /* clock cycles before a bounded wait gives up */
+  int64_t segment_start;  /* candidate segments (0, 0: one suffix): see below */
+  int64_t segment_tokens;
 } cxs_attend_geometry;
 
 typedef struct cxs_attend_buffers {
@@ -287,10 +306,30 @@ int cxs_compressed_select(const void* query,      /* [Q, H, 16, 64] bf16 */
                           float* scores,          /* [Q, H, C] or NULL */
                           void* stream);
 
+/* cxs_compressed_select over candidate segments (segment_start and
+ * segment_tokens as in cxs_attend_geometry, both multiples of block_size;
+ * 0, 0 is cxs_compressed_select). Summaries use segment positions: summary c
+ * covers positions [c * BS, (c + 1) * BS). A row of segment s skips the
+ * summaries of the gap, selects among its visible blocks and returns
+ * segment block ids; `total` is the true history + suffix length of one
+ * candidate (it fixes width). No counterpart in the reference. */
+int cxs_compressed_select_segments(const void* query, const void* compressed,
+                                   int32_t summaries, const int32_t* positions,
+                                   int32_t queries, int32_t heads, int32_t block_size,
+                                   int32_t count, int64_t total, int64_t segment_start,
+                                   int64_t segment_tokens, void* out, int32_t* blocks,
+                                   float* scores, void* stream);
+
 /* Mean-pool complete BS-token blocks of `tokens` records [n, H, 128] into
  * `summaries` [n / BS, H, 128] bf16 (models/nsa/ops.py:62-70). */
 int cxs_block_summaries(const void* tokens, int64_t count, int32_t heads, int32_t block_size,
                         void* summaries, void* stream);
+/* cxs_block_summaries for `segments` runs at once: run s pools the `count`
+ * records starting at tokens + s * token_stride records into summaries +
+ * s * summary_stride records (one launch for every candidate segment). */
+int cxs_block_summaries_segments(const void* tokens, int64_t count, int32_t heads,
+                                 int32_t block_size, void* summaries, int32_t segments,
+                                 int64_t token_stride, int64_t summary_stride, void* stream);
 
 /* ------------------------------------------------------- layer glue ---
  * Fused elementwise steps around the cuBLAS projections of one NSA layer,
@@ -309,6 +348,15 @@ int cxs_qkv_rope(const void* proj, int32_t proj_stride, const int32_t* positions
                  const float* inv_freq, int32_t tokens, int32_t q_heads, int32_t kv_heads,
                  void* query, void* records, int32_t records_stride, void* current,
                  int32_t current_stride, void* gates, void* stream);
+/* cxs_qkv_rope for candidate segments: token t writes its record and current
+ * KV at row (t / segment_rows) * segment_stride + t % segment_rows instead of
+ * row t (segment_rows = tokens per candidate, segment_stride = records per
+ * candidate segment); query and gates stay at row t. */
+int cxs_qkv_rope_segments(const void* proj, int32_t proj_stride, const int32_t* positions,
+                          const float* inv_freq, int32_t tokens, int32_t q_heads,
+                          int32_t kv_heads, void* query, void* records, int32_t records_stride,
+                          void* current, int32_t current_stride, void* gates,
+                          int32_t segment_rows, int32_t segment_stride, void* stream);
 /* out[r, c] = bf16(silu(gate_up[r, c])) * gate_up[r, ffn + c] (SwiGLU). */
 int cxs_silu_mul(const void* gate_up, int32_t rows, int32_t ffn, void* out, void* stream);
 

@@ -47,3 +47,44 @@ def test_users_replayed_back_to_back_match_their_eager_extends(cuda):
             assert sum(r[0]["misses"] + r[1]["misses"] for r in counts) > 0
     finally:
         model.close()
+
+
+def test_users_with_candidate_segments_replay_back_to_back(cuda):
+    """configs[3] with candidate segments: each user's request holds 2
+    candidates over that user's own jittered history; every user's captured
+    graph, replayed back to back with the others, reproduces that user's
+    eager segmented step bit for bit."""
+    cfg = NSAConfig(layers=2, hot=64)
+    histories = {"u0": 1000, "u1": 1337, "u2": 777}
+    extend, candidates = 64, 2
+    model = NSAExtendModel(cfg, device=cuda, seed=0, max_users=len(histories),
+                           max_history=max(histories.values()) + extend + 64, chunk=512,
+                           workspaces=cfg.layers * len(histories) + 4)
+    try:
+        g = torch.Generator().manual_seed(12)
+        ids = {}
+        for user, length in histories.items():
+            model.prefill(torch.randint(0, cfg.vocab, (length,), generator=g).to(cuda), user=user)
+            ids[user] = torch.randint(0, cfg.vocab, (candidates * extend,), generator=g).to(cuda)
+        eager = {}
+        for user in histories:
+            model.prepare_fast(extend, user, candidates)
+            eager[user] = model.extend_fast(ids[user]).clone()
+            torch.cuda.synchronize()
+            model.counters.clear()
+        graphs = {}
+        for user in histories:
+            graph, static_ids, static_out, counters = model.capture_extend(
+                extend, user=user, candidates=candidates)
+            static_ids.copy_(ids[user])
+            graphs[user] = (graph, static_out, counters, static_ids)
+        for _ in range(2):
+            for user in histories:
+                graphs[user][0].replay()
+            torch.cuda.synchronize()
+            for user in histories:
+                assert torch.equal(graphs[user][1], eager[user]), user
+        for user in histories:
+            assert sum(r["misses"] for c in graphs[user][2] for r in c.materialize()) > 0
+    finally:
+        model.close()
