@@ -62,6 +62,15 @@ def parse():
     p.add_argument("--jitter", type=int, default=1000)
     p.add_argument("--sigma", type=float, default=0.5)
     p.add_argument("--candidates", type=int, default=16)
+    p.add_argument("--hot-policy", default=None, choices=("frequency", "replica"),
+                   help="frequency: the reference's hot set (256 tokens per layer and KV "
+                        "head, refreshed every forward); replica: a static HBM replica of "
+                        "the most recent --replica-blocks blocks (+ --straddle half-resident "
+                        "blocks). Default: replica for headsplit (configs[4]), else frequency")
+    p.add_argument("--replica-blocks", type=int, default=256)
+    p.add_argument("--straddle", type=float, default=None,
+                   help="fraction of blocks made half resident (default 0.2 for headsplit, "
+                        "else 0)")
     p.add_argument("--packed", action="store_true",
                    help="pack several candidates into one suffix, as the reference does "
                         "(worker/prompt.py:24-55), instead of one segment per candidate")
@@ -71,6 +80,10 @@ def parse():
     args = p.parse_args()
     if args.history is None:
         args.history = {"serving": 32768, "headsplit": 131072}.get(args.workload, 16384)
+    if args.hot_policy is None:
+        args.hot_policy = "replica" if args.workload == "headsplit" else "frequency"
+    if args.straddle is None:
+        args.straddle = 0.2 if args.workload == "headsplit" else 0.0
     return args
 
 
@@ -199,13 +212,26 @@ def run_reference(args):
     }))
 
 
+def hot_config(args):
+    if args.hot_policy == "frequency":
+        return "256 tokens per (layer, kv head), reference frequency policy"
+    return (f"static HBM replica: most recent {args.replica_blocks} blocks of 64 tokens "
+            f"per (layer, kv head), {args.straddle:.0%} of blocks half resident "
+            f"(mixed-source gather)")
+
+
+def model_options(args):
+    return dict(hot_policy=args.hot_policy, replica_blocks=args.replica_blocks,
+                straddle=args.straddle)
+
+
 def workload(args):
     return {"workload": f"BASELINE configs[1]: NSA-1B-shaped extend, H={args.history}, "
                         f"E={args.extend}, 1 user per GPU",
             "history": args.history, "extend": args.extend, "layers": args.layers,
             "hidden": 2048, "heads": "32q/2kv", "block_size": 64, "top_n": 16,
             "window": 512, "compression": "mean pooling, block = stride = 64",
-            "hot": "256 tokens per (layer, kv head), reference frequency policy",
+            "hot": hot_config(args),
             "pool": "NUMA-local pinned host memory, cudaHostRegister mapped",
             "read_order": args.read_order,
             "l2": "inputs larger than L2: 1.4 GB of weights stream per step",
@@ -224,7 +250,7 @@ def run_ours(args):
 
     cfg = NSAConfig(layers=args.layers)
     model = NSAExtendModel(cfg, device=device, seed=0, max_history=args.history + args.extend,
-                           read_order=args.read_order)
+                           read_order=args.read_order, **model_options(args))
     g = torch.Generator().manual_seed(1000 + rank)
     history = torch.randint(0, cfg.vocab, (args.history,), generator=g).to(device)
     candidates = torch.randint(0, cfg.vocab, (args.extend,), generator=g)
@@ -459,7 +485,7 @@ def run_serving(args):
     model = NSAExtendModel(cfg, device=device, seed=0, max_users=len(mine),
                            max_history=max(lengths[u] for u in mine) + suffix + 64 * segments,
                            read_order=args.read_order,
-                           workspaces=cfg.layers * len(mine) + 4)
+                           workspaces=cfg.layers * len(mine) + 4, **model_options(args))
     t0 = time.perf_counter()
     candidates = {}
     for u in mine:
@@ -556,7 +582,7 @@ def run_serving(args):
                        "users": users_total, "users_per_gpu": args.users_per_gpu,
                        "history_lengths_rank0": [lengths[u] for u in mine],
                        "layers": args.layers, "block_size": 64, "top_n": 16, "window": 512,
-                       "hot": "256 tokens per (layer, kv head), reference frequency policy",
+                       "hot": hot_config(args),
                        "pool": "per-GPU NUMA-local pinned host slice",
                        "parallelism": f"users round-robin over {world} GPU(s)"},
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s",
@@ -617,7 +643,8 @@ def run_headsplit(args):
                            max_history=args.history + suffix + 64 * segments,
                            read_order=args.read_order,
                            workspaces=cfg.layers * len(mine) + 4, head_shard=(shard, shards),
-                           exchange=head_exchange(group, shards) if shards > 1 else None)
+                           exchange=head_exchange(group, shards) if shards > 1 else None,
+                           **model_options(args))
     t0 = time.perf_counter()
     candidates = {}
     for u in mine:
@@ -707,7 +734,7 @@ def run_headsplit(args):
                                    f"{args.queries} queries x E={args.extend} per user",
                        "users": users_total, "pairs": pairs, "kv_heads_per_gpu": model.kv_local,
                        "layers": args.layers, "block_size": 64, "top_n": 16, "window": 512,
-                       "hot": "256 tokens per (layer, kv head), reference frequency policy",
+                       "hot": hot_config(args),
                        "exchange": "NCCL all-gather of the [E, 16, 64] attention output per "
                                    "layer within the pair (inside the captured graph)",
                        "parallelism": f"{pairs} pair(s) x 2 KV-head shards" if shards > 1

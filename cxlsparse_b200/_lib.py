@@ -51,7 +51,7 @@ PLAN_BUFFER_FIELDS = (
     "stats", "address", "hbm", "valid", "starts", "flags", "slots", "ioids", "ranks",
     "missing", "all_ids", "all_counts", "row_positions", "region_counts", "row_depth",
     "first_depth", "near_consumers", "chosen", "private_required",
-    "private_occurrences", "canonical",
+    "private_occurrences", "canonical", "hbm_locs",
 )
 
 

@@ -227,11 +227,14 @@ __global__ void addresses_kernel(Geo g, cxs_plan_buffers b) {
   int row = (int)b.desc[h * 5];
   int old = (int)b.desc[h * 5 + 1];
   long long pointer = b.desc[h * 5 + 3];
+  // With a residency table every history token is looked up directly; the
+  // hot hash is only built from the tags otherwise.
+  const int32_t* table = b.hbm_locs ? b.hbm_locs + (long long)row * g.MAXH : nullptr;
   for (int i = threadIdx.x; i < g.HASH; i += blockDim.x) hkeys[i] = -1;
   __syncthreads();
   const int32_t* tags = b.tags + (long long)row * (g.HOT + 1);
   const int32_t* locs = b.locs + (long long)row * (g.HOT + 1);
-  for (int i = threadIdx.x; i < g.HOT; i += blockDim.x) {
+  for (int i = threadIdx.x; i < (table ? 0 : g.HOT); i += blockDim.x) {
     int token = tags[i];
     if (token < 0 || token >= old) continue;
     uint32_t s = hash_slot(token, g.HASH - 1);
@@ -262,7 +265,9 @@ __global__ void addresses_kernel(Geo g, cxs_plan_buffers b) {
     bool valid = active && o < req;
     bool previous = valid && token < old;
     int location = -1;
-    if (previous) {
+    if (previous && table) {
+      location = token < g.MAXH ? table[token] : -1;
+    } else if (previous) {
       uint32_t s = hash_slot((int)token, g.HASH - 1);
       for (int probe = 0; probe < g.HASH; ++probe) {
         int key = hkeys[s];
@@ -1054,11 +1059,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const int row = (int)b.desc[h * 5];
       const int old = (int)b.desc[h * 5 + 1];
       const long long pointer = b.desc[h * 5 + 3];
+      const int32_t* table = b.hbm_locs ? b.hbm_locs + (long long)row * g.MAXH : nullptr;
       for (int i = threadIdx.x; i < g.HASH; i += kFusedThreads) hkeys[i] = -1;
       __syncthreads();
       const int32_t* tags = b.tags + (long long)row * (g.HOT + 1);
       const int32_t* locs = b.locs + (long long)row * (g.HOT + 1);
-      for (int i = threadIdx.x; i < g.HOT; i += kFusedThreads) {
+      for (int i = threadIdx.x; i < (table ? 0 : g.HOT); i += kFusedThreads) {
         const int token = tags[i];
         if (token < 0 || token >= old) continue;
         uint32_t s = hash_slot(token, g.HASH - 1);
@@ -1104,7 +1110,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           const bool previous = valid && token < old;
           location[t] = -1;
           source[t] = -1;
-          if (previous) {
+          if (previous && table) {
+            location[t] = token < g.MAXH ? table[token] : -1;
+            if (location[t] < 0 && token < g.MAXH)
+              source[t] = b.host_locs[(long long)row * g.MAXH + token];
+          } else if (previous) {
             uint32_t s = hash_slot((int)token, g.HASH - 1);
             for (int probe = 0; probe < g.HASH; ++probe) {
               const int key = hkeys[s];

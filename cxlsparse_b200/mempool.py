@@ -209,6 +209,40 @@ class HiSparseCache:
         self.has_last_use = True
         self.planner_calls = 0
         self.bound_lengths = [0] * rows
+        self.replica_locs = None  # optional residency table (enable_replica)
+        self.replica = None
+        self.replica_used = 0
+
+    def enable_replica(self, capacity):
+        """A static HBM replica of up to ``capacity`` history tokens with a
+        per-token residency table ``replica_locs[row, token]`` (replica slot
+        or -1). Unlike the hot hash (at most ``hot`` tokens per row, refreshed
+        by the frequency policy), the table holds any residency pattern of
+        any size: the most recent N blocks, interleaved or partly resident
+        blocks. Not in the reference, whose replica is the hot hash."""
+        device = self.data.device
+        self.replica_locs = torch.full((self.rows, self.max_history), -1, dtype=torch.int32,
+                                       device=device)
+        self.replica = torch.zeros((max(1, capacity), self.dim), dtype=torch.bfloat16,
+                                   device=device)
+        self.replica_used = 0
+
+    def replicate(self, row, tokens, records):
+        """Make history ``tokens`` (device int64 [n]) of ``row`` resident in the
+        replica with their KV ``records`` [n, dim]."""
+        n = len(tokens)
+        if self.replica_locs is None or self.replica_used + n > len(self.replica):
+            raise ValueError("replica disabled or full")
+        if not n:
+            return
+        stream = torch.cuda.current_stream(self.data.device)
+        stream.wait_event(self.last_use)
+        slots = torch.arange(self.replica_used, self.replica_used + n, dtype=torch.int32,
+                             device=self.data.device)
+        self.replica[slots.long()] = records
+        self.replica_locs[row, tokens] = slots
+        self.replica_used += n
+        self.last_use.record(stream)
 
     def bind(self, row, slots):
         stream = torch.cuda.current_stream(self.data.device)

@@ -78,13 +78,45 @@ def rotary(query, key, positions, inv_freq):
     return rotate(query), rotate(key)
 
 
+def residency_pattern(history, block_size, recent_blocks, straddle=0.0, seed=0):
+    """Which history tokens the static HBM replica holds (bool [history]).
+
+    The most recent ``recent_blocks`` blocks are resident; then a seeded
+    ``straddle`` fraction of all blocks is made half resident, so that their
+    tokens come from two tiers: such a block inside the recent region loses
+    its first half, one outside gains its second half. Selected blocks of
+    the second kind go through the mixed-source token gather.
+    """
+    bs = block_size
+    resident = torch.zeros(history, dtype=torch.bool)
+    first = max(0, history - recent_blocks * bs)
+    resident[first:] = True
+    blocks = -(-history // bs)
+    count = int(round(straddle * blocks))
+    if count:
+        g = torch.Generator().manual_seed(seed)
+        for b in torch.randperm(blocks, generator=g)[:count].tolist():
+            lo, mid, hi = b * bs, b * bs + bs // 2, min(history, (b + 1) * bs)
+            if lo >= first:
+                resident[lo:min(mid, hi)] = False
+            else:
+                resident[mid:hi] = True
+    return resident
+
+
 class NSAExtendModel:
-    """Random-init NSA model whose attention runs on the B200 selected path."""
+    """Random-init NSA model whose attention runs on the B200 selected path.
+
+    ``hot_policy``: "frequency" (the reference's hot set: the ``hot`` most
+    frequently selected tokens of the last forward per layer and KV head),
+    "static" (hot set left as is) or "replica" (a static HBM replica holding
+    ``residency_pattern(H, BS, replica_blocks, straddle)`` of every history,
+    filled during prefill, looked up through a per-token table)."""
 
     def __init__(self, cfg=None, *, device="cuda", seed=0, max_users=1, max_history=16384,
                  hot_policy="frequency", read_order="consumption_depth",
                  cross_query_dedup=True, pool_regions=1, chunk=1024, workspaces=None,
-                 head_shard=(0, 1), exchange=None):
+                 head_shard=(0, 1), exchange=None, replica_blocks=256, straddle=0.0):
         self.cfg = cfg = cfg or NSAConfig()
         self.device = torch.device(device)
         # KV-head sharding (BASELINE configs[4]): this instance owns KV heads
@@ -125,6 +157,13 @@ class NSAExtendModel:
         self.cache = HiSparseCache(self.pool, rows=max_users * cfg.layers * self.kv_local,
                                    max_history=max_history, hot=cfg.hot,
                                    topk=min(cfg.hot, 256), dim=128)
+        self.replica_blocks, self.straddle = replica_blocks, straddle
+        self.resident = None  # residency pattern of the history being prefilled
+        if hot_policy == "replica":
+            bs = cfg.block_size
+            per_row = min(max_history, replica_blocks * bs
+                          + int(straddle * math.ceil(max_history / bs) + 1) * bs)
+            self.cache.enable_replica(self.cache.rows * per_row)
         self.transport = GRSelectedTransport(
             self.cache, read_order=read_order, cross_query_dedup=cross_query_dedup,
             hot_policy=hot_policy, capacity=workspaces or cfg.layers + 4, async_hot=True)
@@ -191,10 +230,17 @@ class NSAExtendModel:
         """Persist this chunk as history: pool write, slot table, summaries, window."""
         cfg = self.cfg
         old = st.length
+        chosen = None
+        if self.resident is not None:
+            chosen = self.resident[old:old + len(records)].nonzero().flatten()
         for h in range(self.kv_local):
             slots = self.pool.token_slots(st.pages[index][h], old, old + len(records))
             self.pool.write_many(slots, records[:, h].contiguous(), asynchronous=True)
             self.cache.append_slots(st.row + index * self.kv_local + h, old, slots)
+            if chosen is not None and len(chosen):
+                self.cache.replicate(st.row + index * self.kv_local + h,
+                                     (chosen + old).to(self.device),
+                                     records[chosen.to(self.device), h])
         st.summaries[index], st.tails[index] = compressed, tail
         st.windows[index] = window_kv[max(0, len(window_kv) - cfg.window + 1):].clone()
 
@@ -210,13 +256,21 @@ class NSAExtendModel:
         return rms_norm(hidden, self.final_norm, self.cfg.rms_eps)
 
     def prefill(self, token_ids, user="user"):
-        """Push a history through the model chunk by chunk, persisting its KV."""
+        """Push a history through the model chunk by chunk, persisting its KV
+        (and, with the replica policy, the resident part into the replica)."""
         st = self.user(user)
+        if self.cache.replica_locs is not None:
+            if st.length:
+                raise ValueError("the replica policy fills a history in one prefill")
+            self.resident = residency_pattern(len(token_ids), self.cfg.block_size,
+                                              self.replica_blocks, self.straddle,
+                                              seed=st.row)
         for begin in range(0, len(token_ids), self.chunk):
             ids = token_ids[begin:begin + self.chunk]
             positions = torch.arange(st.length, st.length + len(ids), device=self.device)
             self.forward(ids, positions, user, append=True)
             self.counters.clear()
+        self.resident = None
         self.pool.flush_read_stats()
         torch.cuda.synchronize(self.device)
 
@@ -445,8 +499,9 @@ class NSAExtendModel:
         """One eager extend step that also plans each layer query-privately
         (reference QueryPrivatePlanAdapter semantics) on the same selections
         and cache state; returns (dedup misses, private misses) in tokens."""
+        policy = "replica" if self.cache.replica_locs is not None else "static"
         self.probe = GRSelectedTransport(self.cache, cross_query_dedup=False,
-                                         read_order="physical", hot_policy="static",
+                                         read_order="physical", hot_policy=policy,
                                          capacity=self.cfg.layers + 2)
         self.probe_counters, self.counters = [], []
         try:

@@ -23,13 +23,18 @@ class ActivePlanAdapter:
 
     private = False
 
-    def __init__(self, cache, *, read_order="consumption_depth"):
+    def __init__(self, cache, *, read_order="consumption_depth", residency_table=False):
         if read_order not in _lib.READ_ORDERS:
             raise ValueError("Invalid NSA read priority configuration")
         if cache.hot < 1:
             raise ValueError("Positive hot capacity is required")
+        if residency_table and cache.replica_locs is None:
+            raise ValueError("residency_table needs cache.enable_replica()")
         self.cache, self.pool = cache, cache.pool
         self.read_order = read_order
+        # True: residency from the cache's per-token table (cache.replica /
+        # replica_locs) instead of the hot tags.
+        self.residency_table = residency_table
 
     # planning/active.py:517-552
     def geometry(self, queries, heads, width, fetches, bs, *, map_blocks=None):
@@ -120,10 +125,13 @@ class ActivePlanAdapter:
 
     def bind(self, w, blocks, positions, desc, bases):
         """Fill the C buffer table for these (static) input tensors."""
+        table = self.residency_table
         names = dict(
             blocks=blocks, positions=positions, desc=desc, bases=bases,
             tags=self.cache.tags, locs=self.cache.locs, host_locs=self.cache.host_locs,
-            hot_data=self.cache.data, row_positions=w["positions"])
+            hot_data=self.cache.replica if table else self.cache.data,
+            hbm_locs=self.cache.replica_locs if table else None,
+            row_positions=w["positions"])
         fields = {}
         for field in _lib.PLAN_BUFFER_FIELDS:
             tensor = names.get(field, w.get(field))

@@ -99,8 +99,8 @@ class GRSelectedTransport:
                  async_hot=False):
         if read_order not in _lib.READ_ORDERS:
             raise ValueError("Invalid NSA read priority configuration")
-        if hot_policy not in ("frequency", "static"):
-            raise ValueError("hot_policy must be 'frequency' or 'static'")
+        if hot_policy not in ("frequency", "static", "replica"):
+            raise ValueError("hot_policy must be 'frequency', 'static' or 'replica'")
         if query_group != 1:
             raise ValueError("Only single-token consumers (query_group=1) are supported")
         if capacity < 1 or workspace_bytes < 1:
@@ -110,7 +110,10 @@ class GRSelectedTransport:
         self.read_order, self.cross_query_dedup = read_order, cross_query_dedup
         self.hot_policy, self.spin_limit = hot_policy, spin_limit
         adapter = ActivePlanAdapter if cross_query_dedup else QueryPrivatePlanAdapter
-        self.active_plan = adapter(cache, read_order=read_order)
+        # "replica": residency from the cache's static per-token table
+        # (HiSparseCache.enable_replica); like "static", nothing is committed.
+        self.active_plan = adapter(cache, read_order=read_order,
+                                   residency_table=hot_policy == "replica")
         self.cuda_graphs, self.capacity = cuda_graphs, capacity
         self.workspace_budget = workspace_bytes
         self.workspaces = OrderedDict()

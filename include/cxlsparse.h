@@ -156,6 +156,13 @@ typedef struct cxs_plan_buffers {
   int32_t* private_required;    /* [H, CAP] */
   int32_t* private_occurrences; /* [R, W] */
   int32_t* canonical;           /* [H, sort_extent] */
+  /* optional HBM residency table (NULL: the hot tags/locs hash). When set,
+   * history token t of cache row r is resident at hot_data +
+   * hbm_locs[r * max_history + t] * 256 if that entry is >= 0, else it comes
+   * from the backing pool; tags/locs are not read. Any residency pattern
+   * (a recency window of any size, interleaved or partial blocks) is a
+   * table. No counterpart in the reference, whose replica is the hot hash. */
+  const int32_t* hbm_locs;      /* [rows, max_history] */
 } cxs_plan_buffers;
 
 

@@ -65,8 +65,12 @@ def _hot_lookup(tags, locs, row, old, hot):
 
 
 def _resolve(geo, keys_by_head, counts, required, desc, tags, locs, host_locs,
-             hot_data, bases, pool_tokens, page_size, stats, region_counts):
-    """Per-token source resolution (active.py:209-295)."""
+             hot_data, bases, pool_tokens, page_size, stats, region_counts, hbm_locs=None):
+    """Per-token source resolution (active.py:209-295).
+
+    ``hbm_locs`` [rows, max_history] (optional, not in the reference) replaces
+    the hot tags: history token t of row r is resident at hot_data +
+    hbm_locs[r, t] * 256 when that entry is >= 0."""
     heads, cap, bs, hot = geo["heads"], geo["per_head"], geo["bs"], geo["hot"]
     p_total = heads * cap
     address = np.zeros((p_total, bs), np.int64)
@@ -80,7 +84,11 @@ def _resolve(geo, keys_by_head, counts, required, desc, tags, locs, host_locs,
     for h in range(heads):
         row, old = int(desc[h, 0]), int(desc[h, 1])
         pointer = int(desc[h, 3])
-        table = _hot_lookup(tags, locs, row, old, hot)
+        if hbm_locs is None:
+            table = _hot_lookup(tags, locs, row, old, hot)
+        else:
+            table = {t: int(hbm_locs[row, t]) for t in range(min(old, hbm_locs.shape[1]))
+                     if hbm_locs[row, t] >= 0}
         for c in range(cap):
             p = h * cap + c
             active = c < counts[h]
@@ -200,7 +208,7 @@ def hot_choice(frequencies, hot):
 
 def active_plan(blocks, positions, desc, tags, locs, host_locs, hot_data, bases,
                 *, bs, hot, map_blocks, pool_tokens, page_size, consumer_ctas=None,
-                read_order="consumption_depth"):
+                read_order="consumption_depth", hbm_locs=None):
     """Full deduplicating plan; returns a dict of reference-workspace arrays.
 
     ``blocks`` [Q, H, W] int32, ``positions`` [Q] (negative = padded row).
@@ -264,7 +272,7 @@ def active_plan(blocks, positions, desc, tags, locs, host_locs, hot_data, bases,
     region_counts = np.zeros(len(bases), np.int64)
     address, hbm, slots, valid, starts, flags = _resolve(
         geo, keys, counts, required, desc, tags, locs, host_locs, hot_data, bases,
-        pool_tokens, page_size, stats, region_counts)
+        pool_tokens, page_size, stats, region_counts, hbm_locs)
     # Occurrence rows (occurrences.py:7-35): original order, duplicates kept.
     rows = q_count * heads
     all_ids = np.full((rows, width), -1, np.int32)
@@ -350,7 +358,7 @@ def retain_hot(plan, desc, tags, locs, *, bs, hot):
 
 def private_plan(blocks, positions, desc, tags, locs, host_locs, hot_data, bases,
                  *, bs, hot, map_blocks, pool_tokens, page_size,
-                 consumer_ctas=None, read_order="consumption_depth"):
+                 consumer_ctas=None, read_order="consumption_depth", hbm_locs=None):
     """Query-private (no cross-row sharing) plan (planning/query_private.py:29-457).
 
     Each (row query, head, block) owns a payload slot; repeats inside one query
@@ -415,7 +423,7 @@ def private_plan(blocks, positions, desc, tags, locs, host_locs, hot_data, bases
     region_counts = np.zeros(len(bases), np.int64)
     address, hbm, slots, valid, starts, flags = _resolve(
         geo, keys, counts, required, desc, tags, locs, host_locs, hot_data, bases,
-        pool_tokens, page_size, stats, region_counts)
+        pool_tokens, page_size, stats, region_counts, hbm_locs)
     rows = q_count * heads
     all_ids = np.full((rows, width), -1, np.int32)
     all_counts = np.zeros(rows, np.int32)
