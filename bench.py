@@ -68,6 +68,9 @@ def parse():
                         "the most recent --replica-blocks blocks (+ --straddle half-resident "
                         "blocks). Default: replica for headsplit (configs[4]), else frequency")
     p.add_argument("--replica-blocks", type=int, default=256)
+    p.add_argument("--compression", default="mean", choices=("mean", "mlp"),
+                   help="mean: the reference's mean-pooled block summaries; mlp: BASELINE's "
+                        "NSA params (32/16 MLP compression, block 0 + 2 local blocks forced)")
     p.add_argument("--straddle", type=float, default=None,
                    help="fraction of blocks made half resident (default 0.2 for headsplit, "
                         "else 0)")
@@ -220,6 +223,21 @@ def hot_config(args):
             f"(mixed-source gather)")
 
 
+def nsa_config(args):
+    from cxlsparse_b200.model import NSAConfig
+
+    if args.compression == "mlp":
+        return NSAConfig.baseline(layers=args.layers)
+    return NSAConfig(layers=args.layers)
+
+
+def compression_config(args):
+    if args.compression == "mlp":
+        return ("MLP over 32-token windows at stride 16, selection scores aggregated over the "
+                "overlapping windows, block 0 + 2 local blocks forced (BASELINE NSA params)")
+    return "mean pooling, block = stride = 64 (reference geometry)"
+
+
 def model_options(args):
     return dict(hot_policy=args.hot_policy, replica_blocks=args.replica_blocks,
                 straddle=args.straddle)
@@ -230,7 +248,7 @@ def workload(args):
                         f"E={args.extend}, 1 user per GPU",
             "history": args.history, "extend": args.extend, "layers": args.layers,
             "hidden": 2048, "heads": "32q/2kv", "block_size": 64, "top_n": 16,
-            "window": 512, "compression": "mean pooling, block = stride = 64",
+            "window": 512, "compression": compression_config(args),
             "hot": hot_config(args),
             "pool": "NUMA-local pinned host memory, cudaHostRegister mapped",
             "read_order": args.read_order,
@@ -248,7 +266,7 @@ def run_ours(args):
     from cxlsparse_b200.model import NSAConfig, NSAExtendModel
     from cxlsparse_b200.sharding import gather_scores
 
-    cfg = NSAConfig(layers=args.layers)
+    cfg = nsa_config(args)
     model = NSAExtendModel(cfg, device=device, seed=0, max_history=args.history + args.extend,
                            read_order=args.read_order, **model_options(args))
     g = torch.Generator().manual_seed(1000 + rank)
@@ -416,7 +434,7 @@ def run_dedup(args):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    cfg = NSAConfig(layers=args.layers)
+    cfg = nsa_config(args)
     E = args.candidates * 128
     segments = 1 if args.packed else args.candidates
     model = NSAExtendModel(cfg, device=device, seed=0,
@@ -473,7 +491,7 @@ def run_serving(args):
     world, rank, local = dist_setup(torch)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    cfg = NSAConfig(layers=args.layers)
+    cfg = nsa_config(args)
     users_total = args.users_per_gpu * world
     jitter = torch.Generator().manual_seed(3000)
     lengths = [args.history + int(torch.randint(-args.jitter, args.jitter + 1, (1,),
@@ -582,6 +600,7 @@ def run_serving(args):
                        "users": users_total, "users_per_gpu": args.users_per_gpu,
                        "history_lengths_rank0": [lengths[u] for u in mine],
                        "layers": args.layers, "block_size": 64, "top_n": 16, "window": 512,
+                       "compression": compression_config(args),
                        "hot": hot_config(args),
                        "pool": "per-GPU NUMA-local pinned host slice",
                        "parallelism": f"users round-robin over {world} GPU(s)"},
@@ -634,7 +653,7 @@ def run_headsplit(args):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     group, shard, shards, pair, pairs = head_pair_groups(world)
-    cfg = NSAConfig(layers=args.layers)
+    cfg = nsa_config(args)
     users_total = args.users_per_pair * pairs
     mine = users_for_rank(list(range(users_total)), pair, pairs)
     suffix = args.queries * args.extend
@@ -734,6 +753,7 @@ def run_headsplit(args):
                                    f"{args.queries} queries x E={args.extend} per user",
                        "users": users_total, "pairs": pairs, "kv_heads_per_gpu": model.kv_local,
                        "layers": args.layers, "block_size": 64, "top_n": 16, "window": 512,
+                       "compression": compression_config(args),
                        "hot": hot_config(args),
                        "exchange": "NCCL all-gather of the [E, 16, 64] attention output per "
                                    "layer within the pair (inside the captured graph)",

@@ -66,6 +66,12 @@ class AttendGeometry(ctypes.Structure):
             "window_start", "spin_limit", "segment_start", "segment_tokens")]
 
 
+class SelectGeometry(ctypes.Structure):
+    _fields_ = [(name, c_i32) for name in (
+        "queries", "heads", "block_size", "count", "summaries", "window", "stride",
+        "forced")] + [(name, c_i64) for name in ("total", "segment_start", "segment_tokens")]
+
+
 ATTEND_BUFFER_FIELDS = (
     "query", "kv", "all_ids", "all_counts", "row_positions", "starts", "valid", "flags",
     "ioids", "missing", "address", "sources", "kinds", "ready", "control", "error",
@@ -121,6 +127,10 @@ def lib():
             "cxs_compressed_select_segments": (c_i32, [c_vp, c_vp, c_i32, c_vp, c_i32, c_i32,
                                                        c_i32, c_i32, c_i64, c_i64, c_i64, c_vp,
                                                        c_vp, c_vp, c_vp]),
+            "cxs_compressed_select_nsa": (c_i32, [ctypes.POINTER(SelectGeometry), c_vp, c_vp,
+                                                  c_vp, c_vp, c_vp, c_vp, c_vp]),
+            "cxs_select_score_columns": (c_i32, [ctypes.POINTER(SelectGeometry),
+                                                 ctypes.POINTER(c_i32)]),
             "cxs_block_summaries": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
             "cxs_block_summaries_segments": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_i32,
                                                      c_i64, c_i64, c_vp]),
@@ -172,5 +182,6 @@ def exported_symbols():
             "cxs_plan_select_commit_hot", "cxs_plan_commit_hot",
             "cxs_fetch_attend", "cxs_attend_capacity", "cxs_fetch_attend_noalloc",
             "cxs_compressed_select", "cxs_compressed_select_segments",
+            "cxs_compressed_select_nsa", "cxs_select_score_columns",
             "cxs_block_summaries", "cxs_block_summaries_segments", "cxs_rms_norm",
             "cxs_qkv_rope", "cxs_qkv_rope_segments", "cxs_silu_mul")

@@ -44,6 +44,11 @@ int* g_select_error_address[kMaxDevices] = {nullptr};
 struct SelectArgs {
   int Q, H, C, BS, count, width, score_len;
   int seg_block, seg_blocks;  // candidate segments in blocks (seg_blocks 0: one suffix)
+  int seg_key, seg_keys;      // the same in compressed-key slots
+  int cmp_block, cmp_stride;  // compressed window l and stride d (key i: [i d, i d + l))
+  int identity;               // l == d == BS: key i is block i (the reference geometry)
+  int forced;                 // 1: previous block and block 0 follow the current block
+  int nb, nb_len;             // block-score columns (non-identity), padded length
   long long total;
   const __nv_bfloat16* query;
   const int32_t* positions;
@@ -53,24 +58,110 @@ struct SelectArgs {
   int* error;
 };
 
-// Blocks [lo, hi) a row at `pos` never sees: for a row of candidate segment
-// s > 0, the segments before its own (and the part of segment 0 past the
-// history); empty otherwise.
+// What one query row sees. Positions, block ids and key slots use the
+// candidate-segment layout when seg_blocks > 0: history below seg_block (key
+// slots below seg_key) is shared, candidate s owns seg_blocks blocks (seg_keys
+// key slots) after it, and a row of candidate s > 0 never sees the segments
+// before its own (the gaps). Without segments the row sees keys [0, nc).
 struct Gap {
   int lo = 0, hi = 0;
   __device__ __forceinline__ bool hides(int c) const { return c >= lo && c < hi; }
 };
 
-__device__ __forceinline__ Gap segment_gap(const SelectArgs& a, int pos) {
-  Gap gap;
-  if (a.seg_blocks > 0 && pos >= 0) {
-    const int s = (pos / a.BS - a.seg_block) / a.seg_blocks;
-    if (pos / a.BS >= a.seg_block && s > 0) {
-      gap.lo = a.seg_block;
-      gap.hi = a.seg_block + s * a.seg_blocks;
+struct RowGeo {
+  int nc = 0;       // key slots [0, nc) minus the key gap: complete windows by the row
+  Gap keys, blocks;  // other candidates' key slots / blocks
+  int s = 0;        // the row's candidate segment (0 outside segments)
+  int current = -1, previous = -1, first = -1;  // block ids of the true current,
+                                                // previous and first blocks
+  __device__ __forceinline__ bool key_visible(int c) const { return c < nc && !keys.hides(c); }
+};
+
+__device__ __forceinline__ RowGeo row_geo(const SelectArgs& a, int pos) {
+  RowGeo r;
+  if (pos < 0) return r;
+  const int bs = a.BS;
+  const bool in_segment = a.seg_blocks > 0 && pos / bs >= a.seg_block;
+  int truth = pos;
+  if (in_segment) {
+    const int start = a.seg_block * bs, span = a.seg_blocks * bs;
+    r.s = (pos - start) / span;
+    truth = start + (pos - start) % span;
+    if (r.s > 0) {
+      r.keys.lo = a.seg_key;
+      r.keys.hi = a.seg_key + r.s * a.seg_keys;
+      r.blocks.lo = a.seg_block;
+      r.blocks.hi = a.seg_block + r.s * a.seg_blocks;
     }
   }
-  return gap;
+  // Complete windows i * d + l <= truth + 1, as key slots.
+  const int complete =
+      truth + 1 >= a.cmp_block ? (truth + 1 - a.cmp_block) / a.cmp_stride + 1 : 0;
+  r.nc = in_segment && complete > a.seg_key
+             ? a.seg_key + r.s * a.seg_keys + (complete - a.seg_key)
+             : complete;
+  r.nc = min(r.nc, a.C);
+  auto block_id = [&](int true_block) {  // true block -> this row's block id
+    return in_segment && true_block >= a.seg_block
+               ? a.seg_block + r.s * a.seg_blocks + (true_block - a.seg_block)
+               : true_block;
+  };
+  r.current = pos / bs;
+  r.previous = truth / bs >= 1 ? block_id(truth / bs - 1) : -1;
+  r.first = block_id(0);
+  return r;
+}
+
+// Selection-block scores of one row from its compressed-key scores when the
+// windows are not the blocks (l, d != BS): block j sums, in ascending window
+// order, the scores of the windows that overlap it, each weighted by the
+// number of its stride steps inside the block. Only candidates (blocks before
+// the current one, outside the gap) are computed; other entries are 0.
+__device__ __forceinline__ void aggregate_blocks(const SelectArgs& a, const RowGeo& r,
+                                                 const float* key_scores, float* out, int lane) {
+  const int bs = a.BS, l = a.cmp_block, d = a.cmp_stride;
+  for (int j = lane; j < a.nb; j += 32) {
+    float acc = 0.f;
+    if (j < r.current && !r.blocks.hides(j)) {
+      const bool own = a.seg_blocks > 0 && j >= a.seg_block;
+      const int jt = own ? a.seg_block + (j - a.seg_block) % a.seg_blocks : j;
+      const int lo = jt * bs, hi = lo + bs;
+      const int first = lo - l + 1 > 0 ? (lo - l + 1 + d - 1) / d : 0;
+      const int last = (hi - 1) / d;
+      for (int i = first; i <= last; ++i) {
+        const int w = (min(i * d + l, hi) - max(i * d, lo)) / d;
+        if (w <= 0) continue;
+        const int slot = a.seg_blocks > 0 && i >= a.seg_key
+                             ? a.seg_key + r.s * a.seg_keys + (i - a.seg_key)
+                             : i;
+        if (slot < a.C) acc += (float)w * key_scores[slot];
+      }
+    }
+    out[j] = acc;
+  }
+}
+
+// Entries written before the ranked picks: the current block, then (forced)
+// the previous block and the first block, each once and only if before the
+// current one; the forced blocks are marked taken (-1) in `sc`. Returns the
+// number of entries written. Warp-collective.
+__device__ __forceinline__ int forced_picks(const SelectArgs& a, const RowGeo& r, int32_t* brow,
+                                            float* sc, int lane) {
+  int k = 0;
+  if (lane == 0) brow[0] = r.current;
+  ++k;
+  if (a.forced) {
+    const int picks[2] = {r.previous, r.first};
+    for (int f = 0; f < 2; ++f) {
+      const int b = picks[f];
+      if (b < 0 || b >= r.current || (f == 1 && b == r.previous)) continue;
+      if (k < a.width && lane == 0) brow[k] = b;
+      if (lane == 0) sc[b] = -2.f;  // taken
+      ++k;
+    }
+  }
+  __syncwarp();
+  return k < a.width ? k : a.width;
 }
 
 __global__ void __launch_bounds__(kWarps * 32)
@@ -97,8 +188,8 @@ __global__ void __launch_bounds__(kWarps * 32)
   int q = row / a.H, h = row % a.H;
   int pos = a.positions[q];
   int g = lane >> 2, c = lane & 3;
-  int nc = pos >= 0 ? min((pos + 1) / a.BS, a.C) : 0;  // complete summaries
-  const Gap gap = segment_gap(a, pos);
+  const RowGeo rg = row_geo(a, pos);
+  const int nc = rg.nc;
   int tiles = (nc + kTileKeys - 1) / kTileKeys;
   long long spin = 1ll << 31;
   for (int i = threadIdx.x; i < score_len; i += blockDim.x) scores[i] = 0.f;
@@ -123,8 +214,7 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
     phase ^= 1;
     int base = t * kTileKeys;
-    sm.step(qa, k_addr, v_addr, lane,
-            [&](int k) { return base + k < nc && !gap.hides(base + k); });
+    sm.step(qa, k_addr, v_addr, lane, [&](int k) { return rg.key_visible(base + k); });
     __syncwarp();
   }
   // Merge the warps' (max, sum, accumulator) per head through shared memory.
@@ -197,7 +287,7 @@ __global__ void __launch_bounds__(kWarps * 32)
       for (int e = 0; e < 2; ++e) {
         int key = t * kTileKeys + nt * 8 + 2 * c + e;
         float p = 0.f;
-        if (key < nc && !gap.hides(key))
+        if (rg.key_visible(key))
           p = expf(sc[nt][e] - gm[0]) * inv[0] + expf(sc[nt][e + 2] - gm[1]) * inv[1];
         p += __shfl_xor_sync(0xffffffffu, p, 4);
         p += __shfl_xor_sync(0xffffffffu, p, 8);
@@ -208,23 +298,36 @@ __global__ void __launch_bounds__(kWarps * 32)
     __syncwarp();
   }
   __syncthreads();
+  // Block scores: the key scores themselves in the reference geometry, else
+  // aggregated into the region after the merge buffers.
+  float* bsc = scores;
+  if (!a.identity) {
+    bsc = reinterpret_cast<float*>(bars + kWarps);
+    if (warp == 0) aggregate_blocks(a, rg, scores, bsc, lane);
+    __syncthreads();
+  }
+  const int columns = a.identity ? a.C : a.nb;
   if (a.scores) {
-    float* srow = a.scores + (long long)row * a.C;
-    for (int i = threadIdx.x; i < a.C; i += blockDim.x) srow[i] = scores[i];
+    float* srow = a.scores + (long long)row * columns;
+    for (int i = threadIdx.x; i < columns; i += blockDim.x) srow[i] = bsc[i];
   }
   __syncthreads();
   if (warp != 0) return;
-  // Top-n: current block first, then (score desc, block asc) among earlier blocks.
+  // Top-n: current block first (then, forced, the previous and first
+  // blocks), then (score desc, block asc) among earlier blocks.
   int32_t* brow = a.blocks + (long long)row * a.width;
-  int current = pos >= 0 ? pos / a.BS : -1;
-  int limit = min(current, score_len);  // candidates: blocks before the current one
-  if (lane == 0) brow[0] = current >= 0 ? current : -1;
-  for (int k = 1; k < a.width; ++k) {
+  const int current = rg.current;
+  const int limit = min(current, a.identity ? score_len : a.nb);  // candidates: before current
+  if (current < 0) {
+    for (int k = lane; k < a.width; k += 32) brow[k] = -1;
+    return;
+  }
+  for (int k = forced_picks(a, rg, brow, bsc, lane); k < a.width; ++k) {
     float best = -1.f;
     int best_idx = 0x7fffffff;
     for (int i = lane; i < limit; i += 32) {
-      if (gap.hides(i)) continue;
-      float v = scores[i];
+      if (rg.blocks.hides(i)) continue;
+      float v = bsc[i];
       if (v > best || (v == best && i < best_idx)) {
         best = v;
         best_idx = i;
@@ -240,8 +343,8 @@ __global__ void __launch_bounds__(kWarps * 32)
       }
     }
     if (lane == 0) {
-      brow[k] = best_idx < limit ? best_idx : -1;
-      if (best_idx < limit) scores[best_idx] = -2.f;  // taken
+      brow[k] = best_idx < limit && best >= 0.f ? best_idx : -1;
+      if (best_idx < limit) bsc[best_idx] = -2.f;  // taken
     }
     __syncwarp();
   }
@@ -276,9 +379,9 @@ constexpr int kTcTmemCols = 512;                    // S (256) + O (64), power o
 constexpr int kTcMaxScores = 2048;                  // per-row score slots in shared memory
 constexpr int kTcReduceBytes = 2 * 4 * 128 * 4;     // per-quarter row max / sum
 
-size_t tc_smem_bytes(int kres, int score_len) {
+size_t tc_smem_bytes(int kres, int score_len, int nb_len) {
   return 1024 + (size_t)kTcQBytes + 2 * (size_t)kres * kTcChunkBytes + kTcPBytes +
-         kTcReduceBytes + (size_t)kTcRows * score_len * 4 + 64;
+         kTcReduceBytes + (size_t)kTcRows * (score_len + nb_len) * 4 + 64;
 }
 
 // Top-n key of a score: non-negative scores order like their bit patterns;
@@ -306,7 +409,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   float* red_max = reinterpret_cast<float*>(p_tile + kTcPBytes);  // [4][128]
   float* red_sum = red_max + 4 * 128;                               // [4][128]
   float* scores = red_sum + 4 * 128;                                // [kTcRows][score_len]
-  uint64_t* tma_bar = reinterpret_cast<uint64_t*>(scores + kTcRows * score_len);
+  float* bscores = scores + kTcRows * score_len;                    // [kTcRows][nb_len]
+  uint64_t* tma_bar = reinterpret_cast<uint64_t*>(bscores + kTcRows * a.nb_len);
   uint64_t* mma_bar = tma_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
 
@@ -350,9 +454,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int ql = m >> 4, g = m & 15, q = q0 + ql;
   const bool row_ok = q < a.Q;
   const int pos = row_ok ? a.positions[q] : -1;
-  const int nc = pos >= 0 ? min((pos + 1) / a.BS, C) : 0;
-  const Gap gap = segment_gap(a, pos);
-  auto visible = [&](int c) { return c < nc && !gap.hides(c); };
+  const RowGeo rg = row_geo(a, pos);
+  auto visible = [&](int c) { return rg.key_visible(c); };
   const long long qrow = ((long long)q * H + h) * cxs::kGroups + g;  // [Q, H, 16] row index
 #pragma unroll
   for (int c = 2 * cq; c < 2 * cq + 2; ++c) {
@@ -574,11 +677,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   }
   __syncthreads();
+  // Block scores of each row: its key scores in the reference geometry, else
+  // aggregated by warp r for row r.
+  const bool rank_keys = a.identity;
+  if (!rank_keys) {
+    if (warp < kTcRows && q0 + warp < a.Q) {
+      const RowGeo wr = row_geo(a, a.positions[q0 + warp]);
+      aggregate_blocks(a, wr, scores + warp * score_len, bscores + warp * a.nb_len, lane);
+    }
+    __syncthreads();
+  }
+  float* const ranked = rank_keys ? scores : bscores;
+  const int ranked_len = rank_keys ? score_len : a.nb_len;
+  const int columns = rank_keys ? C : a.nb;
   if (a.scores) {
     for (int r = 0; r < kTcRows; ++r) {
       if (q0 + r >= a.Q) break;
-      float* srow = a.scores + ((long long)(q0 + r) * H + h) * C;
-      for (int i = tid; i < C; i += kTcThreads) srow[i] = scores[r * score_len + i];
+      float* srow = a.scores + ((long long)(q0 + r) * H + h) * columns;
+      for (int i = tid; i < columns; i += kTcThreads) srow[i] = ranked[r * ranked_len + i];
     }
     __syncthreads();
   }
@@ -588,27 +704,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // min block id among the lanes holding it) and one rescan by the owner.
   if (warp < kTcRows && q0 + warp < a.Q) {
     const int qq = q0 + warp;
-    const int p = a.positions[qq];
-    const int current = p >= 0 ? p / a.BS : -1;
-    const int limit = min(current, score_len);
-    const Gap row_gap = segment_gap(a, p);
-    float* sc = scores + warp * score_len;
+    const RowGeo wr = row_geo(a, a.positions[qq]);
+    const int current = wr.current;
+    const int limit = min(current, ranked_len);
+    float* sc = ranked + warp * ranked_len;
     int32_t* brow = a.blocks + ((long long)qq * H + h) * a.width;
-    if (lane == 0) brow[0] = current >= 0 ? current : -1;
     uint32_t best = 0, best_idx = 0xffffffffu;
     auto rescan = [&]() {
       best = 0;
       best_idx = 0xffffffffu;
       for (int i = lane; i < limit; i += 32) {
-        const uint32_t key = row_gap.hides(i) ? 0u : topn_key(sc[i]);
+        const uint32_t key = wr.blocks.hides(i) ? 0u : topn_key(sc[i]);
         if (key > best) {
           best = key;
           best_idx = i;
         }
       }
     };
+    int k = 1;
+    if (current < 0) {
+      if (lane == 0) brow[0] = -1;
+    } else {
+      k = forced_picks(a, wr, brow, sc, lane);
+    }
     rescan();
-    for (int k = 1; k < a.width; ++k) {
+    for (; k < a.width; ++k) {
       const uint32_t top = __reduce_max_sync(0xffffffffu, best);
       const uint32_t idx = __reduce_min_sync(0xffffffffu, best == top ? best_idx : 0xffffffffu);
       if (lane == 0) brow[k] = top ? (int32_t)idx : -1;
@@ -644,13 +764,43 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
-extern "C" int cxs_compressed_select_segments(
-    const void* query, const void* compressed, int32_t summaries, const int32_t* positions,
-    int32_t queries, int32_t heads, int32_t block_size, int32_t count, int64_t total,
-    int64_t segment_start, int64_t segment_tokens, void* out, int32_t* blocks, float* scores,
-    void* stream) {
+extern "C" int cxs_select_score_columns(const cxs_select_geometry* geometry,
+                                        int32_t* columns) {
+  if (!geometry || !columns) return set_error(CXS_ERR_INVALID, "null argument");
+  const cxs_select_geometry& g = *geometry;
+  const int bs = g.block_size, l = g.window, d = g.stride;
+  if (bs < 1 || l < 1 || d < 1 || g.summaries < 0 || g.total < 1)
+    return set_error(CXS_ERR_INVALID, "invalid compressed-select geometry");
+  if (l == bs && d == bs) {
+    *columns = g.summaries;
+  } else if (g.segment_tokens > 0) {
+    const long long seg_key = g.segment_start >= l ? (g.segment_start - l) / d + 1 : 0;
+    const long long seg_keys = g.segment_tokens / d;
+    const long long segments = seg_keys ? (g.summaries - seg_key + seg_keys - 1) / seg_keys : 0;
+    *columns = (int32_t)(g.segment_start / bs + (segments > 0 ? segments : 0) *
+                                                    (g.segment_tokens / bs));
+  } else {
+    *columns = (int32_t)((g.total + bs - 1) / bs);
+  }
+  return CXS_OK;
+}
+
+extern "C" int cxs_compressed_select_nsa(const cxs_select_geometry* geometry, const void* query,
+                                         const void* compressed, const int32_t* positions,
+                                         void* out, int32_t* blocks, float* scores,
+                                         void* stream) {
+  if (!geometry) return set_error(CXS_ERR_INVALID, "null compressed-select geometry");
+  const cxs_select_geometry& g = *geometry;
+  const int queries = g.queries, heads = g.heads, block_size = g.block_size, count = g.count;
+  const int summaries = g.summaries, l = g.window, d = g.stride;
+  const long long total = g.total, segment_start = g.segment_start,
+                  segment_tokens = g.segment_tokens;
   if (queries < 1 || heads < 1 || block_size < 1 || count < 1 || total < 1 || summaries < 0)
     return set_error(CXS_ERR_INVALID, "invalid compressed-select geometry");
+  if (d < 1 || l < d || l % d || block_size % d || (g.forced != 0 && g.forced != 1))
+    return set_error(CXS_ERR_INVALID,
+                     "window must be a multiple of the stride, the block a multiple of the "
+                     "stride, forced 0 or 1");
   if (segment_tokens < 0 || segment_start < 0 ||
       (segment_tokens > 0 && (segment_start % block_size || segment_tokens % block_size ||
                               segment_start + segment_tokens * (long long)queries > INT32_MAX)))
@@ -663,6 +813,9 @@ extern "C" int cxs_compressed_select_segments(
   long long blocks_total = (total + block_size - 1) / block_size;
   int width = (int)(count < blocks_total ? count : blocks_total);
   if (summaries > (1 << 20)) return set_error(CXS_ERR_CAPACITY, "too many summaries");
+  int32_t columns = 0;
+  int status = cxs_select_score_columns(geometry, &columns);
+  if (status != CXS_OK) return status;
   auto fn = encode_fn();
   if (!fn) return set_error(CXS_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
   CUtensorMap map;
@@ -688,6 +841,14 @@ extern "C" int cxs_compressed_select_segments(
   a.total = total;
   a.seg_block = segment_tokens > 0 ? (int)(segment_start / block_size) : 0;
   a.seg_blocks = (int)(segment_tokens / block_size);
+  a.seg_key = segment_tokens > 0 ? (int)(segment_start >= l ? (segment_start - l) / d + 1 : 0) : 0;
+  a.seg_keys = (int)(segment_tokens / d);
+  a.cmp_block = l;
+  a.cmp_stride = d;
+  a.identity = l == block_size && d == block_size;
+  a.forced = g.forced;
+  a.nb = a.identity ? 0 : columns;
+  a.nb_len = a.identity ? 0 : (columns + 3) & ~3;
   a.query = (const __nv_bfloat16*)query;
   a.positions = positions;
   a.out = (__nv_bfloat16*)out;
@@ -709,13 +870,14 @@ extern "C" int cxs_compressed_select_segments(
   }
   a.error = g_select_error_address[device];
   long long longest = summaries > blocks_total ? summaries : blocks_total;
-  if (longest > (1 << 20)) return set_error(CXS_ERR_CAPACITY, "too many blocks");
+  if (longest > (1 << 20) || columns > (1 << 20))
+    return set_error(CXS_ERR_CAPACITY, "too many blocks");
   int score_len = (int)((longest + 3) & ~3ll);
   a.score_len = score_len;
   int chunks = (summaries + kTcChunk - 1) / kTcChunk;
   int kres = chunks <= kTcMaxResident ? (chunks > 0 ? chunks : 1) : 1;
-  if (kres > 1 && tc_smem_bytes(kres, score_len) > (size_t)kMaxSmem) kres = 1;
-  size_t tc_smem = tc_smem_bytes(kres, score_len);
+  if (kres > 1 && tc_smem_bytes(kres, score_len, a.nb_len) > (size_t)kMaxSmem) kres = 1;
+  size_t tc_smem = tc_smem_bytes(kres, score_len, a.nb_len);
   if (score_len <= kTcMaxScores && tc_smem <= (size_t)kMaxSmem) {
     int grid = ((queries + kTcRows - 1) / kTcRows) * heads;
     compressed_select_tc_kernel<<<grid, kTcThreads, tc_smem, (cudaStream_t)stream>>>(map, a, kres);
@@ -723,13 +885,33 @@ extern "C" int cxs_compressed_select_segments(
     return CXS_OK;
   }
   size_t smem = 1024 + (size_t)kWarps * 2 * kTileBytes + (size_t)score_len * 4 +
-                (size_t)kWarps * (32 + 16 * 64) * 4 + kWarps * 8;
+                (size_t)kWarps * (32 + 16 * 64) * 4 + kWarps * 8 + (size_t)a.nb_len * 4;
   if (smem > (size_t)kMaxSmem) return set_error(CXS_ERR_CAPACITY, "too many summaries for one warp");
   int rows = queries * heads;
   compressed_select_kernel<<<rows, kWarps * 32, smem, (cudaStream_t)stream>>>(
       map, a);
   CXS_LAUNCH_CHECK("compressed_select_kernel");
   return CXS_OK;
+}
+
+extern "C" int cxs_compressed_select_segments(
+    const void* query, const void* compressed, int32_t summaries, const int32_t* positions,
+    int32_t queries, int32_t heads, int32_t block_size, int32_t count, int64_t total,
+    int64_t segment_start, int64_t segment_tokens, void* out, int32_t* blocks, float* scores,
+    void* stream) {
+  cxs_select_geometry g = {};
+  g.queries = queries;
+  g.heads = heads;
+  g.block_size = block_size;
+  g.count = count;
+  g.summaries = summaries;
+  g.window = block_size;
+  g.stride = block_size;
+  g.forced = 0;
+  g.total = total;
+  g.segment_start = segment_start;
+  g.segment_tokens = segment_tokens;
+  return cxs_compressed_select_nsa(&g, query, compressed, positions, out, blocks, scores, stream);
 }
 
 extern "C" int cxs_compressed_select(const void* query, const void* compressed, int32_t summaries,

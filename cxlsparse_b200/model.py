@@ -43,10 +43,36 @@ class NSAConfig:
     block_counts: int = 16
     window: int = 512
     hot: int = 256
+    # Compressed branch. "mean": the reference's summaries (mean of each
+    # selection block, models/nsa/ops.py:62-70). "mlp": BASELINE's NSA
+    # geometry: a key/value per window of cmp_block tokens at stride
+    # cmp_stride from a per-layer MLP with intra-window position encoding,
+    # selection scores aggregated over the overlapping windows.
+    compression: str = "mean"
+    cmp_block: int = 32
+    cmp_stride: int = 16
+    cmp_hidden: int = 256
+    forced_blocks: bool = False  # block 0 and the two local blocks always selected
 
     @property
     def groups(self):
         return self.q_heads // self.kv_heads
+
+    @property
+    def windows(self):
+        """(window, stride) of the compressed keys."""
+        if self.compression == "mean":
+            return self.block_size, self.block_size
+        return self.cmp_block, self.cmp_stride
+
+    @classmethod
+    def baseline(cls, **overrides):
+        """BASELINE's NSA parameters: compression 32 / stride 16 with an MLP,
+        selection block 64, top-16 including block 0 and 2 local blocks,
+        window 512."""
+        values = dict(compression="mlp", cmp_block=32, cmp_stride=16, forced_blocks=True)
+        values.update(overrides)
+        return cls(**values)
 
 
 @dataclass
@@ -141,14 +167,23 @@ class NSAExtendModel:
         d, kvd = cfg.hidden, cfg.kv_heads * cfg.head_dim
         self.embed = normal(cfg.vocab, d)
         self.final_norm = torch.ones(d, dtype=torch.bfloat16, device=self.device)
+        if cfg.compression not in ("mean", "mlp"):
+            raise ValueError("compression must be 'mean' or 'mlp'")
         self.layers = []
         for _ in range(cfg.layers):
-            self.layers.append(dict(
+            layer = dict(
                 in_norm=torch.ones(d, dtype=torch.bfloat16, device=self.device),
                 post_norm=torch.ones(d, dtype=torch.bfloat16, device=self.device),
                 q=normal(cfg.q_heads * cfg.head_dim, d), k=normal(kvd, d), v=normal(kvd, d),
                 g=normal(cfg.q_heads * 3, d), o=normal(d, cfg.q_heads * cfg.head_dim),
-                gate=normal(cfg.ffn, d), up=normal(cfg.ffn, d), down=normal(d, cfg.ffn)))
+                gate=normal(cfg.ffn, d), up=normal(cfg.ffn, d), down=normal(d, cfg.ffn))
+            if cfg.compression == "mlp":
+                # K and V compression MLPs, stacked [K, V] for batched GEMMs.
+                l, hid = cfg.cmp_block, cfg.cmp_hidden
+                layer.update(cmp_pe=normal(2, l, cfg.head_dim),
+                             cmp_w1=normal(2, hid, l * cfg.head_dim),
+                             cmp_w2=normal(2, cfg.head_dim, hid))
+            self.layers.append(layer)
         self.inv_freq = 1.0 / (cfg.rope_theta ** (
             torch.arange(0, cfg.head_dim, 2, device=self.device).float() / cfg.head_dim))
         pages_per_user = cfg.layers * self.kv_local * math.ceil(max_history / 64)
@@ -203,10 +238,16 @@ class NSAExtendModel:
         gates = gates[:, own].contiguous()
         records = torch.cat((k[:, own], v[:, own]), -1).contiguous()
         total = old + len(records)
-        compressed, tail = ops.append_compressed(st.summaries[index], st.tails[index], records,
-                                                 cfg.block_size)
+        if cfg.compression == "mean":
+            compressed, tail = ops.append_compressed(st.summaries[index], st.tails[index],
+                                                     records, cfg.block_size)
+        else:
+            compressed, tail = self._append_windows(w, st.summaries[index], st.tails[index],
+                                                    records)
+        l, d = cfg.windows
         cmp_out, blocks = ops.compressed_attention_select(
-            query, compressed, positions, total, cfg.block_size, cfg.block_counts)
+            query, compressed, positions, total, cfg.block_size, cfg.block_counts, window=l,
+            stride=d, forced=cfg.forced_blocks)
         window_kv = torch.cat((st.windows[index], records))
         window_start = old - len(st.windows[index])
         base = st.row + index * self.kv_local
@@ -225,6 +266,32 @@ class NSAExtendModel:
         if append:
             self._append(index, st, records, compressed, tail, window_kv)
         return hidden
+
+    def compress(self, w, windows):
+        """MLP compression of token windows [n, l, H, 128] -> keys [n, H, 128]:
+        for K and V, phi(x) = w2 silu(w1 vec(x + pe)) (bf16 GEMMs)."""
+        n, l, heads = windows.shape[:3]
+        dim = self.cfg.head_dim
+        out = torch.empty((n, heads, 2 * dim), dtype=windows.dtype, device=windows.device)
+        if not n:
+            return out
+        x = windows.reshape(n, l, heads, 2, dim).permute(3, 0, 2, 1, 4)  # [2, n, H, l, dim]
+        x = (x + w["cmp_pe"][:, None, None]).reshape(2, n * heads, l * dim)
+        hidden = F.silu(torch.bmm(x, w["cmp_w1"].transpose(1, 2)))
+        keys = torch.bmm(hidden, w["cmp_w2"].transpose(1, 2))          # [2, n * H, dim]
+        out.view(n, heads, 2, dim).copy_(keys.view(2, n, heads, dim).permute(1, 2, 0, 3))
+        return out
+
+    def _append_windows(self, w, keys, tail, records):
+        """Keys of the windows that complete in tail || records (the tail
+        starts at the first incomplete window) and the new tail."""
+        l, d = self.cfg.windows
+        values = torch.cat((tail, records))
+        count = (len(values) - l) // d + 1 if len(values) >= l else 0
+        if count:
+            windows = values.unfold(0, l, d).permute(0, 3, 1, 2)      # [count, l, H, 128]
+            keys = torch.cat((keys, self.compress(w, windows)))
+        return keys, values[count * d:].clone()
 
     def _append(self, index, st, records, compressed, tail, window_kv):
         """Persist this chunk as history: pool write, slot table, summaries, window."""
@@ -316,16 +383,22 @@ class NSAExtendModel:
         old = st.length
         layout = SegmentLayout(old, E, n_cand, bs)
         tail_len, start, seg_tokens = layout.tail, layout.start, layout.tokens
+        mlp = cfg.compression == "mlp"
+        l, stride = cfg.windows
+        arange_l = torch.arange(l)
         layers = []
         for index in range(cfg.layers):
             kept = len(st.windows[index])
+            # mean: history records past the last complete block; mlp: past
+            # the start of the first incomplete window.
             tail = len(st.tails[index])
             if tail > kept:
                 raise ValueError("window must retain the summary tail")
             c_hist = len(st.summaries[index])
-            new = (tail + E) // bs
             base = st.row + index * kl
+            last_window = (old + E - l) // stride  # last window complete by the suffix end
             if n_cand == 1:
+                new = (tail + E) // bs if not mlp else max(0, last_window + 1 - c_hist)
                 window_buf = torch.empty((kept + E, kl, 128), dtype=torch.bfloat16, device=d)
                 window_buf[:kept] = st.windows[index]
                 summaries = torch.empty((c_hist + new, kl, 128), dtype=torch.bfloat16, device=d)
@@ -333,36 +406,72 @@ class NSAExtendModel:
                 current = torch.empty((kl, E, 128), dtype=torch.bfloat16, device=d)
                 fetches = [dict(row=base + h, cached_length=old, history_length=old,
                                 current_kv=current[h]) for h in range(kl)]
-                layers.append(dict(kept=kept, tail=tail, c_hist=c_hist, new=new,
-                                   window_buf=window_buf, summaries=summaries, current=current,
-                                   fetches=fetches, window_start=old - kept))
+                entry = dict(kept=kept, tail=tail, c_hist=c_hist, new=new,
+                             window_buf=window_buf, summaries=summaries, current=current,
+                             fetches=fetches, window_start=old - kept)
+                if mlp and new:
+                    # Window i covers true positions i*d .. i*d + l - 1, at
+                    # window-buffer row kept + (t - old).
+                    first = torch.arange(c_hist, c_hist + new) * stride
+                    entry.update(cmp_rows=(kept - old + first[:, None] + arange_l).to(d),
+                                 cmp_slots=torch.arange(c_hist, c_hist + new, device=d))
+                layers.append(entry)
                 continue
-            if tail != tail_len or c_hist * bs != start:
-                raise ValueError("layer state does not match the history length")
+            if kept < tail_len:
+                raise ValueError("window must retain the history tail")
             # Window buffer of a fixed length (W - 1 history records + the
             # segments), the history right-aligned against the segments: users
             # with different history lengths share workspace shapes. Records
             # before the first kept one are never inside a window.
-            shared = kept - tail                            # window records below `start`
+            shared = kept - tail_len                        # window records below `start`
             lead = cfg.window - 1
             window_buf = torch.zeros((lead + n_cand * seg_tokens, kl, 128),
                                      dtype=torch.bfloat16, device=d)
             window_buf[lead - shared:lead] = st.windows[index][:shared]
+            tail_records = st.windows[index][shared:]       # history past `start`
             segs = window_buf[lead:].view(n_cand, seg_tokens, kl, 128)
-            segs[:, :tail] = st.tails[index]
-            nsb = seg_tokens // bs
-            summaries = torch.zeros((c_hist + n_cand * nsb, kl, 128), dtype=torch.bfloat16,
-                                    device=d)
-            summaries[:c_hist] = st.summaries[index]
+            segs[:, :tail_len] = tail_records
             current = torch.zeros((kl, n_cand * seg_tokens, 128), dtype=torch.bfloat16,
                                   device=d)
-            current.view(kl, n_cand, seg_tokens, 128)[:, :, :tail] = (
-                st.tails[index].permute(1, 0, 2)[:, None])
+            current.view(kl, n_cand, seg_tokens, 128)[:, :, :tail_len] = (
+                tail_records.permute(1, 0, 2)[:, None])
             fetches = [dict(row=base + h, cached_length=start, history_length=start,
                             current_kv=current[h]) for h in range(kl)]
-            layers.append(dict(kept=lead, tail=tail, c_hist=c_hist, new=new, nsb=nsb,
-                               window_buf=window_buf, summaries=summaries, current=current,
-                               fetches=fetches, window_start=start - lead))
+            entry = dict(kept=lead, tail=tail_len, window_buf=window_buf, current=current,
+                         fetches=fetches, window_start=start - lead)
+            if not mlp:
+                if c_hist * bs != start:
+                    raise ValueError("layer state does not match the history length")
+                nsb = seg_tokens // bs
+                summaries = torch.zeros((c_hist + n_cand * nsb, kl, 128),
+                                        dtype=torch.bfloat16, device=d)
+                summaries[:c_hist] = st.summaries[index]
+                entry.update(c_hist=c_hist, new=(tail_len + E) // bs, nsb=nsb,
+                             summaries=summaries)
+            else:
+                # Key slots: the windows that end below `start` are shared;
+                # candidate c owns seg_keys slots for its windows from seg_key
+                # on (those crossing `start` and those in its segment).
+                seg_key = (start - l) // stride + 1 if start >= l else 0
+                seg_keys = seg_tokens // stride
+                summaries = torch.zeros((seg_key + n_cand * seg_keys, kl, 128),
+                                        dtype=torch.bfloat16, device=d)
+                summaries[:seg_key] = st.summaries[index][:seg_key]
+                static = st.summaries[index][seg_key:c_hist]  # windows inside the history
+                rows_, slots_ = [], []
+                for c in range(n_cand):
+                    own = seg_key + c * seg_keys
+                    summaries[own:own + len(static)] = static
+                    for i in range(c_hist, last_window + 1):
+                        t = i * stride + arange_l
+                        rows_.append(torch.where(t < start, lead - (start - t),
+                                                 lead + c * seg_tokens + (t - start)))
+                        slots_.append(own + i - seg_key)
+                entry.update(c_hist=c_hist, new=len(slots_), summaries=summaries)
+                if slots_:
+                    entry.update(cmp_rows=torch.stack(rows_).to(d),
+                                 cmp_slots=torch.tensor(slots_, device=d))
+            layers.append(entry)
         r = torch.arange(rows, device=d)
         true_positions = (old + r % E).to(torch.int32)
         if n_cand == 1:
@@ -392,13 +501,14 @@ class NSAExtendModel:
         proj = F.linear(x, w["qkvg"])
         kl = self.kv_local
         segments = f["segments"]
+        mlp = cfg.compression == "mlp"
         if segments is None:
             records = L["window_buf"][L["kept"]:]
             _lib.check(lib.cxs_qkv_rope(
                 proj.data_ptr(), proj.shape[1], positions.data_ptr(), self.inv_freq.data_ptr(),
                 E, kl * cfg.groups, kl, query.data_ptr(), records.data_ptr(),
                 kl * 128, L["current"].data_ptr(), E * 128, gates.data_ptr(), stream))
-            if L["new"]:
+            if L["new"] and not mlp:
                 start = L["window_buf"][L["kept"] - L["tail"]:]
                 _lib.check(lib.cxs_block_summaries(
                     start.data_ptr(), L["tail"] + E, kl, cfg.block_size,
@@ -413,13 +523,19 @@ class NSAExtendModel:
                 self.inv_freq.data_ptr(), E, kl * cfg.groups, kl, query.data_ptr(),
                 records.data_ptr(), kl * 128, current.data_ptr(), L["current"].shape[1] * 128,
                 gates.data_ptr(), per, seg_tokens, stream))
-            if L["new"]:
+            if L["new"] and not mlp:
                 ops.block_summaries_segments(
                     L["window_buf"][L["kept"]:], tail + per, cfg.block_size,
                     L["summaries"][L["c_hist"]:], f["candidates"], seg_tokens, L["nsb"])
+        if mlp and "cmp_rows" in L:
+            # Keys of the windows this step completes, gathered from the window
+            # buffer (history rows and the step's suffix rows).
+            L["summaries"].index_copy_(0, L["cmp_slots"],
+                                       self.compress(w, L["window_buf"][L["cmp_rows"]]))
+        l, d = cfg.windows
         cmp_out, blocks = ops.compressed_attention_select(
             query, L["summaries"], positions, f["total"], cfg.block_size, cfg.block_counts,
-            segments=segments)
+            segments=segments, window=l, stride=d, forced=cfg.forced_blocks)
         if self.selections is not None:
             self.selections.append(blocks)
         if self.probe is not None:  # comparison plan on the same selections / cache state

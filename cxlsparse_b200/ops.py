@@ -13,14 +13,36 @@ import torch
 from . import _lib
 
 
+def select_geometry(queries, heads, summaries, total, block_size, count, *, segments=None,
+                    window=None, stride=None, forced=False):
+    """The C geometry of one compressed-select call (see ``cxs_select_geometry``)."""
+    segment_start, segment_tokens = segments or (0, 0)
+    return _lib.SelectGeometry(
+        queries=queries, heads=heads, block_size=block_size, count=count, summaries=summaries,
+        window=window or block_size, stride=stride or block_size, forced=int(bool(forced)),
+        total=total, segment_start=segment_start, segment_tokens=segment_tokens)
+
+
+def score_columns(geometry):
+    """Columns of the block-score output for ``geometry``."""
+    columns = _lib.c_i32(0)
+    _lib.check(_lib.lib().cxs_select_score_columns(geometry, columns))
+    return columns.value
+
+
 def compressed_attention_select(query, compressed, positions, total, block_size, count, *,
-                                scores=None, segments=None):
+                                scores=None, segments=None, window=None, stride=None,
+                                forced=False):
     """Compressed-token attention and top-n block ids; ``scores`` optionally
-    receives the [Q, H, C] fp32 block scores the selection was made from.
+    receives the [Q, H, columns] fp32 block scores the selection was made
+    from (columns = C in the reference geometry, see ``score_columns``).
     ``segments=(segment_start, segment_tokens)`` selects over candidate
     segments (positions, summaries and returned block ids in the segment
     layout of ``cxs_attend_geometry``; ``total`` is one candidate's true
-    history + suffix length)."""
+    history + suffix length). ``window`` / ``stride`` (default: the block
+    size, the reference's mean-pooled summaries) describe overlapping
+    compressed keys; ``forced`` adds the previous block and block 0 after
+    the current one (BASELINE's NSA geometry)."""
     queries, heads, groups, dim = query.shape
     if groups != 16 or dim != 64 or query.dtype != torch.bfloat16:
         raise ValueError("query must be bf16 [Q, H, 16, 64]")
@@ -32,14 +54,14 @@ def compressed_attention_select(query, compressed, positions, total, block_size,
     width = min(count, (total + block_size - 1) // block_size)
     output = torch.empty_like(query)
     blocks = torch.empty((queries, heads, width), dtype=torch.int32, device=query.device)
-    if scores is not None and scores.shape != (queries, heads, len(compressed)):
-        raise ValueError("scores must be [Q, H, C] fp32")
+    geometry = select_geometry(queries, heads, len(compressed), total, block_size, count,
+                               segments=segments, window=window, stride=stride, forced=forced)
+    if scores is not None and scores.shape != (queries, heads, score_columns(geometry)):
+        raise ValueError("scores must be [Q, H, score_columns] fp32")
     stream = torch.cuda.current_stream(query.device)
-    segment_start, segment_tokens = segments or (0, 0)
-    _lib.check(_lib.lib().cxs_compressed_select_segments(
-        query.data_ptr(), compressed.data_ptr() if len(compressed) else None, len(compressed),
-        positions.data_ptr(), queries, heads, block_size, count, total, segment_start,
-        segment_tokens, output.data_ptr(), blocks.data_ptr(), _lib.ptr(scores),
+    _lib.check(_lib.lib().cxs_compressed_select_nsa(
+        geometry, query.data_ptr(), compressed.data_ptr() if len(compressed) else None,
+        positions.data_ptr(), output.data_ptr(), blocks.data_ptr(), _lib.ptr(scores),
         stream.cuda_stream))
     return output, blocks
 

@@ -327,6 +327,39 @@ int cxs_compressed_select_segments(const void* query, const void* compressed,
                                    int64_t segment_tokens, void* out, int32_t* blocks,
                                    float* scores, void* stream);
 
+/* Compressed branch + top-n in BASELINE's NSA geometry, of which the two
+ * entry points above are the special case window = stride = block_size,
+ * forced = 0. No counterpart in the reference. Compressed key i (row i of
+ * `compressed`) summarises the tokens [i * stride, i * stride + window); a
+ * row at true position p attends to the keys with i * stride + window <=
+ * p + 1. Selection-block scores: block j sums, in ascending i, the key
+ * scores of the windows overlapping it, each weighted by its stride steps
+ * inside the block (the published NSA aggregation; the identity when window
+ * = stride = block_size). Top-n: the current block, then with forced = 1
+ * the block before it and block 0, then the other earlier blocks by score
+ * descending, ties to the lower id.
+ * With candidate segments (as in cxs_attend_geometry) key slots below
+ * seg_key = (segment_start - window) / stride + 1 are the windows that end
+ * in the shared history; candidate s owns segment_tokens / stride slots
+ * after them, slot seg_key + s * (segment_tokens / stride) + k being true
+ * window seg_key + k of that candidate (windows that cross segment_start
+ * included). `scores` (optional) receives [Q, H, columns] block scores,
+ * columns from cxs_select_score_columns. */
+typedef struct cxs_select_geometry {
+  int32_t queries, heads, block_size, count;
+  int32_t summaries;  /* compressed keys C */
+  int32_t window;     /* tokens per compressed key (a multiple of stride) */
+  int32_t stride;     /* tokens between keys (divides block_size) */
+  int32_t forced;     /* 1: previous and first block follow the current one */
+  int64_t total;      /* true history + suffix length of one candidate */
+  int64_t segment_start, segment_tokens;  /* 0, 0: one suffix */
+} cxs_select_geometry;
+int cxs_compressed_select_nsa(const cxs_select_geometry* geometry, const void* query,
+                              const void* compressed, const int32_t* positions, void* out,
+                              int32_t* blocks, float* scores, void* stream);
+/* Columns of the block-score output of cxs_compressed_select_nsa. */
+int cxs_select_score_columns(const cxs_select_geometry* geometry, int32_t* columns);
+
 /* Mean-pool complete BS-token blocks of `tokens` records [n, H, 128] into
  * `summaries` [n / BS, H, 128] bf16 (models/nsa/ops.py:62-70). */
 int cxs_block_summaries(const void* tokens, int64_t count, int32_t heads, int32_t block_size,

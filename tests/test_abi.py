@@ -37,7 +37,8 @@ def _c_layout(struct, fields):
 def test_ctypes_structs_match_c_layout(tmp_path):
     pairs = [("cxs_plan_geometry", _lib.PlanGeometry), ("cxs_plan_buffers", _lib.PlanBuffers),
              ("cxs_attend_geometry", _lib.AttendGeometry),
-             ("cxs_attend_buffers", _lib.AttendBuffers)]
+             ("cxs_attend_buffers", _lib.AttendBuffers),
+             ("cxs_select_geometry", _lib.SelectGeometry)]
     source = ["#include <stdio.h>", "#include <stddef.h>", '#include "cxlsparse.h"',
               "int main(void) {"]
     for name, cls in pairs:

@@ -206,8 +206,9 @@ def test_transport_segments_match_each_candidate(cuda, history):
         case["pool"].close()
 
 
-@pytest.mark.parametrize("history", [1000, 1024])
-def test_model_candidates_match_separate_extends(cuda, history):
+@pytest.mark.parametrize("history,compression", [(1000, "mean"), (1024, "mean"),
+                                                 (1000, "mlp"), (1024, "mlp")])
+def test_model_candidates_match_separate_extends(cuda, history, compression):
     """A segmented extend of 3 candidates against each candidate extended on
     its own, and against itself with the candidates rotated over the
     segments. Both comparisons change the GEMM batch or row placement, so
@@ -219,7 +220,8 @@ def test_model_candidates_match_separate_extends(cuda, history):
     captured graph equal to the eager step bit for bit."""
     from cxlsparse_b200.model import NSAConfig, NSAExtendModel
 
-    cfg = NSAConfig(layers=2, hot=64)
+    cfg = (NSAConfig(layers=2, hot=64) if compression == "mean"
+           else NSAConfig.baseline(layers=2, hot=64))
     extend, candidates = 64, 3
     model = NSAExtendModel(cfg, device=cuda, seed=0, max_history=history + extend, chunk=512,
                            workspaces=8)
