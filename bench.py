@@ -14,6 +14,7 @@ torch NSA path (restated in oracle/nsa_cpu.py) on the host cores instead.
 """
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -144,7 +145,7 @@ def dist_setup(torch):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 
@@ -615,7 +616,13 @@ def run_serving(args):
         }
         print(json.dumps(result))
     if dist is not None:
+        # Every captured graph (they hold NCCL calls in the head split) must
+        # be released before the process group is destroyed, or the exit
+        # waits for good: drop the last loop references as well.
+        graph = static_ids = static_out = None
         captured.clear()
+        gc.collect()
+        torch.cuda.synchronize(device)
         dist.barrier()
         dist.destroy_process_group()
     model.close()
@@ -769,7 +776,13 @@ def run_headsplit(args):
             "clocks": clocks, "prefill_s_rank0": prefill_s,
         }))
     if dist is not None:
+        # Every captured graph (they hold NCCL calls in the head split) must
+        # be released before the process group is destroyed, or the exit
+        # waits for good: drop the last loop references as well.
+        graph = static_ids = static_out = None
         captured.clear()
+        gc.collect()
+        torch.cuda.synchronize(device)
         dist.barrier()
         dist.destroy_process_group()
     model.close()
