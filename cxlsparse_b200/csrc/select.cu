@@ -75,6 +75,16 @@ struct RowGeo {
   int current = -1, previous = -1, first = -1;  // block ids of the true current,
                                                 // previous and first blocks
   __device__ __forceinline__ bool key_visible(int c) const { return c < nc && !keys.hides(c); }
+  // Bit i: key slot col0 + i visible (one mask per 32 columns, so that the
+  // unrolled column loops test a bit instead of three bounds).
+  __device__ __forceinline__ uint32_t visible_bits(int col0) const {
+    auto below = [](int n) -> uint32_t {
+      return n <= 0 ? 0u : (n >= 32 ? 0xffffffffu : (1u << n) - 1u);
+    };
+    uint32_t m = below(nc - col0);
+    if (keys.hi > keys.lo) m &= ~(below(keys.hi - col0) & ~below(keys.lo - col0));
+    return m;
+  }
 };
 
 __device__ __forceinline__ RowGeo row_geo(const SelectArgs& a, int pos) {
@@ -455,7 +465,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const bool row_ok = q < a.Q;
   const int pos = row_ok ? a.positions[q] : -1;
   const RowGeo rg = row_geo(a, pos);
-  auto visible = [&](int c) { return rg.key_visible(c); };
   const long long qrow = ((long long)q * H + h) * cxs::kGroups + g;  // [Q, H, 16] row index
 #pragma unroll
   for (int c = 2 * cq; c < 2 * cq + 2; ++c) {
@@ -539,11 +548,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::ld32(s_addr + 64 * cq + 32, v1);
     }
     float mt = -INFINITY;
+    const uint32_t vis0 = rg.visible_bits(col0), vis1 = rg.visible_bits(col0 + 32);
     if (mine) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        if (visible(col0 + i)) mt = fmaxf(mt, v0[i]);
-        if (visible(col0 + 32 + i)) mt = fmaxf(mt, v1[i]);
+        if ((vis0 >> i) & 1u) mt = fmaxf(mt, v0[i]);
+        if ((vis1 >> i) & 1u) mt = fmaxf(mt, v1[i]);
       }
     }
     red_max[cq * 128 + m] = mt;
@@ -555,8 +565,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (mine) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        if (visible(col0 + i)) sum += tc::ex2(fmaf(v0[i], tc::kLog2e, -off));
-        if (visible(col0 + 32 + i)) sum += tc::ex2(fmaf(v1[i], tc::kLog2e, -off));
+        if ((vis0 >> i) & 1u) sum += tc::ex2(fmaf(v0[i], tc::kLog2e, -off));
+        if ((vis1 >> i) & 1u) sum += tc::ex2(fmaf(v1[i], tc::kLog2e, -off));
       }
     }
     red_sum[cq * 128 + m] = sum;
@@ -593,9 +603,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int col0 = kTcChunk * j + 64 * cq + 32 * half;
         float v[32];
         tc::ld32(s_addr + 64 * cq + 32 * half, v);
+        const uint32_t vis = rg.visible_bits(col0);
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          v[i] = visible(col0 + i) ? tc::ex2(fmaf(v[i], tc::kLog2e, -offset)) : 0.f;
+          v[i] = (vis >> i) & 1u ? tc::ex2(fmaf(v[i], tc::kLog2e, -offset)) : 0.f;
         // P (bf16): 16-byte chunks 4 half .. 4 half + 3 of row m of sub-tile cq.
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
