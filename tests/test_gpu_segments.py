@@ -6,9 +6,10 @@ blocks deduplicated across candidates), its sliding window (history tail +
 own suffix) and the gate mix. Checked against the CPU oracle run per
 candidate in true positions (rtol = atol = 0.03, the reference's tolerance,
 tests/test_nsa_tma_transport.py:39-41), selections bit-exactly against the
-ordering rule applied to the kernel's own scores, and, end to end, a
-segmented extend of the model against separate single-candidate extends
-(bf16 tolerance 2e-2).
+ordering rule applied to the kernel's own scores, rotations of the
+candidates over the segments bit-exactly at the transport level, and, end
+to end, a segmented extend of the model against separate single-candidate
+extends (statistically: the batch shapes differ, see that test).
 """
 
 import pytest
