@@ -28,7 +28,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "NSA-1B extend tok/s @H16K/E256 at 1–8 B200; KV-fetch GB/s vs PCIe5 peak"
-REFERENCE_TOK_S = 13503.0  # derived H100 worker tok/s @H16K/E256 (E / worker p50)
+# The reference's published H100 result at H16K/E256, as extend tok/s: E = 256
+# tokens over the 18.959 ms worker p50 of results/final/summary.csv.
+REFERENCE_TOK_S = 13503.0
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # fetch_attend_kernel<64> launch of the H=16384/E=256 extend step, from an
