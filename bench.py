@@ -653,7 +653,7 @@ def run_headsplit(args):
     import torch
 
     from cxlsparse_b200.model import NSAConfig, NSAExtendModel
-    from cxlsparse_b200.sharding import gather_scores, head_exchange, head_pair_groups
+    from cxlsparse_b200.sharding import PeerExchange, gather_scores, head_pair_groups
     from cxlsparse_b200.sharding import users_for_rank
 
     if args.warmup < 3:
@@ -667,11 +667,16 @@ def run_headsplit(args):
     mine = users_for_rank(list(range(users_total)), pair, pairs)
     suffix = args.queries * args.extend
     segments = 1 if args.packed else args.queries
+    exchange = None
+    if shards > 1:
+        exchange = PeerExchange(group, shard, shards, rows=4096, kv_heads=cfg.kv_heads,
+                                kv_local=cfg.kv_heads // shards, device=device,
+                                spin_limit=1 << 31)
     model = NSAExtendModel(cfg, device=device, seed=0, max_users=len(mine),
                            max_history=args.history + suffix + 64 * segments,
                            read_order=args.read_order,
                            workspaces=cfg.layers * len(mine) + 4, head_shard=(shard, shards),
-                           exchange=head_exchange(group, shards) if shards > 1 else None,
+                           exchange=exchange,
                            **model_options(args))
     t0 = time.perf_counter()
     candidates = {}
@@ -718,6 +723,8 @@ def run_headsplit(args):
     errors = [int(c.device_error.item()) for u in mine for c in captured[u][3]]
     if any(errors) or stats[..., 6].any():
         raise RuntimeError(f"device plan/attend errors: {errors}")
+    if exchange is not None:
+        exchange.check()
     fetched = int(stats[..., 3].sum()) * 256
     sampler = ClockSampler(local)
     barrier()
@@ -764,8 +771,9 @@ def run_headsplit(args):
                        "layers": args.layers, "block_size": 64, "top_n": 16, "window": 512,
                        "compression": compression_config(args),
                        "hot": hot_config(args),
-                       "exchange": "NCCL all-gather of the [E, 16, 64] attention output per "
-                                   "layer within the pair (inside the captured graph)",
+                       "exchange": "attention epilogue stores each output row into both GPUs' "
+                                   "gather buffers over NVLink (CUDA IPC), then a bounded "
+                                   "flag barrier per layer (inside the captured graph)",
                        "parallelism": f"{pairs} pair(s) x 2 KV-head shards" if shards > 1
                        else "1 GPU, both KV heads local"},
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s",
@@ -785,6 +793,8 @@ def run_headsplit(args):
         captured.clear()
         gc.collect()
         torch.cuda.synchronize(device)
+        exchange.check()
+        exchange.close()
         dist.barrier()
         dist.destroy_process_group()
     model.close()

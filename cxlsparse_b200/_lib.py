@@ -63,7 +63,8 @@ class AttendGeometry(ctypes.Structure):
     _fields_ = [(name, c_i32) for name in (
         "queries", "heads", "width", "block_size", "physical", "window", "window_len",
         "gate")] + [(name, c_i64) for name in (
-            "window_start", "spin_limit", "segment_start", "segment_tokens")]
+            "window_start", "spin_limit", "segment_start", "segment_tokens")] + [
+        ("out_heads", c_i32), ("out_head0", c_i32)]
 
 
 class SelectGeometry(ctypes.Structure):
@@ -75,7 +76,7 @@ class SelectGeometry(ctypes.Structure):
 ATTEND_BUFFER_FIELDS = (
     "query", "kv", "all_ids", "all_counts", "row_positions", "starts", "valid", "flags",
     "ioids", "missing", "address", "sources", "kinds", "ready", "control", "error",
-    "window_kv", "compressed", "gates", "out",
+    "window_kv", "compressed", "gates", "out", "out_peer",
 )
 
 
@@ -141,6 +142,13 @@ def lib():
                                               c_vp, c_vp, c_i32, c_vp, c_i32, c_vp, c_i32,
                                               c_i32, c_vp]),
             "cxs_silu_mul": (c_i32, [c_vp, c_i32, c_i32, c_vp, c_vp]),
+            "cxs_device_alloc": (c_i32, [ctypes.c_size_t, ctypes.POINTER(c_vp)]),
+            "cxs_device_free": (c_i32, [c_vp]),
+            "cxs_ipc_get_handle": (c_i32, [c_vp, c_vp]),
+            "cxs_ipc_open_handle": (c_i32, [c_vp, ctypes.POINTER(c_vp)]),
+            "cxs_ipc_close": (c_i32, [c_vp]),
+            "cxs_exchange_barrier": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_i64, c_vp,
+                                             c_vp]),
         }
         for name, (restype, argtypes) in sigs.items():
             fn = getattr(handle, name)
@@ -184,4 +192,6 @@ def exported_symbols():
             "cxs_compressed_select", "cxs_compressed_select_segments",
             "cxs_compressed_select_nsa", "cxs_select_score_columns",
             "cxs_block_summaries", "cxs_block_summaries_segments", "cxs_rms_norm",
-            "cxs_qkv_rope", "cxs_qkv_rope_segments", "cxs_silu_mul")
+            "cxs_qkv_rope", "cxs_qkv_rope_segments", "cxs_silu_mul", "cxs_device_alloc",
+            "cxs_device_free", "cxs_ipc_get_handle", "cxs_ipc_open_handle", "cxs_ipc_close",
+            "cxs_exchange_barrier")

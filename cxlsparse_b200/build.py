@@ -12,7 +12,7 @@ from pathlib import Path
 
 PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
-SOURCES = ["capi.cu", "planner.cu", "attend.cu", "select.cu", "glue.cu"]
+SOURCES = ["capi.cu", "planner.cu", "attend.cu", "select.cu", "glue.cu", "exchange.cu"]
 LIBRARY = PACKAGE / "libcxlsparse_b200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -49,6 +49,8 @@ struct AttendArgs {
   const __nv_bfloat16* compressed;
   const __nv_bfloat16* gates;
   __nv_bfloat16* out;
+  __nv_bfloat16* out_peer;  // optional second copy of every output row (a peer GPU's buffer)
+  int out_heads, out_head0;  // output row of (q, h): q * out_heads + out_head0 + h
 };
 
 // Warp gather of one BS-token block: token t comes from address[t] (HBM or
@@ -412,7 +414,10 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
     }
     const long long off = ((long long)row * 16 + (lane & 15)) * 64 + 32 * half;
     const float den = l_run > 0.f ? l_run : 1.f;
-    uint4* dst = reinterpret_cast<uint4*>(a.out + off);
+    const long long out_row = (long long)(row / a.H) * a.out_heads + a.out_head0 + row % a.H;
+    const long long ooff = (out_row * 16 + (lane & 15)) * 64 + 32 * half;
+    uint4* dst = reinterpret_cast<uint4*>(a.out + ooff);
+    uint4* peer = a.out_peer ? reinterpret_cast<uint4*>(a.out_peer + ooff) : nullptr;
     if (!a.gate) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -422,6 +427,7 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
           r[e] = cxs::pack_bf16(bf16_round(o[8 * c + 2 * e] / den),
                                 bf16_round(o[8 * c + 2 * e + 1] / den));
         dst[c] = make_uint4(r[0], r[1], r[2], r[3]);
+        if (peer) peer[c] = make_uint4(r[0], r[1], r[2], r[3]);
       }
     } else {
       // Gate mix in the reference's bf16 rounding sequence (model.py:470-473).
@@ -446,8 +452,12 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
           r[e] = cxs::pack_bf16(x0 + w2.x * g2, x1 + w2.y * g2);
         }
         dst[c] = make_uint4(r[0], r[1], r[2], r[3]);
+        if (peer) peer[c] = make_uint4(r[0], r[1], r[2], r[3]);
       }
     }
+    // Peer stores travel over NVLink: make them visible system-wide before
+    // the exchange barrier that follows this launch announces them.
+    if (peer) __threadfence_system();
     __syncwarp();  // TMEM reads done before the next row's MMAs
   }
 }
@@ -686,6 +696,9 @@ int launch(const cxs_attend_geometry& g, const cxs_attend_buffers& b, cudaStream
   a.compressed = (const __nv_bfloat16*)b.compressed;
   a.gates = (const __nv_bfloat16*)b.gates;
   a.out = (__nv_bfloat16*)b.out;
+  a.out_peer = (__nv_bfloat16*)b.out_peer;
+  a.out_heads = g.out_heads > 0 ? g.out_heads : g.heads;
+  a.out_head0 = g.out_heads > 0 ? g.out_head0 : 0;
 
   int prep_grid = (g.physical + 7) / 8;
   prepare_kernel<<<prep_grid > 0 ? prep_grid : 1, 256, 0, stream>>>(
@@ -738,6 +751,10 @@ extern "C" int cxs_fetch_attend(const cxs_attend_geometry* geometry,
     return set_error(CXS_ERR_INVALID, "kv/query/out must be 16-byte aligned");
   if (g.window > 0 && ((uintptr_t)b.window_kv & 15))
     return set_error(CXS_ERR_INVALID, "window buffer must be 16-byte aligned");
+  if (g.out_heads < 0 || (g.out_heads > 0 && (g.out_head0 < 0 ||
+                                              g.out_head0 + g.heads > g.out_heads)))
+    return set_error(CXS_ERR_INVALID, "output heads must hold this call's heads");
+  if ((uintptr_t)b.out_peer & 15) return set_error(CXS_ERR_INVALID, "out_peer must be 16-byte aligned");
   switch (g.block_size) {
     case 16: return launch<16>(g, b, (cudaStream_t)stream);
     case 32: return launch<32>(g, b, (cudaStream_t)stream);

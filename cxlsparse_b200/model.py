@@ -147,14 +147,17 @@ class NSAExtendModel:
         self.device = torch.device(device)
         # KV-head sharding: this instance owns KV heads
         # [head0, head0 + kv_local) of every layer (their query heads, pool
-        # slice, cache rows, planner and attention); `exchange` turns the
-        # local attention output [E, kv_local, 16, 64] into all heads'
-        # [E, kv_heads, 16, 64] (an all-gather across the shard group).
+        # slice, cache rows, planner and attention); `exchange`
+        # (sharding.PeerExchange) receives every layer's attention rows of all
+        # heads: the attention launch stores this rank's rows into both GPUs'
+        # gather buffers and the exchange barrier waits for the peer's.
         shard, shards = head_shard
         if shards < 1 or cfg.kv_heads % shards or not 0 <= shard < shards:
             raise ValueError("head_shard must split the KV heads evenly")
         if shards > 1 and exchange is None:
             raise ValueError("a head-sharded model needs an exchange")
+        if exchange is not None and cfg.layers % 2:
+            raise ValueError("the peer exchange alternates buffers by layer: even layer count")
         self.kv_local = cfg.kv_heads // shards
         self.head0 = shard * self.kv_local
         self.exchange = exchange
@@ -253,12 +256,14 @@ class NSAExtendModel:
         base = st.row + index * self.kv_local
         fetches = [dict(row=base + h, cached_length=old, history_length=old,
                         current_kv=records[:, h].contiguous()) for h in range(self.kv_local)]
+        target = None if self.exchange is None else self.exchange.targets(index, len(hidden))
         mixed, counters = self.transport.run(
             query, blocks, positions, fetches, cfg.block_size, window=cfg.window,
-            window_kv=window_kv, window_start=window_start, compressed=cmp_out, gates=gates)
+            window_kv=window_kv, window_start=window_start, compressed=cmp_out, gates=gates,
+            output=target)
         self.counters.append(counters)
-        if self.exchange is not None:
-            mixed = self.exchange(mixed)
+        if target is not None:
+            self.exchange.barrier(torch.cuda.current_stream(self.device).cuda_stream)
         hidden = hidden + F.linear(mixed.reshape(len(hidden), -1), w["o"])
         x = rms_norm(hidden, w["post_norm"], cfg.rms_eps)
         hidden = hidden + F.linear(F.silu(F.linear(x, w["gate"])) * F.linear(x, w["up"]),
@@ -541,13 +546,14 @@ class NSAExtendModel:
         if self.probe is not None:  # comparison plan on the same selections / cache state
             self.probe_counters.append(self.probe.plan_only(
                 query, blocks, positions, L["fetches"], cfg.block_size, workspace_id=index))
+        target = None if self.exchange is None else self.exchange.targets(index, E)
         mixed, counters = self.transport.run(
             query, blocks, positions, L["fetches"], cfg.block_size, window=cfg.window,
             window_kv=L["window_buf"], window_start=L["window_start"], compressed=cmp_out,
-            gates=gates, workspace_id=index, segments=segments)
+            gates=gates, workspace_id=index, segments=segments, output=target)
         self.counters.append(counters)
-        if self.exchange is not None:
-            mixed = self.exchange(mixed)
+        if target is not None:
+            self.exchange.barrier(stream)
         hidden = torch.addmm(hidden, mixed.reshape(E, -1), w["o"].t())
         _lib.check(lib.cxs_rms_norm(hidden.data_ptr(), w["post_norm"].data_ptr(), x.data_ptr(),
                                     E, cfg.hidden, cfg.rms_eps, stream))

@@ -265,16 +265,23 @@ class GRSelectedTransport:
         b.gates = _lib.ptr(gates)
         w["binding"] = "direct"
 
-    def _execute(self, w, window_start, window, defer_hot=False, segments=(0, 0)):
+    def _execute(self, w, window_start, window, defer_hot=False, segments=(0, 0), output=None):
         stream = torch.cuda.current_stream(self.cache.data.device)
         self.active_plan.plan(w, stream, defer_hot=defer_hot)
+        buffers = w["c_attend_buffers"]
+        out_heads = out_head0 = 0
+        if output is None:
+            buffers.out, buffers.out_peer = w["output"].data_ptr(), None
+        else:
+            local, peer, out_heads, out_head0 = output
+            buffers.out, buffers.out_peer = local.data_ptr(), peer
         geometry = _lib.AttendGeometry(
             queries=w["queries"], heads=w["heads"], width=w["width"], block_size=w["bs"],
             physical=w["physical"], window=window if w["window_shape"] else 0,
             window_len=w["window_shape"][0] if w["window_shape"] else 0,
             gate=1 if w["window_shape"] else 0, window_start=window_start,
             spin_limit=self.spin_limit, segment_start=segments[0],
-            segment_tokens=segments[1])
+            segment_tokens=segments[1], out_heads=out_heads, out_head0=out_head0)
         timing = self.kernel_timing is not None and not torch.cuda.is_current_stream_capturing()
         if timing:
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -288,7 +295,7 @@ class GRSelectedTransport:
     # -- main entry --------------------------------------------------------
     def run(self, query, blocks, positions, fetches, block_size, *, trace=False,
             window=None, window_kv=None, window_start=0, compressed=None, gates=None,
-            workspace_id=None, segments=None):
+            workspace_id=None, segments=None, output=None):
         """Reference ``run`` plus the fused branches and, optionally, candidate
         segments: ``segments=(segment_start, segment_tokens)`` says that
         ``positions``, ``blocks``, the window buffer and each fetch's
@@ -297,10 +304,18 @@ class GRSelectedTransport:
         ``segment_start`` and its own suffix only). The plan needs nothing
         else: history blocks deduplicate across candidates, suffix blocks
         stay private to their candidate. ``fetches[h]["cached_length"]`` and
-        ``history_length`` must then equal ``segment_start``."""
+        ``history_length`` must then equal ``segment_start``.
+
+        ``output=(local, peer, out_heads, out_head0)`` routes the attention
+        rows of this call's heads into `local` [Q', out_heads, 16, 64] at head
+        offset out_head0 and stores the same rows at the device address
+        `peer` (a GPU pair's NVLink exchange, ``sharding.PeerExchange``); the
+        call then returns `local`."""
         if trace:
             raise ValueError("Collect device activity separately from GR timing")
         segments = tuple(int(x) for x in segments) if segments else (0, 0)
+        if output is not None and self.cuda_graphs:
+            raise ValueError("an output override needs the caller's own graph capture")
         if segments[1]:
             if (segments[0] % block_size or segments[1] % block_size or segments[0] < 0
                     or segments[1] < 0):
@@ -401,7 +416,8 @@ class GRSelectedTransport:
             w["graph"].replay()
             self.replays += 1
         else:
-            self._execute(w, window_start, window, defer_hot=async_hot, segments=segments)
+            self._execute(w, window_start, window, defer_hot=async_hot, segments=segments,
+                          output=output)
         if workspace_id is None:
             counters = DeferredLayerCounters(w["stats"].clone(), 1, self.pool.backend,
                                              w["error"].clone())
@@ -439,7 +455,7 @@ class GRSelectedTransport:
             persistent_mapping_bytes=w["persistent_mapping_bytes"],
             total_submit_wall_ms=(time.perf_counter_ns() - begin) / 1e6,
         )
-        return w["output"][:q_count], counters
+        return (w["output"] if output is None else output[0])[:q_count], counters
 
     def plan_only(self, query, blocks, positions, fetches, block_size, *, workspace_id=None):
         """Run only the fetch planner on these selections (no IO, attention or

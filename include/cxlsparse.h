@@ -240,6 +240,8 @@ typedef struct cxs_attend_geometry {
   int64_t spin_limit;   /* clock cycles before a bounded wait gives up */
   int64_t segment_start;  /* candidate segments (0, 0: one suffix): see below */
   int64_t segment_tokens;
+  int32_t out_heads;  /* 0: `out` is [Q, H, 16, 64]; else [Q, out_heads, 16, 64] and this */
+  int32_t out_head0;  /* call's heads are out_head0 .. out_head0 + H - 1 (KV-head split) */
 } cxs_attend_geometry;
 
 typedef struct cxs_attend_buffers {
@@ -262,7 +264,10 @@ typedef struct cxs_attend_buffers {
   const void* window_kv;     /* [window_len, H, 128] bf16 or NULL */
   const void* compressed;    /* [Q, H, 16, 64] bf16 compressed-branch output (gate) */
   const void* gates;         /* [Q, H, 16, 3] bf16 sigmoid gates (gate) */
-  void* out;                 /* [Q, H, 16, 64] bf16 */
+  void* out;                 /* [Q, H, 16, 64] bf16 (or out_heads, see the geometry) */
+  void* out_peer;            /* NULL, or a peer GPU's buffer of the same layout: every
+                                output row is also stored there over NVLink (KV-head
+                                split exchange; see cxs_exchange_barrier) */
 } cxs_attend_buffers;
 
 int cxs_fetch_attend(const cxs_attend_geometry* geometry, const cxs_attend_buffers* buffers,
@@ -294,6 +299,34 @@ int cxs_attend_capacity(int32_t block_size, int32_t* attention_warps);
 #define CXS_NOALLOC_MAX_PHYSICAL 16384
 int cxs_fetch_attend_noalloc(const cxs_attend_geometry* geometry,
                              const cxs_attend_buffers* buffers, void* stream);
+
+/* ------------------------------------------------ KV-head split exchange ---
+ * The reference is single-GPU. When the two KV heads of a user are split over
+ * a GPU pair, each attention launch stores its output rows into its own and
+ * its peer's gather buffer (cxs_attend_buffers.out_peer, NVLink stores), and
+ * cxs_exchange_barrier then tells the peer that its rows have landed and waits
+ * (bounded) for the peer's. Buffers are shared with CUDA IPC.
+ */
+/* Device allocation outside any caching allocator (its base pointer can be
+ * exported with cxs_ipc_get_handle). */
+int cxs_device_alloc(size_t bytes, void** ptr);
+int cxs_device_free(void* ptr);
+/* Export / import a cxs_device_alloc allocation between processes (64-byte
+ * handle); the import is mapped on the current device with peer access. */
+int cxs_ipc_get_handle(const void* ptr, void* handle);
+int cxs_ipc_open_handle(const void* handle, void** ptr);
+int cxs_ipc_close(void* ptr);
+/* One exchange step of rank `rank` out of `ranks` (at most 8): the step
+ * number is *counter + 1 (device int32, updated in place); the kernel makes
+ * this rank's earlier stores visible system-wide, writes the step into slot
+ * `rank` of every peer's flag array (peer_flags[p], int32 [ranks], mapped
+ * from that peer; entry `rank` itself is ignored) with release semantics,
+ * then waits with acquire loads until every peer's slot in this rank's own
+ * `flags` reaches the step, giving up after `spin_limit` clock cycles with
+ * CXS_DEVICE_ERR_READY_TIMEOUT in `error`. Graph-capturable. */
+int cxs_exchange_barrier(int32_t* counter, int32_t* const* peer_flags, int32_t* flags,
+                         int32_t rank, int32_t ranks, int64_t spin_limit, int32_t* error,
+                         void* stream);
 
 /* -------------------------------------------- compressed branch + top-n ---
  * Compressed-token attention over complete summaries and top-n block

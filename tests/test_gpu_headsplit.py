@@ -1,10 +1,11 @@
 """KV-head split across a GPU pair (BASELINE configs[4] layout, scaled down).
 
 Rank i of the pair owns KV head i of every layer: its 16 query heads, its own
-pool slice, cache rows, planner, fetch and attention; the attention outputs
-are all-gathered once per layer (NCCL) before o_proj. The pair's extend must
-reproduce the single-GPU model that holds both heads, eagerly and from a
-captured graph that contains the collectives. Needs two GPUs.
+pool slice, cache rows, planner, fetch and attention; each attention launch
+stores its output rows into both GPUs' gather buffers (NVLink stores, CUDA
+IPC) and a bounded flag barrier per layer hands them over before o_proj. The
+pair's extend must reproduce the single-GPU model that holds both heads,
+eagerly and from a captured graph that contains the exchange. Needs two GPUs.
 """
 
 import os
@@ -37,7 +38,7 @@ def _rank(rank, port, results):
     import torch.distributed as dist
 
     from cxlsparse_b200.model import NSAConfig, NSAExtendModel
-    from cxlsparse_b200.sharding import head_exchange, head_pair_groups
+    from cxlsparse_b200.sharding import PeerExchange, head_pair_groups
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     device = torch.device("cuda", rank)
@@ -47,9 +48,12 @@ def _rank(rank, port, results):
     try:
         group, shard, shards, _, _ = head_pair_groups(2)
         cfg = NSAConfig(layers=LAYERS, hot=64)
+        # About half a second per wait: a peer that never arrives sets the
+        # error word instead of holding the GPU.
+        exchange = PeerExchange(group, shard, shards, rows=1024, kv_heads=cfg.kv_heads,
+                                kv_local=1, device=device, spin_limit=1 << 30)
         model = NSAExtendModel(cfg, device=device, seed=0, max_history=HISTORY + EXTEND,
-                               chunk=512, head_shard=(shard, shards),
-                               exchange=head_exchange(group, shards))
+                               chunk=512, head_shard=(shard, shards), exchange=exchange)
         history, ids = _inputs(cfg.vocab)
         model.prefill(history.to(device))
         eager = model.extend(ids.to(device)).float().cpu()
@@ -58,9 +62,11 @@ def _rank(rank, port, results):
         graph.replay()
         torch.cuda.synchronize()
         misses = sum(r[0]["misses"] for c in counters for r in [c.materialize()])
+        exchange.check()
         results[rank] = (eager, static_out.float().cpu(), misses)
         del graph
         model.close()
+        exchange.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
