@@ -142,6 +142,8 @@ def lib():
                                               c_vp, c_vp, c_i32, c_vp, c_i32, c_vp, c_i32,
                                               c_i32, c_vp]),
             "cxs_silu_mul": (c_i32, [c_vp, c_i32, c_i32, c_vp, c_vp]),
+            "cxs_compress_windows": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp,
+                                             c_vp, c_vp, c_vp, c_vp, c_vp]),
             "cxs_device_alloc": (c_i32, [ctypes.c_size_t, ctypes.POINTER(c_vp)]),
             "cxs_device_free": (c_i32, [c_vp]),
             "cxs_ipc_get_handle": (c_i32, [c_vp, c_vp]),
@@ -192,6 +194,7 @@ def exported_symbols():
             "cxs_compressed_select", "cxs_compressed_select_segments",
             "cxs_compressed_select_nsa", "cxs_select_score_columns",
             "cxs_block_summaries", "cxs_block_summaries_segments", "cxs_rms_norm",
-            "cxs_qkv_rope", "cxs_qkv_rope_segments", "cxs_silu_mul", "cxs_device_alloc",
+            "cxs_qkv_rope", "cxs_qkv_rope_segments", "cxs_silu_mul", "cxs_compress_windows",
+            "cxs_device_alloc",
             "cxs_device_free", "cxs_ipc_get_handle", "cxs_ipc_open_handle", "cxs_ipc_close",
             "cxs_exchange_barrier")

@@ -178,7 +178,178 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gate_up, int f
   o[col] = __float2bfloat16_rn(s * __bfloat162float(p[ffn + col]));
 }
 
+// Window compression, stage 1: act = bf16(silu(bf16(W1 vec(x)))) for every
+// window, x = bf16(window records + position encoding) (one K or V half).
+// CTA (unit chunk, head, part) owns kCmpUnits hidden units; windows go
+// through shared memory in tiles of kCmpTile, so every W1 row is read once
+// per tile and reused for all of its windows; a lane keeps the CPL 16-byte
+// chunks of the row it needs in registers (all loads in flight together).
+constexpr int kCmpTile = 16;
+constexpr int kCmpUnits = 16;
+constexpr int kCmpWarps = 8;
+
+template <int CPL>
+__global__ void __launch_bounds__(kCmpWarps * 32, 1)
+    compress_hidden_kernel(const __nv_bfloat16* __restrict__ records,
+                           const int64_t* __restrict__ rows, int n, int heads, int hidden,
+                           const __nv_bfloat16* __restrict__ pe,
+                           const __nv_bfloat16* __restrict__ w1, float* __restrict__ act) {
+  extern __shared__ uint4 xs[];  // [kCmpTile][in / 8]: bf16 x, 8 values per chunk
+  constexpr int kIn = CPL * 256, kChunks = kIn / 8, kL = kIn / 64;
+  static_assert(kChunks == kCmpWarps * 32, "one staged chunk per thread");
+  const int part = blockIdx.z, h = blockIdx.y, j0 = blockIdx.x * kCmpUnits;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint4* pe_p = reinterpret_cast<const uint4*>(pe + (long long)part * kIn);
+  // Thread k stages chunk k (8 channels of token k / 8) of every window of the
+  // tile: the row indices, then the records, all loads issued before use.
+  const int k = threadIdx.x, t = k / 8, c8 = (k % 8) * 8;
+  float q[8];
+  unpack8(pe_p[k], q);
+  for (int w0 = 0; w0 < n; w0 += kCmpTile) {
+    const int nt = min(kCmpTile, n - w0);
+    long long row[kCmpTile];
+#pragma unroll
+    for (int w = 0; w < kCmpTile; ++w) row[w] = w < nt ? rows[(long long)(w0 + w) * kL + t] : 0;
+    uint4 rv[kCmpTile];
+#pragma unroll
+    for (int w = 0; w < kCmpTile; ++w)
+      if (w < nt)
+        rv[w] = *reinterpret_cast<const uint4*>(records + (row[w] * heads + h) * 128 +
+                                                part * 64 + c8);
+#pragma unroll
+    for (int w = 0; w < kCmpTile; ++w) {
+      if (w < nt) {
+        float r[8];
+        unpack8(rv[w], r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) r[e] += q[e];
+        xs[w * kChunks + k] = pack8(r);  // rounded to bf16, as the reference adds bf16 tensors
+      }
+    }
+    __syncthreads();
+    for (int u = warp; u < kCmpUnits; u += kCmpWarps) {
+      const int j = j0 + u;
+      if (j >= hidden) break;
+      const uint4* wr = reinterpret_cast<const uint4*>(w1 + ((long long)part * hidden + j) * kIn);
+      uint4 wv[CPL];
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) wv[c] = wr[lane + 32 * c];
+      float acc[kCmpTile];
+#pragma unroll
+      for (int w = 0; w < kCmpTile; ++w) acc[w] = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        float wf[8];
+        unpack8(wv[c], wf);
+#pragma unroll
+        for (int w = 0; w < kCmpTile; ++w) {
+          if (w < nt) {
+            float xf[8];
+            unpack8(xs[w * kChunks + lane + 32 * c], xf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[w] = fmaf(wf[e], xf[e], acc[w]);
+          }
+        }
+      }
+      float mine = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCmpTile; ++w) {
+        float v = acc[w];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (w == lane) mine = v;
+      }
+      if (lane < nt) {
+        const float hv = rbf(mine);
+        act[(((long long)part * heads + h) * n + w0 + lane) * hidden + j] =
+            rbf(hv / (1.f + expf(-hv)));
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Stage 2: key half = bf16(W2 act) into key slot slots[window]. CTA (window,
+// head, part) of 4 warps; warp w computes outputs 16 w .. 16 w + 15, lanes
+// split the hidden units, and the 16 W2 chunks of a lane load together.
+constexpr int kOutPerWarp = 16;
+
+__global__ void __launch_bounds__(128)
+    compress_out_kernel(int n, int heads, int hidden, const __nv_bfloat16* __restrict__ w2,
+                        const float* __restrict__ act, __nv_bfloat16* __restrict__ keys,
+                        const int64_t* __restrict__ slots) {
+  const int window = blockIdx.x, h = blockIdx.y, part = blockIdx.z;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const float4* a = reinterpret_cast<const float4*>(
+      act + (((long long)part * heads + h) * n + window) * hidden);
+  const int c0 = warp * kOutPerWarp;
+  const uint4* wbase = reinterpret_cast<const uint4*>(w2 + ((long long)part * 64 + c0) * hidden);
+  const int chunks = hidden / 8;
+  float acc[kOutPerWarp];
+#pragma unroll
+  for (int u = 0; u < kOutPerWarp; ++u) acc[u] = 0.f;
+  for (int k = lane; k < chunks; k += 32) {
+    const float4 a0 = a[2 * k], a1 = a[2 * k + 1];
+    uint4 wv[kOutPerWarp];
+#pragma unroll
+    for (int u = 0; u < kOutPerWarp; ++u) wv[u] = wbase[(long long)u * chunks + k];
+#pragma unroll
+    for (int u = 0; u < kOutPerWarp; ++u) {
+      float wf[8];
+      unpack8(wv[u], wf);
+      acc[u] = fmaf(wf[0], a0.x, acc[u]);
+      acc[u] = fmaf(wf[1], a0.y, acc[u]);
+      acc[u] = fmaf(wf[2], a0.z, acc[u]);
+      acc[u] = fmaf(wf[3], a0.w, acc[u]);
+      acc[u] = fmaf(wf[4], a1.x, acc[u]);
+      acc[u] = fmaf(wf[5], a1.y, acc[u]);
+      acc[u] = fmaf(wf[6], a1.z, acc[u]);
+      acc[u] = fmaf(wf[7], a1.w, acc[u]);
+    }
+  }
+  float mine = 0.f;
+#pragma unroll
+  for (int u = 0; u < kOutPerWarp; ++u) {
+    float v = acc[u];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (u == lane) mine = v;
+  }
+  if (lane < kOutPerWarp)
+    keys[(slots[window] * heads + h) * 128 + part * 64 + c0 + lane] = __float2bfloat16_rn(mine);
+}
+
 }  // namespace
+
+extern "C" int cxs_compress_windows(const void* records, const int64_t* rows, int32_t windows,
+                                    int32_t heads, int32_t window, int32_t hidden,
+                                    const void* pe, const void* w1, const void* w2,
+                                    void* scratch, void* keys, const int64_t* slots,
+                                    void* stream) {
+  if (windows < 0 || heads < 1 || heads > 65535 || hidden < 8 || hidden % 8 || window != 32)
+    return set_error(CXS_ERR_INVALID, "window-compression geometry: window 32, "
+                                      "hidden a multiple of 8");
+  if (!windows) return CXS_OK;
+  if (!records || !rows || !pe || !w1 || !w2 || !scratch || !keys || !slots)
+    return set_error(CXS_ERR_INVALID, "null window-compression argument");
+  if (((uintptr_t)records | (uintptr_t)pe | (uintptr_t)w1 | (uintptr_t)w2 |
+       (uintptr_t)scratch) & 15)
+    return set_error(CXS_ERR_INVALID, "window-compression buffers must be 16-byte aligned");
+  const int in = window * 64;
+  const size_t smem = (size_t)kCmpTile * in * 2;
+  dim3 grid1((hidden + kCmpUnits - 1) / kCmpUnits, heads, 2);
+  auto* act = static_cast<float*>(scratch);
+  CXS_CUDA(cudaFuncSetAttribute(compress_hidden_kernel<8>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  compress_hidden_kernel<8><<<grid1, kCmpWarps * 32, smem, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)records, rows, windows, heads, hidden, (const __nv_bfloat16*)pe,
+      (const __nv_bfloat16*)w1, act);
+  CXS_LAUNCH_CHECK("compress_hidden_kernel");
+  compress_out_kernel<<<dim3(windows, heads, 2), 128, 0, (cudaStream_t)stream>>>(
+      windows, heads, hidden, (const __nv_bfloat16*)w2, act, (__nv_bfloat16*)keys, slots);
+  CXS_LAUNCH_CHECK("compress_out_kernel");
+  return CXS_OK;
+}
 
 extern "C" int cxs_rms_norm(const void* x, const void* weight, void* out, int32_t rows,
                             int32_t dim, float eps, void* stream) {

@@ -273,19 +273,31 @@ class NSAExtendModel:
         return hidden
 
     def compress(self, w, windows):
-        """MLP compression of token windows [n, l, H, 128] -> keys [n, H, 128]:
-        for K and V, phi(x) = w2 silu(w1 vec(x + pe)) (bf16 GEMMs)."""
+        """MLP compression of token windows [n, l, H, 128] -> keys [n, H, 128]
+        (``cxs_compress_windows``: for K and V, phi(x) = W2 silu(W1 vec(x + pe))
+        with bf16 rounding after the position add, each GEMM and the silu)."""
         n, l, heads = windows.shape[:3]
-        dim = self.cfg.head_dim
-        out = torch.empty((n, heads, 2 * dim), dtype=windows.dtype, device=windows.device)
-        if not n:
-            return out
-        x = windows.reshape(n, l, heads, 2, dim).permute(3, 0, 2, 1, 4)  # [2, n, H, l, dim]
-        x = (x + w["cmp_pe"][:, None, None]).reshape(2, n * heads, l * dim)
-        hidden = F.silu(torch.bmm(x, w["cmp_w1"].transpose(1, 2)))
-        keys = torch.bmm(hidden, w["cmp_w2"].transpose(1, 2))          # [2, n * H, dim]
-        out.view(n, heads, 2, dim).copy_(keys.view(2, n, heads, dim).permute(1, 2, 0, 3))
-        return out
+        windows = windows.contiguous()
+        rows = torch.arange(n * l, device=windows.device).view(n, l)
+        slots = torch.arange(n, device=windows.device)
+        keys = torch.empty((n, heads, windows.shape[-1]), dtype=windows.dtype,
+                           device=windows.device)
+        self._compress_rows(w, windows.view(n * l, heads, -1), rows, slots, keys)
+        return keys
+
+    def _compress_rows(self, w, records, rows, slots, keys, scratch=None):
+        """Keys of the windows rows[i] (records row indices) into keys[slots[i]]."""
+        if not len(slots):
+            return
+        heads, cfg = records.shape[1], self.cfg
+        if scratch is None:
+            scratch = torch.empty(2 * heads * len(slots) * cfg.cmp_hidden, dtype=torch.float32,
+                                  device=records.device)
+        _lib.check(_lib.lib().cxs_compress_windows(
+            records.data_ptr(), rows.data_ptr(), len(slots), heads, cfg.cmp_block,
+            cfg.cmp_hidden, w["cmp_pe"].data_ptr(), w["cmp_w1"].data_ptr(),
+            w["cmp_w2"].data_ptr(), scratch.data_ptr(), keys.data_ptr(), slots.data_ptr(),
+            torch.cuda.current_stream(records.device).cuda_stream))
 
     def _append_windows(self, w, keys, tail, records):
         """Keys of the windows that complete in tail || records (the tail
@@ -419,7 +431,9 @@ class NSAExtendModel:
                     # window-buffer row kept + (t - old).
                     first = torch.arange(c_hist, c_hist + new) * stride
                     entry.update(cmp_rows=(kept - old + first[:, None] + arange_l).to(d),
-                                 cmp_slots=torch.arange(c_hist, c_hist + new, device=d))
+                                 cmp_slots=torch.arange(c_hist, c_hist + new, device=d),
+                                 cmp_scratch=torch.empty(2 * kl * new * cfg.cmp_hidden,
+                                                         dtype=torch.float32, device=d))
                 layers.append(entry)
                 continue
             if kept < tail_len:
@@ -475,7 +489,9 @@ class NSAExtendModel:
                 entry.update(c_hist=c_hist, new=len(slots_), summaries=summaries)
                 if slots_:
                     entry.update(cmp_rows=torch.stack(rows_).to(d),
-                                 cmp_slots=torch.tensor(slots_, device=d))
+                                 cmp_slots=torch.tensor(slots_, device=d),
+                                 cmp_scratch=torch.empty(2 * kl * len(slots_) * cfg.cmp_hidden,
+                                                         dtype=torch.float32, device=d))
             layers.append(entry)
         r = torch.arange(rows, device=d)
         true_positions = (old + r % E).to(torch.int32)
@@ -534,9 +550,9 @@ class NSAExtendModel:
                     L["summaries"][L["c_hist"]:], f["candidates"], seg_tokens, L["nsb"])
         if mlp and "cmp_rows" in L:
             # Keys of the windows this step completes, gathered from the window
-            # buffer (history rows and the step's suffix rows).
-            L["summaries"].index_copy_(0, L["cmp_slots"],
-                                       self.compress(w, L["window_buf"][L["cmp_rows"]]))
+            # buffer (history rows and the step's suffix rows) in two launches.
+            self._compress_rows(w, L["window_buf"], L["cmp_rows"], L["cmp_slots"],
+                                L["summaries"], L["cmp_scratch"])
         l, d = cfg.windows
         cmp_out, blocks = ops.compressed_attention_select(
             query, L["summaries"], positions, f["total"], cfg.block_size, cfg.block_counts,

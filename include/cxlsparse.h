@@ -430,6 +430,18 @@ int cxs_qkv_rope_segments(const void* proj, int32_t proj_stride, const int32_t* 
                           int32_t kv_heads, void* query, void* records, int32_t records_stride,
                           void* current, int32_t current_stride, void* gates,
                           int32_t segment_rows, int32_t segment_stride, void* stream);
+/* Keys of `windows` compressed windows (BASELINE's NSA compression; no
+ * counterpart in the reference): window i gathers the `window` (32)
+ * records rows[i * window + t] of `records` [*, heads, 128] bf16 (K || V);
+ * for K (part 0) and V (part 1) separately, x = bf16(records + pe[part])
+ * ([window, 64]), key = bf16(W2[part] bf16(silu(bf16(W1[part] vec(x))))),
+ * W1 [2, hidden, window * 64], W2 [2, 64, hidden] bf16, fp32 accumulation,
+ * written to keys[slots[i]] ([*, heads, 128]). `scratch` holds
+ * 2 * heads * windows * hidden fp32. Two launches. */
+int cxs_compress_windows(const void* records, const int64_t* rows, int32_t windows,
+                         int32_t heads, int32_t window, int32_t hidden, const void* pe,
+                         const void* w1, const void* w2, void* scratch, void* keys,
+                         const int64_t* slots, void* stream);
 /* out[r, c] = bf16(silu(gate_up[r, c])) * gate_up[r, ffn + c] (SwiGLU). */
 int cxs_silu_mul(const void* gate_up, int32_t rows, int32_t ffn, void* out, void* stream);
 
