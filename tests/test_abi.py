@@ -88,3 +88,44 @@ def test_invalid_attend_arguments_are_rejected_without_a_device():
     g.block_size, g.gate = 16, 1
     assert lib.cxs_fetch_attend(g, b, None) == _lib.ERR_INVALID
     assert b"gate" in lib.cxs_last_error()
+
+
+def test_segment_select_and_exchange_arguments_are_rejected_without_a_device():
+    """Candidate segments, the NSA selection geometry, window compression and
+    the KV-head exchange refuse bad geometry before touching the device."""
+    import ctypes
+
+    lib = _lib.lib()
+    # Segments must be whole blocks.
+    g = _lib.AttendGeometry(queries=4, heads=2, width=4, block_size=64, physical=8,
+                            segment_start=100, segment_tokens=128)
+    assert lib.cxs_fetch_attend(g, _lib.AttendBuffers(), None) == _lib.ERR_INVALID
+    assert b"segment" in lib.cxs_last_error()
+    # The output layout must hold this call's heads.
+    g = _lib.AttendGeometry(queries=4, heads=2, width=4, block_size=64, physical=8,
+                            out_heads=2, out_head0=1)
+    assert lib.cxs_fetch_attend(g, _lib.AttendBuffers(), None) == _lib.ERR_INVALID
+    # NSA geometry: the window must be a multiple of the stride, the stride
+    # must divide the block, forced is 0 or 1.
+    q = ctypes.c_void_p(16)
+    for bad in (dict(window=24, stride=16), dict(window=32, stride=24),
+                dict(window=32, stride=16, forced=2)):
+        sg = _lib.SelectGeometry(queries=1, heads=2, block_size=64, count=16, summaries=0,
+                                 total=100, **bad)
+        assert lib.cxs_compressed_select_nsa(sg, q, None, q, q, q, None, None) == \
+            _lib.ERR_INVALID
+    sg = _lib.SelectGeometry(queries=1, heads=2, block_size=64, count=16, summaries=1039,
+                             window=32, stride=16, total=16640)
+    columns = _lib.c_i32(0)
+    assert lib.cxs_select_score_columns(sg, columns) == _lib.OK and columns.value == 260
+    sg.window = sg.stride = 64
+    assert lib.cxs_select_score_columns(sg, columns) == _lib.OK and columns.value == 1039
+    # Window compression: 32-token windows only.
+    assert lib.cxs_compress_windows(q, q, 1, 2, 16, 256, q, q, q, q, q, q, None) == \
+        _lib.ERR_INVALID
+    # Exchange: 2..8 ranks, rank inside.
+    peers = (ctypes.c_void_p * 2)(None, 16)
+    assert lib.cxs_exchange_barrier(q, peers, q, 0, 1, 100, q, None) == _lib.ERR_INVALID
+    assert lib.cxs_exchange_barrier(q, peers, q, 2, 2, 100, q, None) == _lib.ERR_INVALID
+    assert lib.cxs_exchange_barrier(q, (ctypes.c_void_p * 2)(None, None), q, 0, 2, 100, q,
+                                    None) == _lib.ERR_INVALID
