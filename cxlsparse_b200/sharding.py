@@ -152,9 +152,14 @@ class PeerExchange:
 
     def targets(self, layer, rows):
         """Where layer `layer`'s attention writes its rows: (local gather buffer,
-        peer gather buffer address, heads of the buffer, this rank's first head)."""
-        if rows > self.rows:
-            raise ValueError(f"{rows} rows exceed the exchange buffers ({self.rows})")
+        peer gather buffer address, heads of the buffer, this rank's first head).
+        The launch writes the whole query bucket holding `rows` (padded rows
+        included), so the bucket must fit the buffers."""
+        from .transport import query_bucket
+
+        if query_bucket(rows) > self.rows:
+            raise ValueError(f"{rows} rows (bucket {query_bucket(rows)}) exceed the exchange "
+                             f"buffers ({self.rows})")
         b = layer % 2
         return self.views[b], self.remote[b], self.heads, self.head0
 

@@ -83,16 +83,21 @@ def _head_worker(rank, world, port, results):
     try:
         group, shard, shards, pair, pairs = head_pair_groups(world)
         ipc = _FakeIpc(rank)
-        exchange = PeerExchange(group, shard, shards, rows=8, kv_heads=2, kv_local=1,
+        exchange = PeerExchange(group, shard, shards, rows=64, kv_heads=2, kv_local=1,
                                 device="cpu", ipc=ipc)
         layers = [exchange.targets(layer, 8) for layer in range(4)]
+        try:  # 70 rows are padded to a 128-row bucket: larger than the buffers
+            exchange.targets(0, 70)
+            oversized = False
+        except ValueError:
+            oversized = True
         peer_flags = [int(p or 0) for p in exchange.peer_flags]
         remote = list(exchange.remote)
         exchange.close()
         results[rank] = (shard, shards, pair, pairs,
                          [(view.shape, float(view[0, 0, 0, 0]), peer, heads, head0)
                           for view, peer, heads, head0 in layers],
-                         peer_flags, remote, ipc.log)
+                         peer_flags, remote, ipc.log, oversized)
     finally:
         dist.destroy_process_group()
 
@@ -107,14 +112,15 @@ def test_head_pairs_exchange_buffers():
     mp.start_processes(_head_worker, args=(world, _free_port(), results), nprocs=world,
                        start_method="spawn")
     for rank in range(world):
-        shard, shards, pair, pairs, layers, peer_flags, remote, log = results[rank]
+        shard, shards, pair, pairs, layers, peer_flags, remote, log, oversized = results[rank]
+        assert oversized
         assert (shard, shards, pair, pairs) == (rank % 2, 2, rank // 2, 2)
         peer = rank ^ 1
         peer_allocs = [(peer + 1) * 1_000_000 + k * 1000 for k in (1, 2, 3)]
         assert remote == [a + 7 for a in peer_allocs]
         assert peer_flags[shard] == 0 and peer_flags[1 - shard] == peer_allocs[2] + 7
         for layer, (shape, local_code, peer_ptr, heads, head0) in enumerate(layers):
-            assert tuple(shape) == (8, 2, 16, 64) and heads == 2 and head0 == shard
+            assert tuple(shape) == (64, 2, 16, 64) and heads == 2 and head0 == shard
             assert local_code == (1 + layer % 2) * 1000        # own buffer of this parity
             assert peer_ptr == peer_allocs[layer % 2] + 7     # peer's buffer, same parity
         closes = [i for i, (op, _) in enumerate(log) if op == "close"]
