@@ -132,6 +132,40 @@ def _resolve(geo, keys_by_head, counts, required, desc, tags, locs, host_locs,
     return address, hbm, slots, valid, starts, flags
 
 
+def occurrence_rows(blocks, positions, compact_of, errors, *, bs, map_blocks, per_head):
+    """Occurrence rows (planning/occurrences.py:7-55): row r = q * H + h lists,
+    in the original selection order and with duplicates kept, head * per_head
+    + compact for every block that is in range (0 <= b < map_blocks), causal
+    (b * bs <= pos) and mapped to a compact slot in [0, per_head)
+    (``compact_of(h, b)``). Padded rows (pos < 0) and every row of a head with
+    a nonzero error count are empty. Returns (all_ids, all_counts, positions
+    repeated per head)."""
+    blocks = np.asarray(blocks, np.int64)
+    q_count, heads, width = blocks.shape
+    rows = q_count * heads
+    all_ids = np.full((rows, width), -1, np.int32)
+    all_counts = np.zeros(rows, np.int32)
+    row_positions = np.zeros(rows, np.int64)
+    for q in range(q_count):
+        pos = int(positions[q])
+        for h in range(heads):
+            r = q * heads + h
+            row_positions[r] = pos
+            if errors[h] or pos < 0:
+                continue
+            n_valid = 0
+            for i in range(width):
+                b = int(blocks[q, h, i])
+                if not (0 <= b < map_blocks and b * bs <= pos):
+                    continue
+                compact = int(compact_of(h, b))
+                if 0 <= compact < per_head:
+                    all_ids[r, n_valid] = h * per_head + compact
+                    n_valid += 1
+            all_counts[r] = n_valid
+    return all_ids, all_counts, row_positions
+
+
 def consumption_order(all_ids, all_counts, row_positions, flags, consumer_ctas,
                       width, *, shared=False, near_window=4):
     """Consumption-depth read order (planning/dependencies.py:37-300).
@@ -275,23 +309,9 @@ def active_plan(blocks, positions, desc, tags, locs, host_locs, hot_data, bases,
         pool_tokens, page_size, stats, region_counts, hbm_locs)
     # Occurrence rows (occurrences.py:7-35): original order, duplicates kept.
     rows = q_count * heads
-    all_ids = np.full((rows, width), -1, np.int32)
-    all_counts = np.zeros(rows, np.int32)
-    row_positions = np.zeros(rows, np.int64)
-    for q in range(q_count):
-        pos = int(positions[q])
-        for h in range(heads):
-            r = q * heads + h
-            row_positions[r] = pos
-            if stats[h, 6]:
-                continue
-            n_valid = 0
-            for i in range(width):
-                b = int(blocks[q, h, i])
-                if pos >= 0 and 0 <= b < mb and b * bs <= pos and b in mapping[h]:
-                    all_ids[r, n_valid] = h * cap + mapping[h][b]
-                    n_valid += 1
-            all_counts[r] = n_valid
+    all_ids, all_counts, row_positions = occurrence_rows(
+        blocks, positions, lambda h, b: mapping[h].get(b, -1), stats[:, 6], bs=bs,
+        map_blocks=mb, per_head=cap)
     if consumer_ctas is None:
         consumer_ctas = min(rows, 256)
     if read_order == "physical":

@@ -148,3 +148,68 @@ def test_dependency_distinct_rows_reusing_one_consumer():
     assert first[1] == 0 and first[2] == 0
     assert near[1] == 2 and near[2] == 3
     assert ioids[:missing].tolist() == [2, 1]
+
+
+@pytest.mark.parametrize("error_head", [-1, 0, 1])
+def test_occurrence_rows_keep_duplicates_order_and_exclude_invalid_rows(error_head):
+    """tests/test_nsa_tma_plan.py:43-96: occurrence rows from a given mapping.
+    Duplicates stay in selection order; blocks out of range, in the causal
+    future, unmapped (-1 / -2) or mapped past the per-head capacity drop out;
+    padded rows and every row of a head with an error count are empty."""
+    blocks = np.array([
+        [[1, 0, 0, 2, -1, 6, 3], [1, 0, 1, -1, 2, 6, 0]],
+        [[4, 2, 2, 3, 0, 5, -1], [4, 3, 2, 1, 0, -1, 6]],
+        [[0, 0, 1, 2, 3, 4, 5], [1, 2, 3, 4, 5, 0, 0]],
+    ])
+    positions = np.array([31, 79, -1])
+    mapping = np.array([[2, -1, 0, 4, -2, 3, -2], [1, 0, 3, 2, 4, -1, -2]])
+    errors = np.zeros(2, np.int64)
+    if error_head >= 0:
+        errors[error_head] = 1
+    ids, counts, rows_pos = P.occurrence_rows(
+        blocks, positions, lambda h, b: mapping[h, b], errors, bs=16, map_blocks=6, per_head=4)
+    # Query 0 (pos 31) sees blocks 0-1, query 1 (pos 79) blocks 0-4.
+    head0_q0 = [4 * 0 + 2, 4 * 0 + 2]            # blocks 1 (-1: dropped), 0, 0
+    head1_q0 = [4 + 0, 4 + 1, 4 + 0, 4 + 1]       # blocks 1, 0, 1, 0 -> compact 0, 1, 0, 1
+    head0_q1 = [4 * 0 + 0, 4 * 0 + 0, 0 + 2]      # 4 -> -2, 2, 2, 3 -> 4 (>= cap), 0 -> 2
+    head1_q1 = [4 + 2, 4 + 3, 4 + 0, 4 + 1]       # 4 -> 4 (>= cap), 3, 2, 1, 0
+    expected = {0: head0_q0, 1: head1_q0, 2: head0_q1, 3: head1_q1, 4: [], 5: []}
+    for row, want in expected.items():
+        if error_head >= 0 and row % 2 == error_head:
+            want = []
+        assert counts[row] == len(want), row
+        assert list(ids[row, : len(want)]) == want, row
+        assert (ids[row, len(want):] == -1).all()
+    assert list(rows_pos) == [31, 31, 79, 79, -1, -1]
+
+
+def test_prepare_classification_table():
+    """tests/test_nsa_tma_prepare.py:7-105: the seven source classes of a
+    physical block. Only a missing block of BS contiguous, 16-byte aligned
+    external tokens is a bulk copy (kind 1, its first address as source);
+    other missing blocks are token gathers (kind 2); resident and inactive
+    blocks are kind 0 and ready from the start."""
+    bs, external, resident = 16, 1 << 20, 9 << 20
+    cases = ["inactive", "direct", "resident", "mixed", "tail", "hot_tail", "gather"]
+    address = np.zeros((len(cases), bs), np.int64)
+    valid = np.zeros(len(cases), np.int64)
+    flags = np.zeros(len(cases), np.int64)
+    for p, kind in enumerate(cases):
+        count = {"inactive": 0, "tail": 5, "hot_tail": 7}.get(kind, bs)
+        valid[p] = count
+        flags[p] = kind in ("direct", "mixed", "tail", "gather")
+        t = np.arange(bs)
+        if kind == "direct":
+            address[p] = external + t * 256
+        elif kind in ("resident", "hot_tail"):
+            address[p, :count] = resident + t[:count] * 256
+        elif kind == "mixed":
+            address[p] = np.where(t % 2 == 0, external + t * 256, resident + t * 256)
+        elif kind == "tail":
+            address[p, :count] = external + (16 + t[:count]) * 256
+        elif kind == "gather":
+            address[p] = external + (bs - 1 - t) * 256
+    kinds, first = P.source_kinds(address, valid, flags, bs)
+    assert list(kinds) == [0, 1, 0, 2, 2, 0, 2]
+    assert first[1] == external
+    assert list(1 - flags) == [1, 0, 1, 0, 0, 1, 0]  # ready from the start
