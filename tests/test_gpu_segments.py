@@ -112,7 +112,7 @@ def _segment_inputs(case, order):
                 compressed=case["compressed"][rows], gates=case["gates"][rows])
 
 
-def _segment_case(history=150, extend=20, candidates=3, bs=16, seed=5):
+def _segment_case(history=150, extend=20, candidates=3, bs=16, seed=5, window=48, width=5):
     """Pool + cache holding `history` tokens per head, candidates' queries,
     suffix KV and true-position selections."""
     layout = SegmentLayout(history, extend, candidates, bs)
@@ -120,8 +120,9 @@ def _segment_case(history=150, extend=20, candidates=3, bs=16, seed=5):
     g = torch.Generator().manual_seed(seed)
     hist = torch.randn(history, heads, 128, generator=g).bfloat16()
     suffix = torch.randn(candidates, extend, heads, 128, generator=g).bfloat16()
-    pool = MemoryPool(16, 128, "host", page_size=64)
-    cache = HiSparseCache(pool, rows=heads, max_history=512, hot=64, topk=64, dim=128)
+    pool = MemoryPool(2 * -(-history // 64) + 2, 128, "host", page_size=64)
+    cache = HiSparseCache(pool, rows=heads, max_history=history + 64, hot=64, topk=64,
+                          dim=128)
     rows = candidates * extend
     query = torch.randn(rows, heads, 16, 64, generator=g).bfloat16()
     pages = []
@@ -130,30 +131,35 @@ def _segment_case(history=150, extend=20, candidates=3, bs=16, seed=5):
         slots = pool.token_slots(pages[h], 0, history)
         pool.write_many(slots, hist[:, h].contiguous().cuda())
         cache.bind(h, slots)
-    window = 48
     g2 = torch.Generator().manual_seed(seed + 1)
-    true_blocks = torch.full((rows, heads, 5), -1, dtype=torch.int32)
+    true_blocks = torch.full((rows, heads, width), -1, dtype=torch.int32)
     for row in range(rows):
         cur = (history + row % extend) // bs
         for h in range(heads):
-            chosen = [cur] + torch.randperm(cur, generator=g2)[:4].tolist()
+            chosen = [cur] + torch.randperm(cur, generator=g2)[:width - 1].tolist()
             true_blocks[row, h, : len(chosen)] = torch.tensor(chosen)
     compressed = torch.randn(rows, heads, 16, 64, generator=g).bfloat16()
     gates = torch.rand(rows, heads, 16, 3, generator=g).bfloat16()
     return dict(layout=layout, extend=extend, pool=pool, cache=cache, hist=hist, suffix=suffix,
-                query=query, pages=pages, window=window,
+                query=query, pages=pages, window=window, bs=bs,
                 window_start=layout.start - min(window - 1, layout.start),
                 true_blocks=true_blocks, compressed=compressed, gates=gates)
 
 
-@pytest.mark.parametrize("history", [150, 128])
-def test_transport_segments_match_each_candidate(cuda, history):
+@pytest.mark.parametrize("history,extend,candidates,bs,window,width", [
+    (150, 20, 3, 16, 48, 5),
+    (128, 20, 3, 16, 48, 5),
+    (4096, 128, 4, 64, 512, 16),  # BASELINE configs[0] geometry
+])
+def test_transport_segments_match_each_candidate(cuda, history, extend, candidates, bs, window,
+                                                 width):
     """Each candidate's selected / window / mixed output against the FP64 /
     fp32 oracle in its true positions; cold history fetched once for all
     candidates; and rotating the candidates over the segments rotates the
     outputs bit for bit (a candidate's result does not depend on its
     segment index)."""
-    case = _segment_case(history=history)
+    case = _segment_case(history=history, extend=extend, candidates=candidates, bs=bs,
+                         window=window, width=width)
     layout, extend = case["layout"], case["extend"]
     positions = torch.tensor(layout.positions(), dtype=torch.int32, device=cuda)
     transport = GRSelectedTransport(case["cache"], hot_policy="static")
@@ -162,7 +168,7 @@ def test_transport_segments_match_each_candidate(cuda, history):
     def run(inputs, gates):
         out, counters = transport.run(
             inputs["query"].cuda(), inputs["seg_blocks"].cuda(), positions, inputs["fetches"],
-            16, window=case["window"], window_kv=inputs["window_kv"].cuda(),
+            bs, window=case["window"], window_kv=inputs["window_kv"].cuda(),
             window_start=case["window_start"], compressed=inputs["compressed"].cuda(),
             gates=gates.cuda(), segments=layout.segments())
         torch.cuda.synchronize()
@@ -181,7 +187,7 @@ def test_transport_segments_match_each_candidate(cuda, history):
                 backing = torch.cat([case["hist"], case["suffix"][c]])
                 true_pos = torch.arange(history, history + extend)
                 sel = A.selected_attention(case["query"][rs], backing, case["true_blocks"][rs],
-                                           true_pos, 16)
+                                           true_pos, bs)
                 win = A.window_attention(case["query"][rs].float(), backing.float(), true_pos,
                                          0, case["window"])
                 if mode == "selected":
@@ -193,11 +199,11 @@ def test_transport_segments_match_each_candidate(cuda, history):
                                           win.bfloat16(), gates[rs]).float()
                 torch.testing.assert_close(out[rs], expected, rtol=0.03, atol=0.03)
             # Cold history tokens are fetched once for all candidates.
-            first = layout.start // 16
+            first = layout.start // bs
             for h in range(2):
                 hist_blocks = {int(b) for b in case["true_blocks"][:, h].flatten().tolist()
                                if 0 <= b < first}
-                assert rows[h]["misses"] == len(hist_blocks) * 16
+                assert rows[h]["misses"] == len(hist_blocks) * bs
             rot_gates = gates.view(n, extend, *gates.shape[1:]).roll(-1, 0).flatten(0, 1)
             out_rot, _ = run(rotated, rot_gates.contiguous())
             expected_rot = out.view(n, extend, *out.shape[1:]).roll(-1, 0).flatten(0, 1)

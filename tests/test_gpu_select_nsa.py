@@ -77,11 +77,14 @@ def test_identity_geometry_with_forced_blocks(cuda):
     assert torch.equal(blocks, A.topn_forced(scores, positions, bs, 16, total, True))
 
 
-@pytest.mark.parametrize("history", [1000, 4096])
-def test_nsa_geometry_over_candidate_segments(cuda, history):
+@pytest.mark.parametrize("history,extend,candidates", [
+    (1000, 64, 3), (4096, 64, 3),
+    (4096, 128, 4),  # BASELINE configs[0] geometry
+])
+def test_nsa_geometry_over_candidate_segments(cuda, history, extend, candidates):
     """Candidate segments with overlapping windows: the key slots of the
     windows that cross the history boundary are per candidate."""
-    bs, extend, candidates = 64, 64, 3
+    bs = 64
     layout = SegmentLayout(history, extend, candidates, bs)
     start, tokens = layout.segments()
     seg_key = (start - L) // D + 1
