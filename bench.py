@@ -265,8 +265,7 @@ def run_ours(args):
     world, rank, local = dist_setup(torch)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    from cxlsparse_b200 import _lib
-    from cxlsparse_b200.model import NSAConfig, NSAExtendModel
+    from cxlsparse_b200.model import NSAExtendModel
     from cxlsparse_b200.sharding import gather_scores
 
     cfg = nsa_config(args)
@@ -433,7 +432,7 @@ def run_dedup(args):
     (worker/prompt.py:24-55)."""
     import torch
 
-    from cxlsparse_b200.model import NSAConfig, NSAExtendModel
+    from cxlsparse_b200.model import NSAExtendModel
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
@@ -486,7 +485,7 @@ def run_serving(args):
     collective)."""
     import torch
 
-    from cxlsparse_b200.model import NSAConfig, NSAExtendModel
+    from cxlsparse_b200.model import NSAExtendModel
     from cxlsparse_b200.sharding import gather_scores, users_for_rank
 
     if args.warmup < 3:
@@ -652,7 +651,7 @@ def run_headsplit(args):
     once (one captured graph per user, collectives inside)."""
     import torch
 
-    from cxlsparse_b200.model import NSAConfig, NSAExtendModel
+    from cxlsparse_b200.model import NSAExtendModel
     from cxlsparse_b200.sharding import PeerExchange, gather_scores, head_pair_groups
     from cxlsparse_b200.sharding import users_for_rank
 

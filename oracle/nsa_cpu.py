@@ -13,7 +13,6 @@ History K/V, summaries and windows are seeded N(0, 1) stand-ins of the right
 shapes: throughput does not depend on their values.
 """
 
-import math
 import time
 
 import torch
