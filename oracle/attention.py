@@ -135,20 +135,26 @@ def gate_mix(selected, compressed, window, gates):
 # ---------------------------------------------------------------------------
 
 
-def compress_mlp(records, weights, l, d):
+def compress_mlp(records, weights, l, d, *, bf16_steps=False):
     """records [T, H, 128] (K || V) -> [C, H, 128] for the complete windows
     [i*d, i*d + l), C = (T - l) // d + 1. ``weights`` holds, for K and V,
     pe [l, 64], w1 [hidden, l*64], w2 [64, hidden]: phi(x) = w2 silu(w1
-    vec(x + pe)), computed in fp32 and rounded to bf16 once."""
+    vec(x + pe)), computed in fp32 and rounded to bf16 once, or, with
+    ``bf16_steps``, rounded to bf16 after the position add, w1 and the silu as
+    a bf16 model computes it."""
     t, heads = records.shape[:2]
     count = (t - l) // d + 1 if t >= l else 0
-    out = torch.zeros(count, heads, 128)
+    out = torch.zeros(count, heads, 128, device=records.device)
+
+    def step(x):
+        return x.bfloat16().float() if bf16_steps else x
+
     for part, lo in (("k", 0), ("v", 64)):
         pe, w1, w2 = (weights[f"{part}_{n}"].float() for n in ("pe", "w1", "w2"))
         for i in range(count):
-            x = records[i * d: i * d + l, :, lo: lo + 64].float() + pe[:, None, :]  # [l, H, 64]
+            x = step(records[i * d: i * d + l, :, lo: lo + 64].float() + pe[:, None, :])
             x = x.permute(1, 0, 2).reshape(heads, l * 64)
-            hidden = torch.nn.functional.silu(x @ w1.T)
+            hidden = step(torch.nn.functional.silu(step(x @ w1.T)))
             out[i, :, lo: lo + 64] = hidden @ w2.T
     return out.to(records.dtype)
 

@@ -1,0 +1,69 @@
+"""The whole model against an independent dense oracle (the reference's check,
+tests/test_nsa.py:152-254, relative RMS < 0.008, restated for this model).
+
+With history + suffix within top-n x block size every causal block is
+selected, so NSA reduces to dense compressed / causal / window branches
+(oracle/nsa_dense.py), computed without block tables, plans, pools or caches.
+The model runs its real path: prefill into the pinned pool, the frequency hot
+set, the fetch planner, host->HBM fetches and the fused attention, in the
+eager and the captured fast path, for one candidate and for candidate
+segments (each candidate against the dense forward over the history and its
+own suffix; no selection ties can differ here).
+"""
+
+import pytest
+import torch
+
+from cxlsparse_b200.model import NSAConfig, NSAExtendModel
+from oracle.nsa_dense import dense_forward
+
+pytestmark = pytest.mark.gpu
+
+HISTORY, EXTEND = 700, 100  # 800 tokens: all 13 blocks of 64 fit in the top-16
+
+
+def _dense(model, ids):
+    cfg = model.cfg
+    return dense_forward(ids, model.embed, model.layers, model.final_norm, q_heads=cfg.q_heads,
+                         kv_heads=cfg.kv_heads, head_dim=cfg.head_dim,
+                         block_size=cfg.block_size, window=cfg.window,
+                         rope_theta=cfg.rope_theta, eps=cfg.rms_eps,
+                         compression=cfg.compression, cmp_block=cfg.cmp_block,
+                         cmp_stride=cfg.cmp_stride).float().cpu()
+
+
+def _close(got, want, what):
+    rel = (got - want).norm() / want.norm()
+    cos = torch.nn.functional.cosine_similarity(got, want, dim=-1)
+    assert rel < 0.01 and cos.min() > 0.999, (what, float(rel), float(cos.min()))
+
+
+@pytest.mark.parametrize("compression", ["mean"])
+@pytest.mark.parametrize("candidates", [1, 3])
+def test_model_matches_dense_oracle(cuda, compression, candidates):
+    cfg = (NSAConfig(layers=2, hot=64) if compression == "mean"
+           else NSAConfig.baseline(layers=2, hot=64))
+    model = NSAExtendModel(cfg, device=cuda, seed=0, max_history=HISTORY + EXTEND + 64,
+                           chunk=256, workspaces=8)
+    try:
+        g = torch.Generator().manual_seed(candidates + 10 * (compression == "mlp"))
+        history = torch.randint(0, cfg.vocab, (HISTORY,), generator=g)
+        ids = torch.randint(0, cfg.vocab, (candidates, EXTEND), generator=g)
+        model.prefill(history.to(cuda))
+        if candidates == 1:
+            eager = model.extend(ids[0].to(cuda)).float().cpu()
+        graph, static_ids, static_out, counters = model.capture_extend(
+            EXTEND, candidates=candidates)
+        static_ids.copy_(ids.flatten().to(cuda))
+        graph.replay()
+        torch.cuda.synchronize()
+        fast = static_out.float().cpu().view(candidates, EXTEND, -1)
+        assert sum(r["misses"] for c in counters for r in c.materialize()) > 0
+        for c in range(candidates):
+            want = _dense(model, torch.cat((history, ids[c])).to(cuda))[HISTORY:]
+            _close(fast[c], want, ("fast", c))
+            if candidates == 1:
+                _close(eager, want, "eager")
+        del graph
+    finally:
+        model.close()
