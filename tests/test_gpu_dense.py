@@ -38,7 +38,7 @@ def _close(got, want, what):
     assert rel < 0.01 and cos.min() > 0.999, (what, float(rel), float(cos.min()))
 
 
-@pytest.mark.parametrize("compression", ["mean"])
+@pytest.mark.parametrize("compression", ["mean", "mlp"])
 @pytest.mark.parametrize("candidates", [1, 3])
 def test_model_matches_dense_oracle(cuda, compression, candidates):
     cfg = (NSAConfig(layers=2, hot=64) if compression == "mean"
