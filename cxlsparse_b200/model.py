@@ -44,8 +44,8 @@ class NSAConfig:
     window: int = 512
     hot: int = 256
     # Compressed branch. "mean": the reference's summaries (mean of each
-    # selection block, models/nsa/ops.py:62-70). "mlp": BASELINE's NSA
-    # geometry: a key/value per window of cmp_block tokens at stride
+    # selection block, models/nsa/ops.py:62-70). "mlp": the NSA
+    # paper's geometry (Yuan et al. 2025): a key/value per window of cmp_block tokens at stride
     # cmp_stride from a per-layer MLP with intra-window position encoding,
     # selection scores aggregated over the overlapping windows.
     compression: str = "mean"
@@ -67,7 +67,7 @@ class NSAConfig:
 
     @classmethod
     def baseline(cls, **overrides):
-        """BASELINE's NSA parameters: compression 32 / stride 16 with an MLP,
+        """The NSA paper's parameters (the serving benchmark's geometry): compression 32 / stride 16 with an MLP,
         selection block 64, top-16 including block 0 and 2 local blocks,
         window 512."""
         values = dict(compression="mlp", cmp_block=32, cmp_stride=16, forced_blocks=True)
@@ -145,7 +145,7 @@ class NSAExtendModel:
                  head_shard=(0, 1), exchange=None, replica_blocks=256, straddle=0.0):
         self.cfg = cfg = cfg or NSAConfig()
         self.device = torch.device(device)
-        # KV-head sharding: this instance owns KV heads
+        # KV-head sharding (the long-history serving case, one GPU pair per user): this instance owns KV heads
         # [head0, head0 + kv_local) of every layer (their query heads, pool
         # slice, cache rows, planner and attention); `exchange`
         # (sharding.PeerExchange) receives every layer's attention rows of all

@@ -42,7 +42,7 @@ def compressed_attention_select(query, compressed, positions, total, block_size,
     history + suffix length). ``window`` / ``stride`` (default: the block
     size, the reference's mean-pooled summaries) describe overlapping
     compressed keys; ``forced`` adds the previous block and block 0 after
-    the current one (BASELINE's NSA geometry)."""
+    the current one (the NSA paper's geometry, Yuan et al. 2025)."""
     queries, heads, groups, dim = query.shape
     if groups != 16 or dim != 64 or query.dtype != torch.bfloat16:
         raise ValueError("query must be bf16 [Q, H, 16, 64]")

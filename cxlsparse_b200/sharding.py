@@ -30,7 +30,7 @@ def gather_scores(local, group=None):
 
 
 def head_pair_groups(world):
-    """Process groups of the KV-head split: ranks
+    """Process groups of the KV-head split (long-history serving, one GPU pair per user set): ranks
     (0, 1), (2, 3), ... each serve one set of users, rank 2p + i owning KV
     head i of every layer. Every rank must call this (new_group is collective);
     returns (group of this rank, shard index, shard count, pair index, pairs)."""

@@ -360,7 +360,7 @@ int cxs_compressed_select_segments(const void* query, const void* compressed,
                                    int64_t segment_tokens, void* out, int32_t* blocks,
                                    float* scores, void* stream);
 
-/* Compressed branch + top-n in BASELINE's NSA geometry, of which the two
+/* Compressed branch + top-n in the NSA paper's geometry (Yuan et al. 2025), of which the two
  * entry points above are the special case window = stride = block_size,
  * forced = 0. No counterpart in the reference. Compressed key i (row i of
  * `compressed`) summarises the tokens [i * stride, i * stride + window); a
@@ -430,7 +430,7 @@ int cxs_qkv_rope_segments(const void* proj, int32_t proj_stride, const int32_t* 
                           int32_t kv_heads, void* query, void* records, int32_t records_stride,
                           void* current, int32_t current_stride, void* gates,
                           int32_t segment_rows, int32_t segment_stride, void* stream);
-/* Keys of `windows` compressed windows (BASELINE's NSA compression; no
+/* Keys of `windows` compressed windows (the NSA paper's MLP compression; no
  * counterpart in the reference): window i gathers the `window` (32)
  * records rows[i * window + t] of `records` [*, heads, 128] bf16 (K || V);
  * for K (part 0) and V (part 1) separately, x = bf16(records + pe[part])

@@ -12,7 +12,7 @@
 * ``topn_from_scores``: the ordering rule alone, for bit-exact checks of a
   device selection against its own exported scores.
 * ``compress_mlp``, ``block_scores``, ``topn_forced``, ``compressed_select_nsa``:
-  BASELINE's NSA selection geometry (overlapping MLP-compressed windows,
+  the NSA paper's selection geometry (overlapping MLP-compressed windows,
   aggregated block scores, forced blocks), which the reference does not have:
   a restatement of the published NSA method, not pinned to reference output.
 
@@ -121,7 +121,7 @@ def gate_mix(selected, compressed, window, gates):
 
 
 # ---------------------------------------------------------------------------
-# BASELINE's NSA selection geometry (not in the reference, which uses
+# The NSA paper's selection geometry (Yuan et al. 2025; not in the reference, which uses
 # mean-pooled summaries with block = stride = selection block and only the
 # current block forced): overlapping compression windows of `l` tokens at
 # stride `d` mapped to one key/value each by an MLP, selection-block scores

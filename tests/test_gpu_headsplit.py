@@ -1,4 +1,4 @@
-"""KV-head split across a GPU pair (BASELINE configs[4] layout, scaled down).
+"""KV-head split across a GPU pair (the long-history serving layout, scaled down).
 
 Rank i of the pair owns KV head i of every layer: its 16 query heads, its own
 pool slice, cache rows, planner, fetch and attention; each attention launch

@@ -1,4 +1,4 @@
-"""Device planner vs the oracle at BASELINE configs[2] size.
+"""Device planner vs the oracle at the dedup stress size.
 
 16 candidate queries x 128 extend tokens (2048 query rows) over an H=16384
 history, 2 KV heads, top-16 blocks of 64 tokens, a hot replica of 256 tokens

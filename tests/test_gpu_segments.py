@@ -149,7 +149,7 @@ def _segment_case(history=150, extend=20, candidates=3, bs=16, seed=5, window=48
 @pytest.mark.parametrize("history,extend,candidates,bs,window,width", [
     (150, 20, 3, 16, 48, 5),
     (128, 20, 3, 16, 48, 5),
-    (4096, 128, 4, 64, 512, 16),  # BASELINE configs[0] geometry
+    (4096, 128, 4, 64, 512, 16),  # H4K, 4 candidates x 128, BS 64 (the CPU-runnable case)
 ])
 def test_transport_segments_match_each_candidate(cuda, history, extend, candidates, bs, window,
                                                  width):

@@ -1,4 +1,4 @@
-"""Compressed branch + top-n in BASELINE's NSA geometry on the device:
+"""Compressed branch + top-n in the NSA paper's geometry on the device:
 overlapping windows (32 tokens at stride 16) as compressed keys, BS-64
 selection scores aggregated from the window scores, block 0 and the two
 local blocks forced. Not in the reference (parity unpinned): checked against
@@ -33,7 +33,7 @@ def _run(query, keys, positions, total, bs, forced, segments=None, window=L, str
 
 @pytest.mark.parametrize("history,extend,forced", [
     (1000, 64, True),      # tcgen05 kernel
-    (16384, 256, True),    # BASELINE H16K/E256 shape (1039 keys)
+    (16384, 256, True),    # H16K/E256 headline shape (1039 keys)
     (16384, 256, False),
     (40000, 32, True),     # more than 2048 keys: the mma.sync kernel
 ])
@@ -79,7 +79,7 @@ def test_identity_geometry_with_forced_blocks(cuda):
 
 @pytest.mark.parametrize("history,extend,candidates", [
     (1000, 64, 3), (4096, 64, 3),
-    (4096, 128, 4),  # BASELINE configs[0] geometry
+    (4096, 128, 4),  # H4K, 4 candidates x 128, BS 64 (the CPU-runnable case)
 ])
 def test_nsa_geometry_over_candidate_segments(cuda, history, extend, candidates):
     """Candidate segments with overlapping windows: the key slots of the

@@ -1,4 +1,4 @@
-"""Several users served by one model on one GPU (BASELINE configs[3] shape,
+"""Several users served by one model on one GPU (the multi-user serving shape,
 scaled down): jittered history lengths with partial tail blocks, one captured
 extend graph per user, replayed one after another on one stream."""
 
