@@ -11,6 +11,11 @@ arithmetic, GQA by repeating the KV heads) with this model's geometry
 (selection block, window, compression). It never sees a block table, a plan,
 a pool or a cache, so it checks all of them at once.
 
+Pinned: with mean-pooled compression it is bit-identical to the reference's
+own dense oracle (run on CPU into tests/golden/dense_model.npz; checked by
+tests/test_oracle_golden.py). The MLP-compression branch restates the NSA
+paper's compression (oracle/attention.py compress_mlp) and is not pinned.
+
 Test infrastructure only: the product package never imports it.
 """
 
@@ -46,8 +51,11 @@ def dense_forward(token_ids, embed, layers, final_norm, *, q_heads, kv_heads, he
     hidden = F.embedding(token_ids.to(device), embed)
     length, dim, groups = len(token_ids), head_dim, q_heads // kv_heads
     pos = torch.arange(length, device=device)
-    inv = 1.0 / (rope_theta ** (torch.arange(0, dim, 2, device=device).float() / dim))
-    phase = pos.float()[:, None] * inv[None, :]
+    # position / theta^(i/d), divided rather than multiplied by an inverse
+    # frequency: that is the reference oracle's rounding (the bf16 sine table
+    # differs in a few entries otherwise), which keeps the two bit-identical.
+    freq = rope_theta ** (torch.arange(0, dim, 2, device=device).float() / dim)
+    phase = pos.float()[:, None] / freq[None, :]
     phase = torch.cat((phase, phase), -1)[:, None]
     cos, sin = phase.cos().to(hidden.dtype), phase.sin().to(hidden.dtype)
     causal = pos[None] <= pos[:, None]

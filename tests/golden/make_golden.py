@@ -11,7 +11,9 @@ given checkout and runs:
   residency modes, block sizes and read orders;
 * ``ops.compressed_attention_select`` / ``ops.window_attention`` torch CPU paths
   (``cxl_recsys/models/nsa/ops.py``);
-* ``backends/io_plan.py:selected_attention_oracle`` (FP64).
+* ``backends/io_plan.py:selected_attention_oracle`` (FP64);
+* the independent dense backbone oracle ``dense_oracle``
+  (``tests/test_nsa.py:152-236``) on CPU.
 
 Outputs are small ``.npz`` files beside this script. The tests read only those
 files; nothing at test time needs the reference checkout.
@@ -207,10 +209,83 @@ def select_cases():
     np.savez_compressed(HERE / "select_window.npz", **out)
 
 
+DENSE_LENGTHS = (7, 17, 143, 256)
+
+
+def dense_case(reference_root, seed=2024):
+    """Whole-backbone output of the reference's independent dense oracle
+    (tests/test_nsa.py:152-236) on a 2-layer model of its test checkpoint's
+    geometry (hidden 32, 32 / 2 heads of 64, BS 16, window 128, rope theta
+    5e5), random weights (norm gains included), at its test lengths 7 / 17 /
+    143 and at the selection limit 256. The oracle is written for "cuda"; it
+    runs here on CPU with its module's `torch.tensor` / `torch.arange` device
+    argument dropped and `Tensor.cuda` as the identity, nothing else changed.
+    Importing the test module pulls in the reference's RPC module, whose
+    `orjson` import is satisfied by a JSON stand-in (the oracle never uses it)."""
+    import importlib.util
+    import json
+    import types
+
+    import torch
+
+    sys.modules.setdefault("orjson", types.SimpleNamespace(
+        dumps=lambda o, **_: json.dumps(o).encode(), loads=json.loads))
+    spec = importlib.util.spec_from_file_location(
+        "reference_test_nsa", Path(reference_root) / "tests" / "test_nsa.py")
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+
+    class _CpuTorch:
+        def __getattr__(self, name):
+            attr = getattr(torch, name)
+            if name in ("tensor", "arange"):
+                return lambda *args, device=None, **kw: attr(*args, **kw)
+            return attr
+
+    module.torch = _CpuTorch()
+    hidden, inter, vocab, layers = 32, 64, 256, 2
+    g = torch.Generator().manual_seed(seed)
+
+    def normal(*shape, scale=0.2, mean=0.0):
+        return (torch.randn(shape, generator=g) * scale + mean).bfloat16()
+
+    weights = {"model.embed_tokens.weight": normal(vocab, hidden, scale=1.0),
+               "model.norm.weight": normal(hidden, scale=0.1, mean=1.0)}
+    for layer in range(layers):
+        p = f"model.layers.{layer}."
+        for name in ("input_layernorm.weight", "post_attention_layernorm.weight"):
+            weights[p + name] = normal(hidden, scale=0.1, mean=1.0)
+        for name, shape in {"self_attn.q_proj.weight": (2048, hidden),
+                            "self_attn.k_proj.weight": (128, hidden),
+                            "self_attn.v_proj.weight": (128, hidden),
+                            "self_attn.o_proj.weight": (hidden, 2048),
+                            "self_attn.g_proj.weight": (96, hidden),
+                            "mlp.gate_proj.weight": (inter, hidden),
+                            "mlp.up_proj.weight": (inter, hidden),
+                            "mlp.down_proj.weight": (hidden, inter)}.items():
+            weights[p + name] = normal(*shape)
+    cfg = SimpleNamespace(selected_tokens=256, rope_theta=500000.0, rms_norm_eps=1e-5,
+                          num_hidden_layers=layers)
+    out = {f"w:{k}": v.view(torch.int16).numpy() for k, v in weights.items()}
+    cuda = torch.Tensor.cuda
+    torch.Tensor.cuda = lambda self, *args, **kw: self
+    try:
+        for length in DENSE_LENGTHS:
+            ids = torch.randint(0, vocab, (length,), generator=g)
+            expected = module.dense_oracle(ids.tolist(), cfg, weights)
+            out[f"ids_{length}"] = ids.numpy()
+            out[f"out_{length}"] = expected.view(torch.int16).numpy()
+    finally:
+        torch.Tensor.cuda = cuda
+    out["meta"] = np.array([layers, 16, 128])  # layers, block size, window
+    np.savez_compressed(HERE / "dense_model.npz", **out)
+
+
 def main():
     if len(sys.argv) != 2:
         raise SystemExit(__doc__)
     _setup(Path(sys.argv[1]).resolve())
+    dense_case(Path(sys.argv[1]).resolve())
     common = dict(heads=2, hot=32)
     plan_case("miss_bs16_depth", seed=1, queries=13, width=4, bs=16, old=67,
               current=13, residency="miss", read_order="consumption_depth", **common)

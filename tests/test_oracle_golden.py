@@ -105,3 +105,26 @@ def test_append_compressed_boundaries():
         assert torch.equal(compressed, expected)
         assert torch.equal(tail, values[stop // 16 * 16: stop])
         start = stop
+
+
+@pytest.mark.parametrize("length", [7, 17, 143, 256])
+def test_dense_oracle_matches_reference_dense_oracle(length):
+    """oracle/nsa_dense.py is bit-identical to the reference's independent
+    dense backbone oracle (tests/test_nsa.py:152-236, run on CPU by the
+    fixture script) on a 2-layer model of its test geometry."""
+    from oracle.nsa_dense import dense_forward
+
+    z = load(GOLDEN / "dense_model.npz")
+    layers_n, block_size, window = (int(v) for v in z["meta"])
+    w = {k[2:]: torch.from_numpy(v).view(torch.bfloat16) for k, v in z.items()
+         if k.startswith("w:")}
+    names = dict(q="self_attn.q_proj", k="self_attn.k_proj", v="self_attn.v_proj",
+                 g="self_attn.g_proj", o="self_attn.o_proj", gate="mlp.gate_proj",
+                 up="mlp.up_proj", down="mlp.down_proj", in_norm="input_layernorm",
+                 post_norm="post_attention_layernorm")
+    layers = [{ours: w[f"model.layers.{i}.{theirs}.weight"] for ours, theirs in names.items()}
+              for i in range(layers_n)]
+    got = dense_forward(torch.from_numpy(z[f"ids_{length}"]), w["model.embed_tokens.weight"],
+                        layers, w["model.norm.weight"], q_heads=32, kv_heads=2, head_dim=64,
+                        block_size=block_size, window=window, rope_theta=500000.0, eps=1e-5)
+    assert torch.equal(got, torch.from_numpy(z[f"out_{length}"]).view(torch.bfloat16))
