@@ -61,6 +61,10 @@ def parse():
                         "its own JSON line")
     p.add_argument("--users-per-pair", type=int, default=4)
     p.add_argument("--users-per-gpu", type=int, default=8)
+    p.add_argument("--lanes", type=int, default=1,
+                   help="serving: streams the users' captured graphs are spread over "
+                        "(round-robin); > 1 gives every user its own transport workspaces "
+                        "so one user's host-link-bound fetch runs under another's compute")
     p.add_argument("--queries", type=int, default=4)
     p.add_argument("--jitter", type=int, default=1000)
     p.add_argument("--sigma", type=float, default=0.5)
@@ -502,10 +506,23 @@ def run_serving(args):
     mine = users_for_rank(list(range(users_total)), rank, world)
     suffix = args.queries * args.extend
     segments = 1 if args.packed else args.queries
+    if args.lanes < 1:
+        raise SystemExit("--lanes must be >= 1")
+    lanes = min(args.lanes, len(mine))
+    max_history = max(lengths[u] for u in mine) + suffix + 64 * segments
+    budget = {}
+    if lanes > 1:
+        # One workspace per (user, layer); each is bounded by the estimate
+        # for the longest history.
+        from cxlsparse_b200.transport import query_bucket, workspace_estimate
+        per = workspace_estimate(query_bucket(suffix), max_history,
+                                 cfg.kv_heads, 16, cfg.block_counts, cfg.block_size)
+        budget = dict(user_workspaces=True,
+                      workspace_bytes=max(2 * 1024**3, 2 * per * cfg.layers * len(mine)))
     model = NSAExtendModel(cfg, device=device, seed=0, max_users=len(mine),
-                           max_history=max(lengths[u] for u in mine) + suffix + 64 * segments,
-                           read_order=args.read_order,
-                           workspaces=cfg.layers * len(mine) + 4, **model_options(args))
+                           max_history=max_history, read_order=args.read_order,
+                           workspaces=cfg.layers * len(mine) + 4, **budget,
+                           **model_options(args))
     t0 = time.perf_counter()
     candidates = {}
     for u in mine:
@@ -540,9 +557,25 @@ def run_serving(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
+    lane_streams = [torch.cuda.Stream(device) for _ in range(lanes)] if lanes > 1 else None
+
+    def on_lanes(work):
+        """Run work(i, u) for every local user: in order on the current
+        stream, or round-robin over the lane streams, joined back into it."""
+        if lane_streams is None:
+            for i, u in enumerate(mine):
+                work(i, u)
+            return
+        for lane in lane_streams:
+            lane.wait_stream(stream)
+        for i, u in enumerate(mine):
+            with torch.cuda.stream(lane_streams[i % lanes]):
+                work(i, u)
+        for lane in lane_streams:
+            stream.wait_stream(lane)
+
     def serve_all():
-        for u in mine:
-            captured[u][0].replay()
+        on_lanes(lambda i, u: captured[u][0].replay())
 
     for _ in range(args.warmup):
         serve_all()
@@ -572,12 +605,14 @@ def run_serving(args):
                            pin_memory=True)
     barrier()
     start.record(stream)
+    def request(i, u):
+        graph, static_ids, static_out, _ = captured[u]
+        static_ids.copy_(host_ids[u], non_blocking=True)
+        graph.replay()
+        local_out[i].copy_(static_out.view(segments, -1, cfg.hidden)[:, -1])
+
     for _ in range(args.steps):
-        for i, u in enumerate(mine):
-            graph, static_ids, static_out, _ = captured[u]
-            static_ids.copy_(host_ids[u], non_blocking=True)
-            graph.replay()
-            local_out[i].copy_(static_out.view(segments, -1, cfg.hidden)[:, -1])
+        on_lanes(request)
         gathered = gather_scores(local_out) if dist is not None else local_out[None]
         host_out.copy_(gathered, non_blocking=True)
     end.record(stream)
@@ -600,6 +635,7 @@ def run_serving(args):
                        "suffix": "one packed suffix" if args.packed
                        else "one segment per candidate (history + own suffix)",
                        "users": users_total, "users_per_gpu": args.users_per_gpu,
+                       "lanes": lanes,
                        "history_lengths_rank0": [lengths[u] for u in mine],
                        "layers": args.layers, "block_size": 64, "top_n": 16, "window": 512,
                        "compression": compression_config(args),
@@ -710,9 +746,25 @@ def run_headsplit(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
+    lane_streams = [torch.cuda.Stream(device) for _ in range(lanes)] if lanes > 1 else None
+
+    def on_lanes(work):
+        """Run work(i, u) for every local user: in order on the current
+        stream, or round-robin over the lane streams, joined back into it."""
+        if lane_streams is None:
+            for i, u in enumerate(mine):
+                work(i, u)
+            return
+        for lane in lane_streams:
+            lane.wait_stream(stream)
+        for i, u in enumerate(mine):
+            with torch.cuda.stream(lane_streams[i % lanes]):
+                work(i, u)
+        for lane in lane_streams:
+            stream.wait_stream(lane)
+
     def serve_all():
-        for u in mine:
-            captured[u][0].replay()
+        on_lanes(lambda i, u: captured[u][0].replay())
 
     for _ in range(args.warmup):
         serve_all()
@@ -742,12 +794,14 @@ def run_headsplit(args):
                            pin_memory=True)
     barrier()
     start.record(stream)
+    def request(i, u):
+        graph, static_ids, static_out, _ = captured[u]
+        static_ids.copy_(host_ids[u], non_blocking=True)
+        graph.replay()
+        local_out[i].copy_(static_out.view(segments, -1, cfg.hidden)[:, -1])
+
     for _ in range(args.steps):
-        for i, u in enumerate(mine):
-            graph, static_ids, static_out, _ = captured[u]
-            static_ids.copy_(host_ids[u], non_blocking=True)
-            graph.replay()
-            local_out[i].copy_(static_out.view(segments, -1, cfg.hidden)[:, -1])
+        on_lanes(request)
         gathered = gather_scores(local_out) if dist is not None else local_out[None]
         host_out.copy_(gathered, non_blocking=True)
     end.record(stream)

@@ -142,7 +142,8 @@ class NSAExtendModel:
     def __init__(self, cfg=None, *, device="cuda", seed=0, max_users=1, max_history=16384,
                  hot_policy="frequency", read_order="consumption_depth",
                  cross_query_dedup=True, pool_regions=1, chunk=1024, workspaces=None,
-                 head_shard=(0, 1), exchange=None, replica_blocks=256, straddle=0.0):
+                 head_shard=(0, 1), exchange=None, replica_blocks=256, straddle=0.0,
+                 user_workspaces=False, workspace_bytes=2 * 1024**3):
         self.cfg = cfg = cfg or NSAConfig()
         self.device = torch.device(device)
         # KV-head sharding (the long-history serving case, one GPU pair per user): this instance owns KV heads
@@ -158,6 +159,14 @@ class NSAExtendModel:
             raise ValueError("a head-sharded model needs an exchange")
         if exchange is not None and cfg.layers % 2:
             raise ValueError("the peer exchange alternates buffers by layer: even layer count")
+        # user_workspaces: every user's fast path gets its own per-layer
+        # transport workspaces (plan tables, staging, ready flags, counters)
+        # instead of sharing one per layer, so captured graphs of different
+        # users hold disjoint buffers and may run at the same time on
+        # different streams (one user's host-link-bound fetch under another
+        # user's projections, selection and plan). Costs one workspace per
+        # (user, layer): size `workspaces` / `workspace_bytes` for that.
+        self.user_workspaces = user_workspaces
         self.kv_local = cfg.kv_heads // shards
         self.head0 = shard * self.kv_local
         self.exchange = exchange
@@ -204,7 +213,8 @@ class NSAExtendModel:
             self.cache.enable_replica(self.cache.rows * per_row)
         self.transport = GRSelectedTransport(
             self.cache, read_order=read_order, cross_query_dedup=cross_query_dedup,
-            hot_policy=hot_policy, capacity=workspaces or cfg.layers + 4, async_hot=True)
+            hot_policy=hot_policy, capacity=workspaces or cfg.layers + 4, async_hot=True,
+            workspace_bytes=workspace_bytes)
         self.fast = None          # fused-glue buffers of the user being served
         self.fast_states = {}     # user -> its fused-glue buffers (prepare_fast)
         self.probe, self.probe_counters = None, []
@@ -563,10 +573,11 @@ class NSAExtendModel:
             self.probe_counters.append(self.probe.plan_only(
                 query, blocks, positions, L["fetches"], cfg.block_size, workspace_id=index))
         target = None if self.exchange is None else self.exchange.targets(index, E)
+        workspace = (f["user"], index) if self.user_workspaces else index
         mixed, counters = self.transport.run(
             query, blocks, positions, L["fetches"], cfg.block_size, window=cfg.window,
             window_kv=L["window_buf"], window_start=L["window_start"], compressed=cmp_out,
-            gates=gates, workspace_id=index, segments=segments, output=target)
+            gates=gates, workspace_id=workspace, segments=segments, output=target)
         self.counters.append(counters)
         if target is not None:
             self.exchange.barrier(stream)
@@ -606,7 +617,10 @@ class NSAExtendModel:
         ``prepare_fast``). Graphs of several users may be replayed one after
         another on one stream: they share the transport's per-layer
         workspaces, which the transport keeps (pins) once a captured graph
-        holds them."""
+        holds them. With ``user_workspaces=True`` each user's graph holds its
+        own workspaces (and its own graph memory pool), so graphs of
+        different users may also be replayed concurrently on different
+        streams; one user's graph must not overlap itself."""
         self.prepare_fast(extend_tokens, user, candidates)
         static_ids = torch.zeros(extend_tokens * candidates, dtype=torch.int64,
                                  device=self.device)
