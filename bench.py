@@ -61,7 +61,7 @@ def parse():
                         "its own JSON line")
     p.add_argument("--users-per-pair", type=int, default=4)
     p.add_argument("--users-per-gpu", type=int, default=8)
-    p.add_argument("--lanes", type=int, default=1,
+    p.add_argument("--lanes", type=int, default=4,
                    help="serving: streams the users' captured graphs are spread over "
                         "(round-robin); > 1 gives every user its own transport workspaces "
                         "so one user's host-link-bound fetch runs under another's compute")
