@@ -65,6 +65,9 @@ def parse():
                    help="serving: streams the users' captured graphs are spread over "
                         "(round-robin); > 1 gives every user its own transport workspaces "
                         "so one user's host-link-bound fetch runs under another's compute")
+    p.add_argument("--attend-ctas", type=int, default=37,
+                   help="serving: cap the IO/attention launch at this many CTAs (0: every "
+                        "SM) so concurrent lanes keep SMs for their projections and plans")
     p.add_argument("--queries", type=int, default=4)
     p.add_argument("--jitter", type=int, default=1000)
     p.add_argument("--sigma", type=float, default=0.5)
@@ -522,7 +525,7 @@ def run_serving(args):
     model = NSAExtendModel(cfg, device=device, seed=0, max_users=len(mine),
                            max_history=max_history, read_order=args.read_order,
                            workspaces=cfg.layers * len(mine) + 4, **budget,
-                           **model_options(args))
+                           attend_ctas=args.attend_ctas, **model_options(args))
     t0 = time.perf_counter()
     candidates = {}
     for u in mine:
@@ -635,7 +638,7 @@ def run_serving(args):
                        "suffix": "one packed suffix" if args.packed
                        else "one segment per candidate (history + own suffix)",
                        "users": users_total, "users_per_gpu": args.users_per_gpu,
-                       "lanes": lanes,
+                       "lanes": lanes, "attend_ctas": args.attend_ctas or "every SM",
                        "history_lengths_rank0": [lengths[u] for u in mine],
                        "layers": args.layers, "block_size": 64, "top_n": 16, "window": 512,
                        "compression": compression_config(args),

@@ -23,7 +23,7 @@ READ_ORDERS = {
 }
 
 c_i32, c_i64, c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
-ABI_VERSION = 2  # CXS_ABI_VERSION
+ABI_VERSION = 3  # CXS_ABI_VERSION
 
 
 class CxsError(RuntimeError):
@@ -64,7 +64,7 @@ class AttendGeometry(ctypes.Structure):
         "queries", "heads", "width", "block_size", "physical", "window", "window_len",
         "gate")] + [(name, c_i64) for name in (
             "window_start", "spin_limit", "segment_start", "segment_tokens")] + [
-        ("out_heads", c_i32), ("out_head0", c_i32)]
+        ("out_heads", c_i32), ("out_head0", c_i32), ("ctas", c_i32)]
 
 
 class SelectGeometry(ctypes.Structure):

@@ -655,6 +655,7 @@ int launch(const cxs_attend_geometry& g, const cxs_attend_buffers& b, cudaStream
   int grid = 0;
   int status = grid_size<BS>(&grid);
   if (status != CXS_OK) return status;
+  if (g.ctas > 0 && g.ctas < grid) grid = g.ctas;
   CUtensorMap kv_map, win_map;
   status = encode_kv_map(&kv_map, b.kv, (long long)g.physical * BS, BS);
   if (status != CXS_OK) return status;
@@ -755,6 +756,7 @@ extern "C" int cxs_fetch_attend(const cxs_attend_geometry* geometry,
                                               g.out_head0 + g.heads > g.out_heads)))
     return set_error(CXS_ERR_INVALID, "output heads must hold this call's heads");
   if ((uintptr_t)b.out_peer & 15) return set_error(CXS_ERR_INVALID, "out_peer must be 16-byte aligned");
+  if (g.ctas < 0) return set_error(CXS_ERR_INVALID, "ctas must be >= 0 (0: every SM)");
   switch (g.block_size) {
     case 16: return launch<16>(g, b, (cudaStream_t)stream);
     case 32: return launch<32>(g, b, (cudaStream_t)stream);

@@ -143,7 +143,7 @@ class NSAExtendModel:
                  hot_policy="frequency", read_order="consumption_depth",
                  cross_query_dedup=True, pool_regions=1, chunk=1024, workspaces=None,
                  head_shard=(0, 1), exchange=None, replica_blocks=256, straddle=0.0,
-                 user_workspaces=False, workspace_bytes=2 * 1024**3):
+                 user_workspaces=False, workspace_bytes=2 * 1024**3, attend_ctas=0):
         self.cfg = cfg = cfg or NSAConfig()
         self.device = torch.device(device)
         # KV-head sharding (the long-history serving case, one GPU pair per user): this instance owns KV heads
@@ -214,7 +214,7 @@ class NSAExtendModel:
         self.transport = GRSelectedTransport(
             self.cache, read_order=read_order, cross_query_dedup=cross_query_dedup,
             hot_policy=hot_policy, capacity=workspaces or cfg.layers + 4, async_hot=True,
-            workspace_bytes=workspace_bytes)
+            workspace_bytes=workspace_bytes, attend_ctas=attend_ctas)
         self.fast = None          # fused-glue buffers of the user being served
         self.fast_states = {}     # user -> its fused-glue buffers (prepare_fast)
         self.probe, self.probe_counters = None, []

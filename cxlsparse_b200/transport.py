@@ -96,7 +96,7 @@ class GRSelectedTransport:
     def __init__(self, cache, *, read_order="consumption_depth", cross_query_dedup=True,
                  cuda_graphs=False, capacity=8, workspace_bytes=2 * 1024**3,
                  hot_policy="frequency", spin_limit=1 << 32, query_group=1,
-                 async_hot=False):
+                 async_hot=False, attend_ctas=0):
         if read_order not in _lib.READ_ORDERS:
             raise ValueError("Invalid NSA read priority configuration")
         if hot_policy not in ("frequency", "static", "replica"):
@@ -105,10 +105,16 @@ class GRSelectedTransport:
             raise ValueError("Only single-token consumers (query_group=1) are supported")
         if capacity < 1 or workspace_bytes < 1:
             raise ValueError("Invalid GR selected resource policy")
+        if attend_ctas < 0:
+            raise ValueError("attend_ctas must be >= 0 (0: every SM)")
         _lib.lib()  # fail loudly now if the extension is missing
         self.cache, self.pool = cache, cache.pool
         self.read_order, self.cross_query_dedup = read_order, cross_query_dedup
         self.hot_policy, self.spin_limit = hot_policy, spin_limit
+        # attend_ctas > 0 caps the IO/attention launch at that many CTAs (one
+        # per SM), leaving the other SMs to callers that run other work on
+        # concurrent streams; the plan's consumer count follows the cap.
+        self.attend_ctas = attend_ctas
         adapter = ActivePlanAdapter if cross_query_dedup else QueryPrivatePlanAdapter
         # "replica": residency from the cache's static per-token table
         # (HiSparseCache.enable_replica); like "static", nothing is committed.
@@ -163,7 +169,8 @@ class GRSelectedTransport:
             value = _lib.c_i32(0)
             _lib.check(_lib.lib().cxs_attend_capacity(bs, value))
             self._capacity_cache[bs] = value.value
-        return self._capacity_cache[bs]
+        warps = self._capacity_cache[bs]
+        return min(warps, 4 * self.attend_ctas) if self.attend_ctas else warps
 
     def _workspace(self, qb, heads, width, fetches, bs, window_shape, workspace_id=None):
         # Candidate segments place suffix tokens up to cached + len(current_kv).
@@ -281,7 +288,8 @@ class GRSelectedTransport:
             window_len=w["window_shape"][0] if w["window_shape"] else 0,
             gate=1 if w["window_shape"] else 0, window_start=window_start,
             spin_limit=self.spin_limit, segment_start=segments[0],
-            segment_tokens=segments[1], out_heads=out_heads, out_head0=out_head0)
+            segment_tokens=segments[1], out_heads=out_heads, out_head0=out_head0,
+            ctas=self.attend_ctas)
         timing = self.kernel_timing is not None and not torch.cuda.is_current_stream_capturing()
         if timing:
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define CXS_ABI_VERSION 2
+#define CXS_ABI_VERSION 3
 
 enum cxs_status {
   CXS_OK = 0,
@@ -242,6 +242,10 @@ typedef struct cxs_attend_geometry {
   int64_t segment_tokens;
   int32_t out_heads;  /* 0: `out` is [Q, H, 16, 64]; else [Q, out_heads, 16, 64] and this */
   int32_t out_head0;  /* call's heads are out_head0 .. out_head0 + H - 1 (KV-head split) */
+  int32_t ctas;       /* 0: the IO/attention launch fills every SM; else at most this many
+                         CTAs, leaving the other SMs to work on concurrent streams (the
+                         fetch needs few CTAs to keep the host link busy). The planner's
+                         consumer count should then be min(rows, 4 * ctas). */
 } cxs_attend_geometry;
 
 typedef struct cxs_attend_buffers {

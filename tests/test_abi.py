@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
     assert set(names) == set(_lib.exported_symbols())
     for name in names:
         assert hasattr(lib, name), name
-    assert lib.cxs_abi_version() == _lib.ABI_VERSION == 2
+    assert lib.cxs_abi_version() == _lib.ABI_VERSION == 3
 
 
 def _c_layout(struct, fields):
@@ -88,6 +88,9 @@ def test_invalid_attend_arguments_are_rejected_without_a_device():
     g.block_size, g.gate = 16, 1
     assert lib.cxs_fetch_attend(g, b, None) == _lib.ERR_INVALID
     assert b"gate" in lib.cxs_last_error()
+    g = _lib.AttendGeometry(queries=1, heads=2, width=4, block_size=16, physical=8, ctas=-1)
+    assert lib.cxs_fetch_attend(g, b, None) == _lib.ERR_INVALID
+    assert b"ctas" in lib.cxs_last_error()
 
 
 def test_segment_select_and_exchange_arguments_are_rejected_without_a_device():

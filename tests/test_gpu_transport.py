@@ -61,6 +61,36 @@ def test_live_sources_long_queries_and_replay(cuda, residency):
         pool.close()
 
 
+@pytest.mark.parametrize("ctas", [1, 7])
+@pytest.mark.parametrize("residency", ["miss", "partial"])
+def test_launch_capped_to_few_ctas_matches_oracle(cuda, residency, ctas):
+    """attend_ctas caps the IO/attention launch (SMs left to concurrent
+    streams): one CTA, or seven, still fetch every block and attend every
+    row, the plan's consumer count follows the cap, and outputs and read
+    bytes are unchanged."""
+    pool, cache, backing, source_q, source_pos, source_blocks, fetches = setup_case(residency)
+    transport = GRSelectedTransport(cache, hot_policy="static", attend_ctas=ctas)
+    try:
+        for length in (13, 769):
+            index = torch.arange(length, device="cuda") % len(source_q)
+            query = source_q[index].contiguous()
+            positions = source_pos[index].contiguous()
+            blocks = source_blocks[index].contiguous()
+            expected = _oracle(query, backing, blocks, positions)
+            before = pool.read_bytes
+            output, counters = transport.run(query, blocks, positions, fetches, 16)
+            transport.last_done.synchronize()
+            rows = counters.materialize()
+            pool.flush_read_stats()
+            torch.testing.assert_close(output.cpu().double(), expected, rtol=0.03, atol=0.03)
+            assert pool.read_bytes - before == sum(r["misses"] for r in rows) * 256
+            w = transport.workspace()
+            assert w["consumer_ctas"] == min(w["rows"], 4 * ctas)
+    finally:
+        transport.close()
+        pool.close()
+
+
 @pytest.mark.parametrize("graphs", [False, True])
 def test_poisoned_staging_hot_commit_and_graph(cuda, graphs):
     """tests/test_nsa_tma_transport.py:68-165 (poisoned KV / ready, exact hot commit)."""
