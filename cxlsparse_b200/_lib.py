@@ -178,12 +178,6 @@ def ptr(tensor):
     return None if tensor is None else tensor.data_ptr()
 
 
-def stream_handle(device=None):
-    import torch
-
-    return torch.cuda.current_stream(device).cuda_stream
-
-
 def exported_symbols():
     """Names the header declares (used by the CPU symbol test)."""
     return ("cxs_abi_version", "cxs_last_error", "cxs_launch_count", "cxs_pool_create", "cxs_pool_destroy",

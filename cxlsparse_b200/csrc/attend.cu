@@ -623,11 +623,6 @@ size_t smem_bytes() {
   return 1024 + io + tiles + warps + 128;
 }
 
-struct GridInfo {
-  int grid = 0;
-  int sms = 0;
-};
-
 template <int BS>
 int grid_size(int* grid) {
   static int cached[64] = {0};

@@ -150,16 +150,6 @@ class MemoryPool:
         self.write_operations += 1
         self.write_kernel_launches += 1
 
-    def read_tokens(self, slots):
-        """Host-side copy of token records (test/debug helper)."""
-        out = torch.empty((len(slots), self.dim), dtype=torch.bfloat16)
-        raw = out.view(torch.uint8).numpy()
-        for i, slot in enumerate(slots):
-            region, local = self.location(int(slot))
-            address = self._bases[region][0] + local * self.token_bytes
-            raw[i] = (ctypes.c_uint8 * self.token_bytes).from_address(address)
-        return out
-
     def flush_read_stats(self):
         """Resolve deferred per-region read counts once (mempool/pool.py:459-470)."""
         if not self._pending_read_counts:
