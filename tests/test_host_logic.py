@@ -75,3 +75,16 @@ def test_workspace_estimate_budget_refusal():
     assert t.refusal(256, 16384, 2, 16, 16, 64) == "workspace_budget"
     assert t.refusal(5000, 16384, 2, 16, 16, 64) == "query_bucket_limit"
     assert t.refusal(256, 16384, 2, 8, 16, 64) == "geometry"
+
+
+def test_attend_cta_cap_sets_the_plan_consumer_count():
+    """attend_ctas caps the attention launch; the planner's consumer count
+    (attention warps, 4 per CTA) follows the cap and never exceeds what one
+    CTA per SM gives. A negative cap is refused before touching the device."""
+    with pytest.raises(ValueError, match="attend_ctas"):
+        transport.GRSelectedTransport(SimpleNamespace(pool=None), attend_ctas=-1)
+    t = transport.GRSelectedTransport.__new__(transport.GRSelectedTransport)
+    t._capacity_cache = {64: 148 * 4}
+    for cap, warps in ((0, 592), (37, 148), (1, 4), (148, 592), (500, 592)):
+        t.attend_ctas = cap
+        assert t._attention_warps(64) == warps, cap
