@@ -244,8 +244,10 @@ typedef struct cxs_attend_geometry {
   int32_t out_head0;  /* call's heads are out_head0 .. out_head0 + H - 1 (KV-head split) */
   int32_t ctas;       /* 0: the IO/attention launch fills every SM; else at most this many
                          CTAs, leaving the other SMs to work on concurrent streams (the
-                         fetch needs few CTAs to keep the host link busy). The planner's
-                         consumer count should then be min(rows, 4 * ctas). */
+                         fetch needs few CTAs to keep the host link busy). Any value is
+                         correct; for the best read order the planner's consumer count
+                         is min(rows, 4 * launched CTAs), cxs_attend_capacity giving
+                         4 * the CTAs of an uncapped launch. */
 } cxs_attend_geometry;
 
 typedef struct cxs_attend_buffers {
