@@ -487,9 +487,11 @@ def run_serving(args):
     request per user per step: `queries` candidates of E tokens, each seeing
     the history and its own suffix (candidate segments; --packed packs them
     into one suffix as worker/prompt.py:24-55 does). A step serves every
-    local user once, back to back (one captured graph per user); the final
-    hidden state of every candidate is all-gathered with NCCL (the only
-    collective)."""
+    local user once, one captured graph per user, the users spread over
+    --lanes concurrent streams (each user with its own transport workspaces,
+    the attention launch capped at --attend-ctas CTAs so the other lanes keep
+    SMs; --lanes 1 replays them back to back); the final hidden state of every
+    candidate is all-gathered with NCCL (the only collective)."""
     import torch
 
     from cxlsparse_b200.model import NSAExtendModel
