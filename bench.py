@@ -35,8 +35,11 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # fetch_attend_kernel<64> launch of the H=16384/E=256 extend step, from an
 # ncu --set full capture (NVTX range profile_step). The staged and window KV
-# stay in L2, so DRAM sees far less than the algorithmic bytes.
+# stay in L2, so DRAM sees far less than the algorithmic bytes. A recorded
+# figure, not measured by this run: NCU_TRAFFIC_SOURCE names the capture.
 NCU_DRAM_BYTES_PER_LAUNCH = 2.94e6
+NCU_TRAFFIC_SOURCE = ("recorded, not measured by this run: ncu capture summarised in "
+                      "profiles/fetch_attend_h16k_e256_ncu.md")
 
 
 def parse():
@@ -51,6 +54,9 @@ def parse():
     p.add_argument("--layers", type=int, default=16)
     p.add_argument("--read-order", default="consumption_depth")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-nsa-record", action="store_true",
+                   help="skip the sub-record with BASELINE's NSA parameters (MLP "
+                        "compression) that the default 1-GPU line carries")
     p.add_argument("--workload", default="extend",
                    choices=("extend", "dedup", "serving", "headsplit"),
                    help="dedup: BASELINE configs[2] stress (16 candidates x 128 tokens, "
@@ -266,6 +272,57 @@ def workload(args):
             "parallelism": f"users sharded, {args.gpus} user(s) on {args.gpus} GPU(s)"}
 
 
+def nsa_geometry_record(args, device):
+    """The same extend step with BASELINE's NSA parameters (32/16 MLP
+    compression, block 0 + 2 local blocks forced): tok/s and ms per step of
+    the graph-replayed forward (CUDA events), fetched bytes, and the
+    fetch/attend launch's host-link fraction. A sub-record of the default
+    line, measured after the headline model is closed."""
+    import torch
+
+    from cxlsparse_b200.model import NSAConfig, NSAExtendModel
+
+    cfg = NSAConfig.baseline(layers=args.layers)
+    model = NSAExtendModel(cfg, device=device, seed=0, max_history=args.history + args.extend,
+                           read_order=args.read_order, **model_options(args))
+    try:
+        g = torch.Generator().manual_seed(1000)
+        model.prefill(torch.randint(0, cfg.vocab, (args.history,), generator=g).to(device))
+        ids = torch.randint(0, cfg.vocab, (args.extend,), generator=g)
+        graph, static_ids, _, counters = model.capture_extend(args.extend)
+        static_ids.copy_(ids.to(device))
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize(device)
+        stats = torch.stack([c.statistics for c in counters]).cpu()
+        fetched = int(stats[..., 3].sum()) * 256
+        sampler = ClockSampler(device.index)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize(device)
+        ms = start.elapsed_time(end) / args.steps
+        clocks = sampler.stop()
+        del graph
+        model.transport.kernel_timing = []
+        model.counters.clear()
+        model.extend_fast(static_ids)
+        torch.cuda.synchronize(device)
+        kernel_ms = statistics.mean(s.elapsed_time(e)
+                                    for s, e, _ in model.transport.kernel_timing)
+        model.transport.kernel_timing = None
+        return {"compression": compression_config(argparse.Namespace(compression="mlp")),
+                "value": args.extend / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms,
+                "steps": args.steps, "fetch_bytes_per_step": fetched,
+                "fetch_attend_launch_ms": kernel_ms,
+                "fetch_gb_s_in_kernel": fetched / args.layers / (kernel_ms / 1e3) / 1e9,
+                "clocks": clocks}
+    finally:
+        model.close()
+
+
 def run_ours(args):
     import torch
 
@@ -402,6 +459,7 @@ def run_ours(args):
                          "frac": achieved / hbm,
                          "traffic": NCU_DRAM_BYTES_PER_LAUNCH
                          if (args.history, args.extend) == (16384, 256) else None,
+                         "traffic_source": NCU_TRAFFIC_SOURCE,
                          "binding": "host link: see fetch.frac_of_pcie_in_kernel",
                          "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"
                          if peak_kind == "measured" else "fallback",
@@ -420,6 +478,10 @@ def run_ours(args):
             "clocks": clocks,
             "prefill_s": prefill_s,
         }
+        if world == 1 and args.compression == "mean" and not args.no_nsa_record:
+            del graph
+            model.close()
+            result["nsa_geometry"] = nsa_geometry_record(args, device)
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(args, torch)
         print(json.dumps(result))

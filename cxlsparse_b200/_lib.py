@@ -24,6 +24,11 @@ READ_ORDERS = {
 
 c_i32, c_i64, c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
 ABI_VERSION = 3  # CXS_ABI_VERSION
+# CXS_NOALLOC_MAX_PHYSICAL: most physical blocks cxs_fetch_attend_noalloc
+# takes; its static scratch is 16 bytes per block + 256 (checked against the
+# header by tests/test_abi.py and at compile time in attend.cu).
+NOALLOC_MAX_PHYSICAL = 16384
+NOALLOC_SCRATCH_BYTES = 16 * NOALLOC_MAX_PHYSICAL + 256
 
 
 class CxsError(RuntimeError):

@@ -786,6 +786,8 @@ constexpr size_t kScratchKinds = kScratchSources + 8ull * CXS_NOALLOC_MAX_PHYSIC
 constexpr size_t kScratchReady = kScratchKinds + 4ull * CXS_NOALLOC_MAX_PHYSICAL;
 constexpr size_t kScratchControl = kScratchReady + 4ull * CXS_NOALLOC_MAX_PHYSICAL;
 constexpr size_t kScratchBytes = kScratchControl + 256;
+static_assert(kScratchBytes == 16ull * CXS_NOALLOC_MAX_PHYSICAL + 256,
+              "scratch layout: 8 + 4 + 4 bytes per block plus the 256-byte control word area");
 
 static __device__ __align__(256) unsigned char g_attend_scratch[kScratchBytes];
 

@@ -16,10 +16,52 @@ hot replica).
 """
 
 import ctypes
+from array import array
 
 import torch
 
 from . import _lib
+
+
+class PageAllocator:
+    """Ownership of the pool's pages.
+
+    Free pages sit on a stack. A fresh pool hands pages out in ascending order
+    (0, 1, 2, ...); released pages come back on top, so the most recently
+    released page is handed out first. That is the order of the reference
+    allocator (``mempool/pool.py:100-125``), and the slot numbers of the
+    planner fixtures depend on it. Ownership is one flag per page, so checks
+    cost O(1) per page.
+    """
+
+    def __init__(self, pages):
+        self._owned = bytearray(pages)
+        self._stack = array("q", range(pages - 1, -1, -1))  # top of stack = last item
+
+    @property
+    def free_pages(self):
+        return len(self._stack)
+
+    def owns(self, page):
+        return 0 <= page < len(self._owned) and self._owned[page] == 1
+
+    def allocate(self, count):
+        if not 0 <= count <= len(self._stack):
+            raise ValueError("Backing pool exhausted")
+        keep = len(self._stack) - count
+        taken = self._stack[keep:].tolist()[::-1]
+        del self._stack[keep:]
+        for page in taken:
+            self._owned[page] = 1
+        return taken
+
+    def release(self, pages):
+        pages = list(pages)
+        if len(set(pages)) != len(pages) or not all(self.owns(p) for p in pages):
+            raise ValueError("Invalid page release")
+        for page in pages:
+            self._owned[page] = 0
+        self._stack.extend(pages)
 
 
 class MemoryPool:
@@ -36,8 +78,7 @@ class MemoryPool:
         self.token_bytes = dim * 2
         self.page_bytes = page_size * self.token_bytes
         self.size = pages * self.page_bytes
-        self.free = list(range(pages - 1, -1, -1))
-        self.allocated = set()
+        self.pages_owned = PageAllocator(pages)
         self.read_bytes = self.write_bytes = 0
         self.read_operations = self.write_operations = 0
         self.read_kernel_launches = self.write_kernel_launches = 0
@@ -74,34 +115,28 @@ class MemoryPool:
         return self.regions
 
     def allocate(self, count):
-        if count < 0 or count > len(self.free):
-            raise ValueError("Backing pool exhausted")
-        slots = [self.free.pop() for _ in range(count)]
-        self.allocated.update(slots)
-        return slots
+        return self.pages_owned.allocate(count)
 
     def release(self, slots):
-        if len(slots) != len(set(slots)) or any(s not in self.allocated for s in slots):
-            raise ValueError("Invalid page release")
-        for s in slots:
-            self.allocated.remove(s)
-            self.free.append(s)
+        self.pages_owned.release(slots)
 
     def token_slot(self, page, offset):
-        if page not in self.allocated or not 0 <= offset < self.page_size:
+        if not self.pages_owned.owns(page) or not 0 <= offset < self.page_size:
             raise ValueError("Invalid page or token offset")
         return page * self.page_size + offset
 
     def token_slots(self, pages, start, stop):
-        if not 0 <= start <= stop <= len(pages) * self.page_size:
+        """Slots of token positions [start, stop) of a history laid out over
+        ``pages`` (position t lives at offset t % page_size of pages[t //
+        page_size]); each page is validated once."""
+        size = self.page_size
+        if not 0 <= start <= stop <= len(pages) * size:
             raise ValueError("Invalid token span")
-        slots, cursor = [], start
-        while cursor < stop:
-            page, offset = divmod(cursor, self.page_size)
-            count = min(stop - cursor, self.page_size - offset)
-            base = self.token_slot(pages[page], offset)
-            slots.extend(range(base, base + count))
-            cursor += count
+        slots = []
+        for index in range(start // size, -(-stop // size)):
+            lo, hi = max(start, index * size), min(stop, (index + 1) * size)
+            shift = self.token_slot(pages[index], 0) - index * size
+            slots.extend(range(lo + shift, hi + shift))
         return slots
 
     def location(self, slot):
@@ -234,26 +269,31 @@ class HiSparseCache:
         self.replica_used += n
         self.last_use.record(stream)
 
-    def bind(self, row, slots):
+    def _store_slots(self, row, start, slots, *, clear):
+        """Write pool slots of tokens [start, start + len(slots)) of ``row``
+        into the token -> slot table, ordered after earlier users of the
+        table (``last_use``)."""
         stream = torch.cuda.current_stream(self.data.device)
         stream.wait_event(self.last_use)
-        self.host_locs[row].fill_(-1)
+        table = self.host_locs[row]
+        if clear:
+            table.fill_(-1)
         if len(slots):
-            self.host_locs[row, : len(slots)] = torch.as_tensor(
-                slots, dtype=torch.int64).to(self.data.device)
+            table[start:start + len(slots)].copy_(torch.as_tensor(slots, dtype=torch.int64))
         self.last_use.record(stream)
+
+    def bind(self, row, slots):
+        """Replace the whole history binding of ``row``."""
+        self._store_slots(row, 0, slots, clear=True)
         self.bound_lengths[row] = len(slots)
 
     def append_slots(self, row, start, slots):
-        """Upload an append-only history suffix (mempool/hisparse.py:122-139)."""
-        if not 0 <= row < self.rows or start != self.bound_lengths[row] or \
-                start + len(slots) > self.max_history:
+        """Extend the binding of ``row`` by a suffix that starts where the
+        bound history ends; earlier slots stay as they are
+        (``mempool/hisparse.py:122-139``)."""
+        if (not 0 <= row < self.rows or start != self.bound_lengths[row]
+                or start + len(slots) > self.max_history):
             raise ValueError("Invalid append-only history binding")
-        if not len(slots):
-            return
-        stream = torch.cuda.current_stream(self.data.device)
-        stream.wait_event(self.last_use)
-        self.host_locs[row, start:start + len(slots)] = torch.as_tensor(
-            slots, dtype=torch.int64).to(self.data.device, non_blocking=True)
-        self.last_use.record(stream)
-        self.bound_lengths[row] += len(slots)
+        if len(slots):
+            self._store_slots(row, start, slots, clear=False)
+            self.bound_lengths[row] += len(slots)

@@ -219,6 +219,7 @@ class NSAExtendModel:
         self.fast_states = {}     # user -> its fused-glue buffers (prepare_fast)
         self.probe, self.probe_counters = None, []
         self.selections = None    # a list: eager fast steps append each layer's blocks
+        self.layer_outputs = None  # a list: eager fast steps append each layer's output
         self.users = {}
         self.counters = []
 
@@ -347,7 +348,17 @@ class NSAExtendModel:
             hidden = self._layer(index, hidden, positions, st, append=append)
         if append:
             st.length += len(token_ids)
+        self._check_exchange()
         return rms_norm(hidden, self.final_norm, self.cfg.rms_eps)
+
+    def _check_exchange(self):
+        """Raise if a KV-head exchange barrier of this forward gave up (its
+        wait is bounded; o_proj would then have read a half-filled gather
+        buffer). Reads the device error word, so it synchronises; skipped
+        while a CUDA graph is being captured: whoever replays the graph
+        calls ``exchange.check()`` after the replay."""
+        if self.exchange is not None and not torch.cuda.is_current_stream_capturing():
+            self.exchange.check()
 
     def prefill(self, token_ids, user="user"):
         """Push a history through the model chunk by chunk, persisting its KV
@@ -604,7 +615,10 @@ class NSAExtendModel:
             hidden = F.embedding(token_ids, self.embed)
         for index in range(self.cfg.layers):
             hidden = self._layer_fast(index, hidden)
+            if self.layer_outputs is not None:
+                self.layer_outputs.append(hidden)
         self.transport.join()
+        self._check_exchange()
         out = torch.empty_like(hidden)
         _lib.check(_lib.lib().cxs_rms_norm(
             hidden.data_ptr(), self.final_norm.data_ptr(), out.data_ptr(), len(hidden),

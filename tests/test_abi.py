@@ -132,3 +132,16 @@ def test_segment_select_and_exchange_arguments_are_rejected_without_a_device():
     assert lib.cxs_exchange_barrier(q, peers, q, 2, 2, 100, q, None) == _lib.ERR_INVALID
     assert lib.cxs_exchange_barrier(q, (ctypes.c_void_p * 2)(None, None), q, 0, 2, 100, q,
                                     None) == _lib.ERR_INVALID
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc required")
+def test_noalloc_limit_matches_header(tmp_path):
+    """The Python mirror of CXS_NOALLOC_MAX_PHYSICAL is the header's value."""
+    c_file = tmp_path / "limit.c"
+    c_file.write_text('#include <stdio.h>\n#include "cxlsparse.h"\n'
+                      'int main(void) { printf("%d\\n", CXS_NOALLOC_MAX_PHYSICAL); return 0; }\n')
+    exe = tmp_path / "limit"
+    subprocess.run(["gcc", "-I", str(HEADER.parent), str(c_file), "-o", str(exe)], check=True)
+    value = int(subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout)
+    assert value == _lib.NOALLOC_MAX_PHYSICAL
+    assert _lib.NOALLOC_SCRATCH_BYTES == 16 * value + 256

@@ -54,12 +54,8 @@ def test_noalloc_entry_point_matches_regular_entry_point(cuda, residency):
 
 def test_noalloc_rejects_oversized_geometry(cuda):
     geometry = _lib.AttendGeometry(queries=1, heads=2, width=4, block_size=16,
-                                   physical=_lib_max() + 1)
+                                   physical=_lib.NOALLOC_MAX_PHYSICAL + 1)
     buffers = _lib.AttendBuffers()
     status = _lib.lib().cxs_fetch_attend_noalloc(geometry, buffers, None)
     assert status == _lib.ERR_CAPACITY
     assert b"at most" in _lib.lib().cxs_last_error()
-
-
-def _lib_max():
-    return 16384
