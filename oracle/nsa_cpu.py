@@ -9,8 +9,14 @@ torch on the host cores, vectorised the same way (per-tile bmm). It is test
 infrastructure: ``bench.py`` times it as the CPU baseline and as the
 ``--impl reference`` arm; the product package never imports it.
 
-History K/V, summaries and windows are seeded N(0, 1) stand-ins of the right
-shapes: throughput does not depend on their values.
+Pinned: on one seeded layer, ``CPUExtendPath.layer`` reproduces the output of
+the reference's own CPU route (its ``_project``, ``local_branches(...,
+backend="torch")``, ``indexed_attention`` and ``_finish``, run into
+tests/golden/cpu_layer.npz) within 1e-5, and its selected tokens exactly
+(tests/test_cpu_port_pinned.py).
+
+For timing, history K/V, summaries and windows are seeded N(0, 1) stand-ins
+of the right shapes: throughput does not depend on their values.
 """
 
 import time

@@ -281,10 +281,95 @@ def dense_case(reference_root, seed=2024):
     np.savez_compressed(HERE / "dense_model.npz", **out)
 
 
+CPU_LAYER = dict(hidden=128, q_heads=8, kv_heads=2, head_dim=64, ffn=192, history=640,
+                 extend=40, block_size=64, block_counts=4, window=96, tile=16)
+
+
+def cpu_layer_case(seed=2025):
+    """One NSA extend layer through the reference's own CPU torch route, in
+    fp32: ``NSAModel._project`` (RMSNorm, q/k/v/g projections, rotary),
+    ``ops.append_compressed``, ``ops.local_branches(..., backend="torch")``
+    (compressed branch, top-n, window), ``ops.indexed_attention`` over the
+    selected tokens packed per KV head as the model's ``selected_finish``
+    packs them, and ``NSAModel._finish`` (gate mix, o_proj, FFN)
+    (``models/nsa/model.py:440-492, 828-857``, ``models/nsa/ops.py:12-205``).
+    The model methods run on a stand-in ``self`` carrying only the fields
+    they read. The CPU baseline restatement (oracle/nsa_cpu.py) is pinned to
+    this output."""
+    import json
+    import types
+
+    import torch
+
+    # The model module's import chain reaches the RPC module, whose `orjson`
+    # import a JSON stand-in satisfies (nothing here uses it).
+    sys.modules.setdefault("orjson", types.SimpleNamespace(
+        dumps=lambda o, **_: json.dumps(o).encode(), loads=json.loads))
+    from cxl_recsys.models.nsa import ops
+    from cxl_recsys.models.nsa.model import NSAModel
+
+    c = CPU_LAYER
+    hidden, q_heads, kv_heads, d, ffn = (c[k] for k in ("hidden", "q_heads", "kv_heads",
+                                                         "head_dim", "ffn"))
+    history, extend, bs, window = c["history"], c["extend"], c["block_size"], c["window"]
+    groups = q_heads // kv_heads
+    g = torch.Generator().manual_seed(seed)
+
+    def normal(*shape, scale=0.05):
+        return (torch.randn(shape, generator=g) * scale).bfloat16().float()
+
+    shapes = {"self_attn.q_proj.weight": (q_heads * d, hidden),
+              "self_attn.k_proj.weight": (kv_heads * d, hidden),
+              "self_attn.v_proj.weight": (kv_heads * d, hidden),
+              "self_attn.g_proj.weight": (q_heads * 3, hidden),
+              "self_attn.o_proj.weight": (hidden, q_heads * d),
+              "mlp.gate_proj.weight": (ffn, hidden), "mlp.up_proj.weight": (ffn, hidden),
+              "mlp.down_proj.weight": (hidden, ffn)}
+    weights = {f"model.layers.0.{k}": normal(*s) for k, s in shapes.items()}
+    for name in ("input_layernorm.weight", "post_attention_layernorm.weight"):
+        weights[f"model.layers.0.{name}"] = torch.ones(hidden)
+    model = SimpleNamespace(
+        config=SimpleNamespace(num_attention_heads=q_heads, head_dim=d, rms_norm_eps=1e-6),
+        heads=kv_heads, groups=groups, weights=weights,
+        inv_freq=1.0 / 10000.0 ** (torch.arange(0, d, 2).float() / d))
+    model._finish_prepare = lambda *a, **kw: NSAModel._finish_prepare(model, *a, **kw)
+    history_kv = normal(history, kv_heads, 2 * d, scale=1.0)
+    x = normal(extend, hidden, scale=1.0)
+    positions = torch.arange(history, history + extend)
+    query, records, gates = NSAModel._project(model, x, positions, 0)
+    summaries = history_kv.reshape(-1, bs, kv_heads, 2 * d).float().mean(1)
+    compressed, _ = ops.append_compressed(summaries, history_kv[:0], records, bs)
+    retained = history_kv[history - (window - 1):]
+    cmp_out, win_out, selected = ops.local_branches(
+        query, compressed, torch.cat((retained, records)), positions,
+        total=history + extend, window_start=history - (window - 1), block_size=bs,
+        block_counts=c["block_counts"], window_size=window, tile=c["tile"], backend="torch")
+    sequence = torch.cat((history_kv, records))                       # [T, H, 128]
+    total = len(sequence)
+    values = sequence.permute(1, 0, 2).reshape(kv_heads * total, 2 * d)
+    indices = torch.cat([torch.where(selected[:, h] >= 0, selected[:, h] + h * total, -1)
+                         for h in range(kv_heads)])
+    packed = torch.cat([query[:, h] for h in range(kv_heads)])
+    attended = ops.indexed_attention(packed, values, indices, c["tile"])
+    selected_out = attended.view(kv_heads, extend, groups, d).transpose(0, 1)
+    (out,) = NSAModel._finish(model, x, selected_out, cmp_out, win_out, gates, 0)
+    result = {f"w:{k}": v.bfloat16().view(torch.int16).numpy() for k, v in weights.items()}
+    result.update(history_kv=history_kv.bfloat16().view(torch.int16).numpy(),
+                  hidden=x.bfloat16().view(torch.int16).numpy(),
+                  selected=selected.numpy(), compressed_out=cmp_out.numpy(),
+                  window_out=win_out.numpy(), selected_out=selected_out.numpy(),
+                  output=out.numpy(), meta=np.array([c[k] for k in CPU_LAYER]))
+    np.savez_compressed(HERE / "cpu_layer.npz", **result)
+
+
 def main():
-    if len(sys.argv) != 2:
+    if len(sys.argv) < 2:
         raise SystemExit(__doc__)
     _setup(Path(sys.argv[1]).resolve())
+    if sys.argv[2:] == ["cpu_layer"]:  # regenerate only this fixture
+        cpu_layer_case()
+        return
+    cpu_layer_case()
     dense_case(Path(sys.argv[1]).resolve())
     common = dict(heads=2, hot=32)
     plan_case("miss_bs16_depth", seed=1, queries=13, width=4, bs=16, old=67,
