@@ -220,6 +220,7 @@ class NSAExtendModel:
         self.probe, self.probe_counters = None, []
         self.selections = None    # a list: eager fast steps append each layer's blocks
         self.layer_outputs = None  # a list: eager fast steps append each layer's output
+        self.attention_outputs = None  # a list: ... and each layer's gated attention output
         self.users = {}
         self.counters = []
 
@@ -592,6 +593,8 @@ class NSAExtendModel:
         self.counters.append(counters)
         if target is not None:
             self.exchange.barrier(stream)
+        if self.attention_outputs is not None:  # the transport's output is a borrowed view
+            self.attention_outputs.append(mixed[:E].clone())
         hidden = torch.addmm(hidden, mixed.reshape(E, -1), w["o"].t())
         _lib.check(lib.cxs_rms_norm(hidden.data_ptr(), w["post_norm"].data_ptr(), x.data_ptr(),
                                     E, cfg.hidden, cfg.rms_eps, stream))

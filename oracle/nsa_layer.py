@@ -1,9 +1,10 @@
-"""One NSA extend layer in float64 (test oracle).
+"""One NSA extend layer, in float64 or in the reference's bf16 sequence (test oracle).
 
 Given one layer's input hidden states, its weights, the user's stored
 history K/V for that layer (read back from the backing pool by the caller)
 and the block selections the device made for the layer, this computes the
-layer's output hidden states with every step restated in exact arithmetic:
+layer's output hidden states, either in exact arithmetic (float64) or with
+the reference model's bf16 rounding sequence:
 
 * RMSNorm, q/k/v/gate projections, rotary embedding, o_proj, RMSNorm and the
   SwiGLU FFN (``models/nsa/model.py:440-492``, ``models/tensor_ops.py``);
@@ -28,27 +29,38 @@ Test infrastructure only: the product package never imports it.
 """
 
 import torch
+import torch.nn.functional as F
 
 F64 = torch.float64
 
 
-def _norm(x, weight, eps):
-    return x * torch.rsqrt(x.square().mean(-1, keepdim=True) + eps) * weight.to(F64)
+def _norm(x, weight, eps, acc):
+    """RMSNorm as the reference computes it (models/tensor_ops.py): the
+    statistics in the accumulation type, the result in x's type, then the
+    gain."""
+    value = x.to(acc)
+    normalized = value * torch.rsqrt(value.square().mean(-1, keepdim=True) + eps)
+    return normalized.to(x.dtype) * weight
 
 
-def _rotate(x, positions, theta):
+def _rotate(x, positions, theta, acc):
+    """Rotate-half RoPE; the phase in the accumulation type, cos / sin and the
+    products in x's type (models/tensor_ops.py rotary)."""
     dim = x.shape[-1]
-    inv = 1.0 / theta ** (torch.arange(0, dim, 2, device=x.device, dtype=F64) / dim)
-    phase = positions.to(F64)[:, None] * inv[None, :]
-    phase = torch.cat((phase, phase), -1)[:, None, :]
+    inv = 1.0 / theta ** (torch.arange(0, dim, 2, device=x.device, dtype=acc) / dim)
+    phase = positions.to(acc)[:, None] * inv[None, :]
+    phase = torch.cat((phase, phase), -1)
+    cos, sin = phase.cos().to(x.dtype)[:, None, :], phase.sin().to(x.dtype)[:, None, :]
     left, right = x[..., : dim // 2], x[..., dim // 2:]
-    return x * phase.cos() + torch.cat((-right, left), -1) * phase.sin()
+    return x * cos + torch.cat((-right, left), -1) * sin
 
 
-def _attend(q, k, v, mask):
+def _attend(q, k, v, mask, acc):
     """q [R, H, G, d], k / v [R, H, S, d] per row (or [S, H, d] shared),
-    mask [R, S] or [R, H, S] -> [R, H, G, d]; a row with nothing visible gets 0."""
+    mask [R, S] or [R, H, S] -> [R, H, G, d] in q's type, computed in the
+    accumulation type; a row with nothing visible gets 0."""
     scale = q.shape[-1] ** -0.5
+    q, k, v = q.to(acc), k.to(acc), v.to(acc)
     if k.dim() == 3:
         logits = torch.einsum("rhgd,shd->rhgs", q, k) * scale
     else:
@@ -64,7 +76,8 @@ def _attend(q, k, v, mask):
 
 def _compress_windows(sequence, w, length, stride):
     """Keys [C, H, 128] of the complete windows [i * stride, i * stride +
-    length) of sequence [T, H, 128]: for K and V, W2 silu(W1 vec(x + pe))."""
+    length) of sequence [T, H, 128]: for K and V, W2 silu(W1 vec(x + pe)),
+    every step in the sequence's type."""
     total, heads, width = sequence.shape
     d = width // 2
     count = (total - length) // stride + 1 if total >= length else 0
@@ -74,8 +87,8 @@ def _compress_windows(sequence, w, length, stride):
     parts = []
     for i, lo in enumerate((0, d)):
         x = windows[..., lo: lo + d] + w["cmp_pe"][i]
-        hid = torch.nn.functional.silu(x.reshape(count, heads, length * d) @ w["cmp_w1"][i].T)
-        parts.append(hid @ w["cmp_w2"][i].T)
+        hid = F.silu(F.linear(x.reshape(count, heads, length * d), w["cmp_w1"][i]))
+        parts.append(F.linear(hid, w["cmp_w2"][i]))
     return torch.cat(parts, -1)
 
 
@@ -89,43 +102,58 @@ def _tokens_of(blocks, positions, bs):
     return tokens, keep
 
 
+PRECISIONS = {"f64": (F64, F64), "bf16": (torch.bfloat16, torch.float32)}
+
+
 def extend_layer(hidden, weights, history, positions, blocks, *, q_heads, kv_heads, head_dim,
                  block_size, window, rope_theta=10000.0, eps=1e-6, compression="mean",
-                 cmp_block=32, cmp_stride=16, row_chunk=64, return_records=False):
+                 cmp_block=32, cmp_stride=16, row_chunk=64, precision="f64",
+                 return_records=False, trace=False):
     """One candidate's rows through one layer.
 
     hidden [R, D] (any float dtype; the layer input), history [old, H, 128]
     (K || V of tokens 0 .. old - 1), positions [R] = old .. old + R - 1 (the
     rows are the tokens that follow the history, in order), blocks [R, H, n]
-    true block ids (-1: unused slot) -> output [R, D] float64 (and, with
-    ``return_records``, the rows' own K || V [R, H, 128]).
+    true block ids (-1: unused slot) -> output [R, D].
+
+    ``precision``: "f64" computes everything in float64 (exact arithmetic
+    for these sizes); "bf16" follows the reference model's rounding sequence
+    (``models/nsa/model.py:440-492``, ``models/tensor_ops.py``, the torch
+    branch of ``ops.py``): every tensor, GEMM output and elementwise result
+    rounded to bf16, attention scores / softmax / weighted sums in fp32 with
+    bf16 outputs, gate mix as bf16 multiply and two addcmuls. With
+    ``return_records`` the rows' own K || V [R, H, 128] comes back too; with
+    ``trace`` a dict with "out", "records", "mixed" (the gated attention
+    output [R, H, G, d]) and "branches" (compressed, selected, window).
     """
+    dt, acc = PRECISIONS[precision]
     device = hidden.device
-    w = {name: t.to(F64) for name, t in weights.items()}
+    w = {name: t.to(dt) for name, t in weights.items()}
     rows, groups, d = len(hidden), q_heads // kv_heads, head_dim
     positions = positions.to(device=device, dtype=torch.int64)
-    h = hidden.to(F64)
-    x = _norm(h, w["in_norm"], eps)
-    q = (x @ w["q"].T).view(rows, q_heads, d)
-    k = (x @ w["k"].T).view(rows, kv_heads, d)
-    v = (x @ w["v"].T).view(rows, kv_heads, d)
-    gates = torch.sigmoid(x @ w["g"].T).view(rows, kv_heads, groups, 3)
-    q, k = _rotate(q, positions, rope_theta), _rotate(k, positions, rope_theta)
-    q = q.view(rows, kv_heads, groups, d)
-    sequence = torch.cat((history.to(device, F64), torch.cat((k, v), -1)))  # [T, H, 128]
+    h = hidden.to(dt)
+    x = _norm(h, w["in_norm"], eps, acc)
+    q = F.linear(x, w["q"]).view(rows, q_heads, d)
+    k = F.linear(x, w["k"]).view(rows, kv_heads, d)
+    v = F.linear(x, w["v"]).view(rows, kv_heads, d)
+    gates = torch.sigmoid(F.linear(x, w["g"])).view(rows, kv_heads, groups, 3)
+    q, k = _rotate(q, positions, rope_theta, acc), _rotate(k, positions, rope_theta, acc)
+    q = q.reshape(rows, kv_heads, groups, d)
+    sequence = torch.cat((history.to(device, dt), torch.cat((k, v), -1)))  # [T, H, 128]
     total = len(sequence)
 
     # Compressed branch.
     if compression == "mean":
         complete = total // block_size
         keys = sequence[: complete * block_size].view(complete, block_size, kv_heads, 2 * d)
-        keys = keys.mean(1)
+        keys = keys.to(acc).mean(1).to(dt)
         ends = (torch.arange(complete, device=device) + 1) * block_size
     else:
         keys = _compress_windows(sequence, w, cmp_block, cmp_stride)
         ends = torch.arange(len(keys), device=device) * cmp_stride + cmp_block
     if len(keys):
-        cmp = _attend(q, keys[..., :d], keys[..., d:], ends[None, :] <= positions[:, None] + 1)
+        cmp = _attend(q, keys[..., :d], keys[..., d:],
+                      ends[None, :] <= positions[:, None] + 1, acc).to(dt)
     else:
         cmp = torch.zeros_like(q)
 
@@ -139,21 +167,24 @@ def extend_layer(hidden, weights, history, positions, blocks, *, q_heads, kv_hea
         tokens, keep = _tokens_of(blocks[r], pos, block_size)
         gathered = sequence[tokens.clamp(max=total - 1),  # masked tokens: any index
                             torch.arange(kv_heads, device=device)[None, :, None]]
-        slc[r] = _attend(q[r], gathered[..., :d], gathered[..., d:], keep)
+        slc[r] = _attend(q[r], gathered[..., :d], gathered[..., d:], keep, acc).to(dt)
         # Window (pos - W, pos].
         span = pos[:, None] - window + 1 + torch.arange(window, device=device)[None, :]
         visible = span >= 0
-        near = sequence[span.clamp(min=0)]                              # [r, W, H, 128]
-        near = near.permute(0, 2, 1, 3)
-        win[r] = _attend(q[r], near[..., :d], near[..., d:], visible)
+        near = sequence[span.clamp(min=0)].permute(0, 2, 1, 3)         # [r, H, W, 128]
+        win[r] = _attend(q[r], near[..., :d], near[..., d:], visible, acc).to(dt)
 
-    mixed = slc * gates[..., 1, None] + cmp * gates[..., 0, None] + win * gates[..., 2, None]
-    h = h + mixed.reshape(rows, -1) @ w["o"].T
-    x = _norm(h, w["post_norm"], eps)
-    ffn = torch.nn.functional.silu(x @ w["gate"].T) * (x @ w["up"].T)
-    out = h + ffn @ w["down"].T
+    mixed = slc * gates[..., 1, None]
+    mixed = torch.addcmul(mixed, cmp, gates[..., 0, None])
+    mixed = torch.addcmul(mixed, win, gates[..., 2, None])
+    h = h + F.linear(mixed.reshape(rows, -1), w["o"])
+    x = _norm(h, w["post_norm"], eps, acc)
+    out = h + F.linear(F.silu(F.linear(x, w["gate"])) * F.linear(x, w["up"]), w["down"])
+    records = sequence[len(history):]
+    if trace:
+        return dict(out=out, records=records, mixed=mixed, branches=(cmp, slc, win))
     if return_records:  # this chunk's K || V, as a later chunk's history
-        return out, sequence[len(history):]
+        return out, records
     return out
 
 

@@ -17,6 +17,8 @@ from golden_io import GOLDEN, load
 from oracle.nsa_dense import dense_forward
 from oracle.nsa_layer import _norm, extend_layer, layer_agreement
 
+F64 = torch.float64
+
 NAMES = dict(q="self_attn.q_proj", k="self_attn.k_proj", v="self_attn.v_proj",
              g="self_attn.g_proj", o="self_attn.o_proj", gate="mlp.gate_proj",
              up="mlp.up_proj", down="mlp.down_proj", in_norm="input_layernorm",
@@ -31,24 +33,28 @@ def _all_blocks(positions, heads, bs):
     return table[:, None, :].expand(-1, heads, -1).contiguous()
 
 
-def _chained(ids, embed, layers, final_norm, split, **geometry):
+def _chained(ids, embed, layers, final_norm, split, precision="f64", **geometry):
     """Prefill tokens [0, split) then extend [split, T), layer by layer."""
-    hidden = embed.double()[ids]
+    dt = torch.bfloat16 if precision == "bf16" else F64
+    hidden = embed.to(dt)[ids]
     prefix, suffix = hidden[:split], hidden[split:]
     kv = geometry["kv_heads"]
-    empty = torch.zeros(0, kv, 128, dtype=torch.float64)
+    empty = torch.zeros(0, kv, 128, dtype=dt)
     first = torch.arange(split)
     rest = torch.arange(split, len(ids))
     bs = geometry["block_size"]
     for w in layers:
         prefix, records = extend_layer(prefix, w, empty, first, _all_blocks(first, kv, bs),
-                                       return_records=True, **geometry)
-        suffix = extend_layer(suffix, w, records, rest, _all_blocks(rest, kv, bs), **geometry)
-    return _norm(suffix, final_norm, geometry["eps"])
+                                       return_records=True, precision=precision, **geometry)
+        suffix = extend_layer(suffix, w, records, rest, _all_blocks(rest, kv, bs),
+                              precision=precision, **geometry)
+    acc = torch.float32 if precision == "bf16" else F64
+    return _norm(suffix, final_norm.to(dt), geometry["eps"], acc)
 
 
+@pytest.mark.parametrize("precision", ["f64", "bf16"])
 @pytest.mark.parametrize("length,split", [(143, 100), (256, 137)])
-def test_chained_layer_oracle_matches_reference_dense_oracle(length, split):
+def test_chained_layer_oracle_matches_reference_dense_oracle(length, split, precision):
     z = load(GOLDEN / "dense_model.npz")
     layers_n, block_size, window = (int(v) for v in z["meta"])
     w = {k[2:]: torch.from_numpy(v).view(torch.bfloat16) for k, v in z.items()
@@ -57,14 +63,16 @@ def test_chained_layer_oracle_matches_reference_dense_oracle(length, split):
               for i in range(layers_n)]
     ids = torch.from_numpy(z[f"ids_{length}"])
     got = _chained(ids, w["model.embed_tokens.weight"], layers, w["model.norm.weight"], split,
-                   q_heads=32, kv_heads=2, head_dim=64, block_size=block_size, window=window,
-                   rope_theta=500000.0, eps=1e-5)
+                   precision, q_heads=32, kv_heads=2, head_dim=64, block_size=block_size,
+                   window=window, rope_theta=500000.0, eps=1e-5)
     want = torch.from_numpy(z[f"out_{length}"]).view(torch.bfloat16)[split:]
     diff, cos = layer_agreement(got, want)
     # The reference oracle rounds activations to bf16 (outputs are RMS-normalised,
-    # magnitude ~1, bf16 spacing 2^-7 there): measured 0.027 / 0.031 max-abs,
-    # cosine 0.99995.
-    assert diff <= 0.05 and cos >= 0.9999, (diff, cos)
+    # magnitude ~1-4, bf16 spacing 2^-6 .. 2^-5 there). Measured: float64 mode
+    # 0.027 / 0.031 max-abs, cosine 0.99995; bf16 mode (the same rounding
+    # sequence, different reduction orders) 0.016 / 0.047, cosine >= 0.99996:
+    # two bf16 evaluations of the same arithmetic differ by 1-3 bf16 spacings.
+    assert diff <= 0.0625 and cos >= 0.9999, (precision, diff, cos)
 
 
 @pytest.mark.parametrize("compression", ["mean", "mlp"])
