@@ -272,6 +272,13 @@ def workload(args):
             "parallelism": f"users sharded, {args.gpus} user(s) on {args.gpus} GPU(s)"}
 
 
+def _lib_numa_node(device_index):
+    """NUMA node of a GPU as the pool allocator sees it (-1: unknown)."""
+    from cxlsparse_b200 import _lib
+
+    return int(_lib.lib().cxs_device_numa_node(device_index))
+
+
 def nsa_geometry_record(args, device):
     """The same extend step with BASELINE's NSA parameters (32/16 MLP
     compression, block 0 + 2 local blocks forced): tok/s and ms per step of
@@ -397,7 +404,8 @@ def run_ours(args):
         graph.replay()
     end.record(stream)
     barrier()
-    device_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    local_ms = start.elapsed_time(end) / args.steps
+    device_ms = max_over_ranks(local_ms)
 
     # --- end-to-end: pinned H2D ids, replay, gather scores, D2H ------------
     host_ids = candidates.pin_memory()
@@ -434,6 +442,17 @@ def run_ours(args):
     # Fetched-byte reduction of the deduplicating plan vs the query-private
     # plan on the same selections and cache state (reference traffic metric).
     shared_miss, private_miss = model.compare_private_plan(static_ids)
+    # Every rank's own host-link figures: with several GPUs per host the
+    # pinned-memory reads of all ranks share sockets and PCIe switches.
+    mine = {"rank": rank, "device_ms_per_step": local_ms,
+            "fetch_gb_s_in_kernel": layer_fetch / (kernel_ms / 1e3) / 1e9,
+            "fetch_launch_ms": kernel_ms, "pcie_h2d_peak_gb_s": pcie,
+            "pool_numa_nodes": model.pool.numa_nodes,
+            "gpu_numa_node": _lib_numa_node(local)}
+    per_rank = [mine]
+    if dist is not None:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, mine)
 
     result = None
     if rank == 0:
@@ -477,6 +496,7 @@ def run_ours(args):
                       "fetched_byte_reduction": 1 - shared_miss / max(private_miss, 1)},
             "clocks": clocks,
             "prefill_s": prefill_s,
+            "per_rank": per_rank,
         }
         if world == 1 and args.compression == "mean" and not args.no_nsa_record:
             del graph
