@@ -354,10 +354,16 @@ def run_ours(args):
         for _ in range(args.warmup):
             model.extend_fast(ids)
         torch.cuda.synchronize(device)
+        model.counters.clear()
         torch.cuda.nvtx.range_push("profile_step")
         model.extend_fast(ids)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(device)
+        # Algorithmic host-link bytes of each profiled layer (misses x 256),
+        # to set beside a capture's sysmem / PCIe read counters.
+        misses = [int(c.statistics[:, 3].sum()) for c in model.counters]
+        print(json.dumps({"profile_step_layer_miss_bytes": [m * 256 for m in misses]}),
+              file=sys.stderr)
         model.close()
         return None
     graph, static_ids, static_out, counters = model.capture_extend(args.extend)
