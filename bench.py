@@ -58,13 +58,17 @@ def parse():
                    help="skip the sub-record with BASELINE's NSA parameters (MLP "
                         "compression) that the default 1-GPU line carries")
     p.add_argument("--workload", default="extend",
-                   choices=("extend", "dedup", "serving", "headsplit"),
+                   choices=("extend", "dedup", "serving", "headsplit", "gr"),
                    help="dedup: BASELINE configs[2] stress (16 candidates x 128 tokens, "
                         "all history cold); serving: BASELINE configs[3] (users per GPU "
                         "with jittered ~32K histories, 4 queries x E per user); "
                         "headsplit: BASELINE configs[4] (the KV heads of each user split "
-                        "over a GPU pair, H=128K, 8 queries x E per user); each prints "
+                        "over a GPU pair, H=128K, 8 queries x E per user); gr: GR request "
+                        "replay through the worker / scheduler serving shell; each prints "
                         "its own JSON line")
+    p.add_argument("--gr-points", default="all", choices=("all", "one"),
+                   help="gr: every H in {4K, 8K, 16K} x E in {128, 256}, or only "
+                        "--history / --extend")
     p.add_argument("--users-per-pair", type=int, default=4)
     p.add_argument("--users-per-gpu", type=int, default=8)
     p.add_argument("--lanes", type=int, default=4,
@@ -759,6 +763,82 @@ def run_serving(args):
     return result
 
 
+# The reference's published steady-state medians on one H100 (its own method,
+# case cxl_tma_shared: worker_ms_p50 / e2e_ms_p50 of results/final/summary.csv,
+# batch 1, hot 256, 3 warm-up + 15 measured visits per round, 2 rounds).
+REFERENCE_GR_P50_MS = {
+    (4096, 128): (11.263, 14.403), (4096, 256): (12.944, 16.618),
+    (8192, 128): (12.712, 17.343), (8192, 256): (14.622, 19.023),
+    (16384, 128): (16.803, 25.304), (16384, 256): (18.959, 28.245),
+}
+
+
+def run_gr(args):
+    """GR request replay through the serving shell (cxlsparse_b200/serving.py):
+    for every (history, extend) point one user with that history, then
+    ``--warmup`` + ``--steps`` visits with a fresh candidate suffix of E
+    tokens (8 items) each, admitted by the scheduler one after another and
+    served by the worker (captured 16-layer extend graph per user and
+    suffix length, candidate selection on the final hidden state). Reports
+    per point the median worker execution time and the median end-to-end
+    time (admission to completion seen by the scheduler, in-process) beside
+    the reference's published H100 medians for the same point."""
+    import torch
+
+    from cxlsparse_b200.model import NSAExtendModel
+    from cxlsparse_b200.serving import ExtendRunner, Scheduler, Worker, gr_sequence, percentile
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    if args.gr_points == "all":
+        points = [(h, e) for h in (4096, 8192, 16384) for e in (128, 256)]
+    else:
+        points = [(args.history, args.extend)]
+    histories = sorted({h for h, _ in points})
+    cfg = nsa_config(args)
+    model = NSAExtendModel(cfg, device=device, seed=0, max_users=len(histories),
+                           max_history=max(histories) + max(e for _, e in points),
+                           workspaces=cfg.layers + 4)
+    worker = Worker(ExtendRunner(model, graphs=len(points) + 1), queue_capacity=1)
+    out = []
+    try:
+        for index, (history, extend) in enumerate(points):
+            user = f"history-{history}"
+            requests = gr_sequence(1, history, extend, warmup=args.warmup, measured=args.steps,
+                                   candidates=8, vocab=cfg.vocab, seed=history)
+            for r in requests:
+                r["user_id"] = user
+                r["request_id"] = f"{user}-{extend}-{r['request_id']}"
+            summary = Scheduler(worker).run_sequence(requests, timeout=600)
+            if not summary["passed"]:
+                raise RuntimeError(f"GR replay failed: {summary['state']} "
+                                   f"{summary['worker']['error']}")
+            timed = summary["requests"][args.warmup:]
+            worker_ms = [r["execution_ms"] for r in timed]
+            e2e_ms = [r["e2e_ms"] for r in timed]
+            ref_worker, ref_e2e = REFERENCE_GR_P50_MS.get((history, extend), (None, None))
+            p50 = percentile(e2e_ms, 50)
+            out.append({"history": history, "extend": extend, "visits": len(timed),
+                        "worker_ms_p50": percentile(worker_ms, 50),
+                        "e2e_ms_p50": p50, "e2e_ms_p10": percentile(e2e_ms, 10),
+                        "e2e_ms_p90": percentile(e2e_ms, 90),
+                        "tok_s_at_e2e_p50": extend / (p50 / 1e3),
+                        "fetched_bytes_median": percentile(
+                            [r["result"]["cache"]["read_bytes"] for r in timed], 50),
+                        "reference_h100_worker_ms_p50": ref_worker,
+                        "reference_h100_e2e_ms_p50": ref_e2e,
+                        "e2e_speedup_vs_reference": ref_e2e / p50 if ref_e2e else None})
+    finally:
+        worker.close()
+    print(json.dumps({
+        "workload": "GR request replay through the worker / scheduler serving shell "
+                    "(steady visits, batch 1, frequency hot set of 256 tokens)",
+        "metric": "E2E p50 ms per request (lower is better)", "higher_is_better": False,
+        "compression": compression_config(args), "points": out,
+        "e2e_boundary": "in-process: scheduler admission to completion; the reference's "
+                        "E2E also crosses its gRPC hop"}))
+
+
 def _reserve_stdout():
     """Keep the real stdout for the one JSON line; route everything else that
     writes to file descriptor 1 (e.g. NCCL's version banner) to stderr."""
@@ -951,6 +1031,12 @@ def main():
     args = parse()
     if args.workload == "dedup":
         run_dedup(args)
+        return
+    if args.workload == "gr":
+        if args.impl == "reference":
+            run_reference(args)
+        else:
+            run_gr(args)
         return
     if args.workload in ("serving", "headsplit"):
         if args.impl == "reference":
