@@ -9,16 +9,15 @@
 //    score descending with ties to the lower block id; width =
 //    min(count, ceil(total / BS)); remaining entries -1.
 //
-// Two kernels. compressed_select_tc_kernel (tcgen05 / TMEM, 8 query rows per
-// CTA, 16 warps) serves every geometry whose per-row scores fit in shared memory (up to
-// 2048 blocks); compressed_select_kernel (one CTA of 4 warps per query row,
-// mma.sync tiles) serves longer histories. In the latter the warps split the
-// 64-summary tiles (staged by 3-D tensor TMA). Pass 1: per-warp online
-// softmax + PV, merged across warps in shared memory (compressed branch
-// output). Pass 2: scores recomputed with the merged per-head max /
-// normaliser, reduced over heads; warp 0 selects the top-n.
+// One kernel, compressed_select_tc_kernel (tcgen05 / TMEM, 8 query rows per
+// CTA, 16 warps), serves every geometry: the per-row key and block scores
+// live in shared memory up to 2048 columns, and in a per-device global
+// scratch beyond that (the BASELINE MLP compression at H = 128K has ~8K
+// keys).
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <mutex>
 
 #include "cxs_common.cuh"
 #include "tile_attn.cuh"
@@ -28,9 +27,7 @@ using cxs_host::set_error;
 
 namespace {
 
-constexpr int kWarps = 4;
 constexpr int kTileKeys = 64;
-constexpr int kTileBytes = kTileKeys * 128;
 
 // Error sink for the kernels' bounded copy waits (their copies read device
 // memory only, so a timeout indicates a broken launch, not a slow link).
@@ -40,6 +37,35 @@ constexpr int kMaxDevices = 64;
 constexpr int kMaxSmem = 227 * 1024;
 bool g_select_ready[kMaxDevices] = {false};
 int* g_select_error_address[kMaxDevices] = {nullptr};
+
+// Per-device global scratch for the score rows of long key lists, grown on
+// demand. Growing allocates, which stream capture forbids: a first call of
+// at least the same size must come before any capture.
+float* g_score_scratch[kMaxDevices] = {nullptr};
+size_t g_score_scratch_bytes[kMaxDevices] = {0};
+std::mutex g_score_scratch_mutex;
+
+int score_scratch(int device, size_t bytes, cudaStream_t stream, float** out) {
+  std::lock_guard<std::mutex> lock(g_score_scratch_mutex);
+  if (g_score_scratch_bytes[device] < bytes) {
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    CXS_CUDA(cudaStreamIsCapturing(stream, &capture));
+    if (capture != cudaStreamCaptureStatusNone)
+      return set_error(CXS_ERR_CAPACITY,
+                       "compressed select needs %zu bytes of score scratch on device %d; make "
+                       "one call of this size before capturing a graph", bytes, device);
+    if (g_score_scratch[device]) {
+      CXS_CUDA(cudaDeviceSynchronize());  // a launch may still use the old scratch
+      CXS_CUDA(cudaFree(g_score_scratch[device]));
+      g_score_scratch[device] = nullptr;
+      g_score_scratch_bytes[device] = 0;
+    }
+    CXS_CUDA(cudaMalloc((void**)&g_score_scratch[device], bytes));
+    g_score_scratch_bytes[device] = bytes;
+  }
+  *out = g_score_scratch[device];
+  return CXS_OK;
+}
 
 struct SelectArgs {
   int Q, H, C, BS, count, width, score_len;
@@ -55,6 +81,7 @@ struct SelectArgs {
   __nv_bfloat16* out;
   int32_t* blocks;
   float* scores;
+  float* row_scores;  // global per-row score rows (long key lists), or null: shared memory
   int* error;
 };
 
@@ -74,7 +101,6 @@ struct RowGeo {
   int s = 0;        // the row's candidate segment (0 outside segments)
   int current = -1, previous = -1, first = -1;  // block ids of the true current,
                                                 // previous and first blocks
-  __device__ __forceinline__ bool key_visible(int c) const { return c < nc && !keys.hides(c); }
   // Bit i: key slot col0 + i visible (one mask per 32 columns, so that the
   // unrolled column loops test a bit instead of three bounds).
   __device__ __forceinline__ uint32_t visible_bits(int col0) const {
@@ -174,192 +200,6 @@ __device__ __forceinline__ int forced_picks(const SelectArgs& a, const RowGeo& r
   return k < a.width ? k : a.width;
 }
 
-__global__ void __launch_bounds__(kWarps * 32)
-    compressed_select_kernel(const __grid_constant__ CUtensorMap map, SelectArgs a) {
-  // One CTA per (query row, KV head); warp w owns summary tiles w, w + 4, ...
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  int score_len = a.score_len;
-  uint8_t* k_tile = smem + warp * 2 * kTileBytes;
-  uint8_t* v_tile = k_tile + kTileBytes;
-  float* scores = reinterpret_cast<float*>(smem + kWarps * 2 * kTileBytes);
-  float* merge = scores + score_len;                    // [kWarps][16 m | 16 l | 16x64 o]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + kWarps * (32 + 16 * 64));
-  uint64_t* bar = &bars[warp];
-  if (lane == 0) {
-    cxs::mbar_init(bar, 1);
-    cxs::fence_mbar_init();
-  }
-  __syncwarp();
-  uint32_t k_addr = cxs::smem_addr(k_tile), v_addr = cxs::smem_addr(v_tile);
-  uint32_t phase = 0;
-  int row = blockIdx.x;
-  int q = row / a.H, h = row % a.H;
-  int pos = a.positions[q];
-  int g = lane >> 2, c = lane & 3;
-  const RowGeo rg = row_geo(a, pos);
-  const int nc = rg.nc;
-  int tiles = (nc + kTileKeys - 1) / kTileKeys;
-  long long spin = 1ll << 31;
-  for (int i = threadIdx.x; i < score_len; i += blockDim.x) scores[i] = 0.f;
-  uint32_t qa[4][4];
-  cxs::load_query(a.query + (long long)row * cxs::kGroups * cxs::kDim, lane, qa);
-  // Pass 1: each warp runs online softmax + PV over its tiles.
-  cxs::Softmax<kTileKeys> sm;
-  sm.reset();
-  bool ok = true;
-  for (int t = warp; t < tiles && ok; t += kWarps) {
-    if (lane == 0) {
-      cxs::fence_proxy_async_shared();
-      cxs::mbar_expect_tx(bar, 2 * kTileBytes);
-      cxs::tma_load_3d(k_addr, &map, 0, h, t * kTileKeys, bar);
-      cxs::tma_load_3d(v_addr, &map, 64, h, t * kTileKeys, bar);
-    }
-    __syncwarp();
-    if (!cxs::mbar_wait_bounded(bar, phase, spin, a.error)) {
-      cxs::mbar_wait_bounded(bar, phase, spin, a.error);
-      ok = false;
-      break;
-    }
-    phase ^= 1;
-    int base = t * kTileKeys;
-    sm.step(qa, k_addr, v_addr, lane, [&](int k) { return rg.key_visible(base + k); });
-    __syncwarp();
-  }
-  // Merge the warps' (max, sum, accumulator) per head through shared memory.
-  float* mine = merge + warp * (32 + 16 * 64);
-  if (c == 0) {
-    mine[g] = sm.m[0];
-    mine[g + 8] = sm.m[1];
-    mine[16 + g] = sm.l[0];
-    mine[16 + g + 8] = sm.l[1];
-  }
-#pragma unroll
-  for (int n = 0; n < 8; ++n) {
-    int dim = n * 8 + 2 * c;
-    mine[32 + g * 64 + dim] = sm.o[n][0];
-    mine[32 + g * 64 + dim + 1] = sm.o[n][1];
-    mine[32 + (g + 8) * 64 + dim] = sm.o[n][2];
-    mine[32 + (g + 8) * 64 + dim + 1] = sm.o[n][3];
-  }
-  __syncthreads();
-  // Global per-head max / normaliser (every warp needs them for pass 2).
-  float gm[2], gl[2];
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    int head = g + r * 8;
-    float m = -INFINITY;
-    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, merge[w * (32 + 16 * 64) + head]);
-    float l = 0.f;
-    for (int w = 0; w < kWarps; ++w) {
-      float mw = merge[w * (32 + 16 * 64) + head];
-      if (mw != -INFINITY) l += merge[w * (32 + 16 * 64) + 16 + head] * expf(mw - m);
-    }
-    gm[r] = m;
-    gl[r] = l;
-  }
-  // Output: 16 heads x 64 dims spread over the CTA's 128 threads.
-  __nv_bfloat16* orow = a.out + (long long)row * cxs::kGroups * cxs::kDim;
-  for (int e = threadIdx.x; e < 16 * 64; e += blockDim.x) {
-    int head = e / 64;
-    float m = -INFINITY, l = 0.f, acc = 0.f;
-    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, merge[w * (32 + 16 * 64) + head]);
-    for (int w = 0; w < kWarps; ++w) {
-      const float* part = merge + w * (32 + 16 * 64);
-      if (part[head] == -INFINITY) continue;
-      float f = expf(part[head] - m);
-      l += part[16 + head] * f;
-      acc += part[32 + e] * f;
-    }
-    orow[e] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
-  }
-  // Pass 2: block scores = sum over heads of exp(s - M) / L with the merged M, L.
-  float inv[2] = {gl[0] > 0.f ? 1.f / gl[0] : 0.f, gl[1] > 0.f ? 1.f / gl[1] : 0.f};
-  for (int t = warp; t < tiles && ok; t += kWarps) {
-    if (lane == 0) {
-      cxs::fence_proxy_async_shared();
-      cxs::mbar_expect_tx(bar, kTileBytes);
-      cxs::tma_load_3d(k_addr, &map, 0, h, t * kTileKeys, bar);
-    }
-    __syncwarp();
-    if (!cxs::mbar_wait_bounded(bar, phase, spin, a.error)) {
-      cxs::mbar_wait_bounded(bar, phase, spin, a.error);
-      ok = false;
-      break;
-    }
-    phase ^= 1;
-    float sc[kTileKeys / 8][4];
-    cxs::score_tile<kTileKeys>(qa, k_addr, lane, sc);
-#pragma unroll
-    for (int nt = 0; nt < kTileKeys / 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        int key = t * kTileKeys + nt * 8 + 2 * c + e;
-        float p = 0.f;
-        if (rg.key_visible(key))
-          p = expf(sc[nt][e] - gm[0]) * inv[0] + expf(sc[nt][e + 2] - gm[1]) * inv[1];
-        p += __shfl_xor_sync(0xffffffffu, p, 4);
-        p += __shfl_xor_sync(0xffffffffu, p, 8);
-        p += __shfl_xor_sync(0xffffffffu, p, 16);
-        if (g == 0 && key < a.C) scores[key] = p;
-      }
-    }
-    __syncwarp();
-  }
-  __syncthreads();
-  // Block scores: the key scores themselves in the reference geometry, else
-  // aggregated into the region after the merge buffers.
-  float* bsc = scores;
-  if (!a.identity) {
-    bsc = reinterpret_cast<float*>(bars + kWarps);
-    if (warp == 0) aggregate_blocks(a, rg, scores, bsc, lane);
-    __syncthreads();
-  }
-  const int columns = a.identity ? a.C : a.nb;
-  if (a.scores) {
-    float* srow = a.scores + (long long)row * columns;
-    for (int i = threadIdx.x; i < columns; i += blockDim.x) srow[i] = bsc[i];
-  }
-  __syncthreads();
-  if (warp != 0) return;
-  // Top-n: current block first (then, forced, the previous and first
-  // blocks), then (score desc, block asc) among earlier blocks.
-  int32_t* brow = a.blocks + (long long)row * a.width;
-  const int current = rg.current;
-  const int limit = min(current, a.identity ? score_len : a.nb);  // candidates: before current
-  if (current < 0) {
-    for (int k = lane; k < a.width; k += 32) brow[k] = -1;
-    return;
-  }
-  for (int k = forced_picks(a, rg, brow, bsc, lane); k < a.width; ++k) {
-    float best = -1.f;
-    int best_idx = 0x7fffffff;
-    for (int i = lane; i < limit; i += 32) {
-      if (rg.blocks.hides(i)) continue;
-      float v = bsc[i];
-      if (v > best || (v == best && i < best_idx)) {
-        best = v;
-        best_idx = i;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      float ov = __shfl_xor_sync(0xffffffffu, best, o);
-      int oi = __shfl_xor_sync(0xffffffffu, best_idx, o);
-      if (ov > best || (ov == best && oi < best_idx)) {
-        best = ov;
-        best_idx = oi;
-      }
-    }
-    if (lane == 0) {
-      brow[k] = best_idx < limit && best >= 0.f ? best_idx : -1;
-      if (best_idx < limit) bsc[best_idx] = -2.f;  // taken
-    }
-    __syncwarp();
-  }
-}
-
 // ------------------------------------------------- tcgen05 / TMEM variant ---
 // One CTA of 16 warps per (8 query rows, KV head h). The 8 rows x 16 GQA
 // heads form the M = 128 rows of the A operand: TMEM lane m (warps m / 32,
@@ -418,9 +258,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* p_tile = v_base + kres * kTcChunkBytes;
   float* red_max = reinterpret_cast<float*>(p_tile + kTcPBytes);  // [4][128]
   float* red_sum = red_max + 4 * 128;                               // [4][128]
-  float* scores = red_sum + 4 * 128;                                // [kTcRows][score_len]
-  float* bscores = scores + kTcRows * score_len;                    // [kTcRows][nb_len]
-  uint64_t* tma_bar = reinterpret_cast<uint64_t*>(bscores + kTcRows * a.nb_len);
+  // Per-row key scores [kTcRows][score_len] and block scores
+  // [kTcRows][nb_len]: in shared memory, or, for long key lists, in this
+  // CTA's rows of the global score scratch (L2-resident; every access is
+  // ordered by the same CTA barriers).
+  float* const rows_smem = red_sum + 4 * 128;
+  const long long row_floats = (long long)kTcRows * (score_len + a.nb_len);
+  float* scores = a.row_scores ? a.row_scores + (long long)blockIdx.x * row_floats : rows_smem;
+  float* bscores = scores + kTcRows * score_len;
+  uint64_t* tma_bar =
+      reinterpret_cast<uint64_t*>(a.row_scores ? rows_smem : rows_smem + row_floats);
   uint64_t* mma_bar = tma_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
 
@@ -871,10 +718,8 @@ extern "C" int cxs_compressed_select_nsa(const cxs_select_geometry* geometry, co
     return set_error(CXS_ERR_UNSUPPORTED, "device index %d beyond %d", device, kMaxDevices);
   if (!g_select_ready[device]) {
     // Once per device: the error sink's device address and the shared-memory
-    // opt-in for both kernels (up to the per-block maximum).
+    // opt-in (up to the per-block maximum).
     CXS_CUDA(cudaGetSymbolAddress((void**)&g_select_error_address[device], g_select_error));
-    CXS_CUDA(cudaFuncSetAttribute(compressed_select_kernel,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
     CXS_CUDA(cudaFuncSetAttribute(compressed_select_tc_kernel,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
     g_select_ready[device] = true;
@@ -885,23 +730,23 @@ extern "C" int cxs_compressed_select_nsa(const cxs_select_geometry* geometry, co
     return set_error(CXS_ERR_CAPACITY, "too many blocks");
   int score_len = (int)((longest + 3) & ~3ll);
   a.score_len = score_len;
+  a.row_scores = nullptr;
+  const int grid = ((queries + kTcRows - 1) / kTcRows) * heads;
   int chunks = (summaries + kTcChunk - 1) / kTcChunk;
   int kres = chunks <= kTcMaxResident ? (chunks > 0 ? chunks : 1) : 1;
   if (kres > 1 && tc_smem_bytes(kres, score_len, a.nb_len) > (size_t)kMaxSmem) kres = 1;
   size_t tc_smem = tc_smem_bytes(kres, score_len, a.nb_len);
-  if (score_len <= kTcMaxScores && tc_smem <= (size_t)kMaxSmem) {
-    int grid = ((queries + kTcRows - 1) / kTcRows) * heads;
-    compressed_select_tc_kernel<<<grid, kTcThreads, tc_smem, (cudaStream_t)stream>>>(map, a, kres);
-    CXS_LAUNCH_CHECK("compressed_select_tc_kernel");
-    return CXS_OK;
+  if (score_len > kTcMaxScores || tc_smem > (size_t)kMaxSmem) {
+    // Long key lists: the score rows go to the device's global scratch.
+    const size_t need = (size_t)grid * kTcRows * (score_len + a.nb_len) * sizeof(float);
+    int status = score_scratch(device, need, (cudaStream_t)stream, &a.row_scores);
+    if (status != CXS_OK) return status;
+    kres = chunks <= kTcMaxResident && tc_smem_bytes(chunks, 0, 0) <= (size_t)kMaxSmem
+               ? (chunks > 0 ? chunks : 1) : 1;
+    tc_smem = tc_smem_bytes(kres, 0, 0);
   }
-  size_t smem = 1024 + (size_t)kWarps * 2 * kTileBytes + (size_t)score_len * 4 +
-                (size_t)kWarps * (32 + 16 * 64) * 4 + kWarps * 8 + (size_t)a.nb_len * 4;
-  if (smem > (size_t)kMaxSmem) return set_error(CXS_ERR_CAPACITY, "too many summaries for one warp");
-  int rows = queries * heads;
-  compressed_select_kernel<<<rows, kWarps * 32, smem, (cudaStream_t)stream>>>(
-      map, a);
-  CXS_LAUNCH_CHECK("compressed_select_kernel");
+  compressed_select_tc_kernel<<<grid, kTcThreads, tc_smem, (cudaStream_t)stream>>>(map, a, kres);
+  CXS_LAUNCH_CHECK("compressed_select_tc_kernel");
   return CXS_OK;
 }
 

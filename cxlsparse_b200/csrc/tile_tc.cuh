@@ -26,6 +26,7 @@ namespace cxs {
 namespace tc {
 
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLazyRescale = 8.f / kLog2e;  // natural-log units: a factor of 2^8
 constexpr int kEngines = 4;                    // attention warps per CTA (one per TMEM subpartition)
 constexpr int kTileRows = 64;                  // tokens per key tile (N of S, K of P.V)
 constexpr int kTileBytes = kTileRows * 128;    // one K or V tile
@@ -224,8 +225,9 @@ __device__ __forceinline__ float ex2(float x) {
 // 32 * half + 31) of its head's row; tokens outside [lo, hi] are masked. The
 // lane and its partner (lane ^ 16) agree on the tile max and sum. Writes the
 // lane's 32 bf16 probabilities into P row `m` and returns the factor the
-// running output must be scaled by. p = 2^(s log2e - m log2e), the exp2 form
-// of the reference's exp(s - m).
+// running output must be scaled by (1 unless the reference maximum moved).
+// p = 2^(s log2e - m log2e), the exp2 form of the reference's exp(s - m),
+// with m the running reference maximum.
 __device__ __forceinline__ float softmax_half(uint8_t* p_tile, uint32_t s_addr, int lo, int hi,
                                               float& m_run, float& l_run, int m, int half) {
   float sv[32];
@@ -268,8 +270,13 @@ __device__ __forceinline__ float softmax_half(uint8_t* p_tile, uint32_t s_addr, 
   for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], sv[i]);
   float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
   mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
-  const float updated = fmaxf(m_run, mt);
-  const float factor = m_run == -INFINITY ? 0.f : ex2((m_run - updated) * kLog2e);
+  // The reference maximum moves only when a score exceeds it by more than
+  // 2^8 in probability (so p <= 256 in between, exact in bf16's exponent
+  // range): most tiles then need no rescale of O in TMEM.
+  const float updated = mt > m_run + kLazyRescale ? mt : m_run;
+  const float factor = m_run == -INFINITY ? 0.f
+                       : updated == m_run ? 1.f
+                                          : ex2((m_run - updated) * kLog2e);
   m_run = updated;
   // A fully masked row so far (updated = -inf) gets p = 0 everywhere.
   const float offset = updated == -INFINITY ? 0.f : updated * kLog2e;

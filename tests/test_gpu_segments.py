@@ -33,7 +33,7 @@ def _true_columns(layout, candidate, summaries_true):
     (1000, 64, 3, 64),    # tail 40: two blocks per segment, tcgen05 kernel
     (4096, 128, 4, 64),   # aligned history
     (300, 40, 3, 16),     # BS 16
-    (2100 * 16, 48, 2, 16),  # more than 2048 blocks: the mma.sync kernel
+    (2100 * 16, 48, 2, 16),  # more than 2048 blocks: score rows in the global scratch
 ])
 def test_select_over_segments_matches_each_candidate(cuda, history, extend, candidates, bs):
     layout = SegmentLayout(history, extend, candidates, bs)

@@ -35,7 +35,7 @@ def _run(query, keys, positions, total, bs, forced, segments=None, window=L, str
     (1000, 64, True),      # tcgen05 kernel
     (16384, 256, True),    # H16K/E256 headline shape (1039 keys)
     (16384, 256, False),
-    (40000, 32, True),     # more than 2048 keys: the mma.sync kernel
+    (40000, 32, True),     # more than 2048 keys: score rows in the global scratch
 ])
 def test_nsa_geometry_matches_oracle(cuda, history, extend, forced):
     bs = 64
