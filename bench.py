@@ -796,10 +796,15 @@ def run_gr(args):
         points = [(args.history, args.extend)]
     histories = sorted({h for h, _ in points})
     cfg = nsa_config(args)
+    # Every captured (user, suffix) graph holds one transport workspace per
+    # layer: room for all of them, so no eviction is ever needed.
     model = NSAExtendModel(cfg, device=device, seed=0, max_users=len(histories),
                            max_history=max(histories) + max(e for _, e in points),
-                           workspaces=cfg.layers + 4)
-    worker = Worker(ExtendRunner(model, graphs=len(points) + 1), queue_capacity=1)
+                           workspaces=len(points) * cfg.layers + 4,
+                           workspace_bytes=32 * 1024**3)
+    # Closed loop, batch 1: the next visit is admitted once the previous one
+    # has finished, so a request's end-to-end time is its own latency.
+    worker = Worker(ExtendRunner(model, graphs=len(points) + 1), queue_capacity=0)
     out = []
     try:
         for index, (history, extend) in enumerate(points):
@@ -809,7 +814,7 @@ def run_gr(args):
             for r in requests:
                 r["user_id"] = user
                 r["request_id"] = f"{user}-{extend}-{r['request_id']}"
-            summary = Scheduler(worker).run_sequence(requests, timeout=600)
+            summary = Scheduler(worker, poll_s=0.0002).run_sequence(requests, timeout=600)
             if not summary["passed"]:
                 raise RuntimeError(f"GR replay failed: {summary['state']} "
                                    f"{summary['worker']['error']}")
@@ -832,7 +837,8 @@ def run_gr(args):
         worker.close()
     print(json.dumps({
         "workload": "GR request replay through the worker / scheduler serving shell "
-                    "(steady visits, batch 1, frequency hot set of 256 tokens)",
+                    "(steady visits, batch 1, closed loop: one visit in flight, frequency "
+                    "hot set of 256 tokens)",
         "metric": "E2E p50 ms per request (lower is better)", "higher_is_better": False,
         "compression": compression_config(args), "points": out,
         "e2e_boundary": "in-process: scheduler admission to completion; the reference's "

@@ -193,6 +193,13 @@ class GRSelectedTransport:
             victim = next((k for k, v in self.workspaces.items() if not v.get("pinned")), None)
             if victim is None:
                 raise GRWorkspaceLimit("every cached workspace is bound into a captured graph")
+            if torch.cuda.is_current_stream_capturing():
+                # Evicting waits for the last launch, which a capture forbids
+                # (the wait would invalidate the caller's graph).
+                raise GRWorkspaceLimit(
+                    "workspace cache full while a graph is being captured: give the transport "
+                    "room for every workspace the captured graphs hold (capacity / "
+                    "workspace_bytes)")
             if self.submitted:
                 self.last_done.synchronize()
             old = self.workspaces.pop(victim)
