@@ -12,7 +12,6 @@
 #include <mutex>
 
 #include "cxs_common.cuh"
-#include "tile_attn.cuh"
 #include "tile_tc.cuh"
 
 using cxs::kTokenBytes;

@@ -105,6 +105,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tensor_map, i
       : "memory");
 }
 
+// 3-D tensor TMA load (no multicast): coordinates {x, y, z}.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tensor_map, int x, int y,
+                                            int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(tensor_map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tensor_map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tensor_map) : "memory");
 }
@@ -138,6 +148,15 @@ __device__ __forceinline__ bool wait_ready_bounded(const int* flag, long long li
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float2 unpack_bf16(uint32_t v) {
+  __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
+  return __bfloat1622float2(h);
+}
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
 }
 
 __device__ __forceinline__ int warp_sum(int v) {
