@@ -8,6 +8,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <climits>
 #include <mutex>
 
@@ -21,9 +22,20 @@ using cxs_host::set_error;
 
 namespace {
 
-constexpr int kAttnWarps = cxs::tc::kEngines;     // one per TMEM subpartition
+constexpr int kAttnWarps = cxs::tc::kEngines;     // engines (warp pairs) per CTA
 constexpr int kTmemAlloc = kAttnWarps * cxs::tc::kTmemCols;  // 512: all of TMEM
-constexpr int kThreads = 32 * (1 + kAttnWarps);
+constexpr int kIoWarp = 2 * kAttnWarps;           // warps 0-3 softmax, 4-7 engine, 8 IO
+constexpr int kThreads = 32 * (kIoWarp + 1);
+// Host-link requests kept in flight by the IO warps of a launch. Every IO
+// warp has one block copy outstanding, and the link shares its bandwidth
+// among them, so a block arrives after about (IO warps x block bytes) /
+// bandwidth. Far above the link's bandwidth-delay product (about 110 KB at
+// 55 GB/s and 2 us), more warps only delay the first blocks of the
+// consumption order, which the attention warps wait on. Measured at
+// H=16384 / E=256 / BS=64 on one B200: 37 IO warps (this budget) take the
+// 16-layer step from 4.80 to 4.68 ms against one IO warp per SM; 17 are
+// slower again (mixed-source gathers need the warps).
+constexpr int kIoInflightBytes = 512 * 1024;
 
 struct AttendArgs {
   int Q, H, W, BS, P, window, window_len, gate;
@@ -50,6 +62,7 @@ struct AttendArgs {
   __nv_bfloat16* out;
   __nv_bfloat16* out_peer;  // optional second copy of every output row (a peer GPU's buffer)
   int out_heads, out_head0;  // output row of (q, h): q * out_heads + out_head0 + h
+  int io_stride;             // CTAs whose blockIdx.x is a multiple of this run the IO loop
 };
 
 // Warp gather of one BS-token block: token t comes from address[t] (HBM or
@@ -117,293 +130,371 @@ __global__ void prepare_kernel(int P, int BS, const int64_t* __restrict__ addres
   }
 }
 
-// ------------------------------------------------------- attention warps ---
-// One attention warp (engine `w` of its CTA): query rows with index
-// w * gridDim.x + blockIdx.x + k * consumers. Per row it runs the
-// sliding-window tiles, then the row's selected occurrences in list order
-// (duplicates attended again, as the reference does), on the tcgen05 engine
-// of tile_tc.cuh, and writes the (gate-mixed) output.
-//
-// Tile t uses K buffer t % 2 and V buffer t % 2; one mbarrier commit C_t per
-// tile covers P.V of tile t-1 and S of tile t. Lane 0 keeps the copies ahead:
-// K of tile j may start once S of tile j-2 is done, V of tile j once P.V of
-// tile j-2 is, and a selected block only after its ready flag is set.
-//   A  every lane waits C_t; lane 0 starts what is free and known ready
-//   B  softmax of S(t) -> P, running max/denominator, O rescale in TMEM
-//   C  lane 0 makes sure K of tile t+1 is under way (acquire-waiting on its
-//      ready flag); the warp agrees on every wait's status, and a failure
-//      ends the launch for this warp once its copies have landed
-//   D  lane 0 issues O += P.V(t) and S(t+1) as their copies land, commits
+// ------------------------------------------------------- attention pairs ---
+// One engine (a warp pair, tile_tc.cuh) per query row at a time: rows
+// e * gridDim.x + blockIdx.x + k * consumers for engine e of the CTA. Per row
+// the sliding-window tiles come first, then the row's selected occurrences
+// in list order (duplicates attended again, as the reference does); the
+// softmax warp writes the (gate-mixed) output.
+
+// Tiles of one query row, computed alike by both warps of an engine.
+struct RowTiles {
+  int h, pos, count, n_hist, n_win, total;
+  int w_lo, w_hi, o_lo, o_hi;
+  // First and last position of window tile j.
+  __device__ __forceinline__ int win_first(int j) const {
+    return j < n_hist ? w_lo + j * cxs::tc::kTileRows : o_lo + (j - n_hist) * cxs::tc::kTileRows;
+  }
+  __device__ __forceinline__ int win_last(int j) const { return j < n_hist ? w_hi : o_hi; }
+};
+
+// Window: positions [w_lo, w_hi], then [o_lo, o_hi] (positions and window
+// bounds fit int32: host-checked), each in tiles of 64 from its start. With
+// candidate segments, a row of segment s sees the history below seg_start,
+// then its own segment, which starts at seg_start + s * seg_tokens (true
+// position = seg_start + offset into the segment); every segment row splits
+// its window there, whatever s, so that a candidate's tiles (and roundings)
+// do not depend on its segment index. Without segments the window is one
+// contiguous range.
+__device__ __forceinline__ RowTiles row_tiles(const AttendArgs& a, int row) {
+  RowTiles r;
+  r.h = row % a.H;
+  r.pos = a.row_positions[row];
+  r.w_lo = 1, r.w_hi = 0, r.o_lo = 1, r.o_hi = 0;
+  if (a.window > 0 && r.pos >= 0) {
+    const int pos = r.pos;
+    const int w_first = (int)a.window_start, w_last = w_first + a.window_len - 1;
+    int own = -1, real = pos;
+    if (a.seg_tokens > 0 && pos >= a.seg_start) {
+      own = a.seg_start + (pos - a.seg_start) / a.seg_tokens * a.seg_tokens;
+      real = a.seg_start + (pos - own);
+    }
+    r.w_lo = max(max(real - a.window + 1, 0), w_first);
+    if (own < 0) {
+      r.w_hi = min(pos, w_last);
+    } else {
+      r.w_hi = min(a.seg_start - 1, w_last);
+      r.o_lo = max(own + max(real - a.window + 1 - a.seg_start, 0), w_first);
+      r.o_hi = min(pos, w_last);
+    }
+  }
+  constexpr int kRows = cxs::tc::kTileRows;
+  r.n_hist = r.w_lo <= r.w_hi ? (r.w_hi - r.w_lo) / kRows + 1 : 0;
+  r.n_win = r.n_hist + (r.o_lo <= r.o_hi ? (r.o_hi - r.o_lo) / kRows + 1 : 0);
+  r.count = r.pos >= 0 ? min(a.all_counts[row], a.W) : 0;
+  r.total = r.n_win + r.count;
+  return r;
+}
+
+// Engine warp: copies and MMAs of its engine's rows, issued by lane 0.
+//   K of tile j goes to K buffer (j mod 3) once S of tile j - 3 has been read
+//   (the softmax warp's "S read" arrival), at most two tiles ahead; a
+//   selected block's copy needs its ready flag (skipped for blocks resident
+//   before the launch, kind 0), polled with relaxed loads issued one tile
+//   early and made an acquire by a fence once seen set.
+//   V of tile j goes to V buffer (j mod 2) once P.V of tile j - 2 is done.
+//   Per tile t: wait "S(t - 1) read", issue S(t) (commit: sbar), then wait
+//   "P(t - 1) written" and issue O (+)= P.V(t - 1) (commit: obar), then
+//   start V(t) (P.V(t - 2) was issued a tile earlier, so rarely waited for).
+// Every wait is bounded; a timeout or the partner's abort ends the launch
+// for the engine after its copies and MMAs in flight have drained.
 template <int BS>
-__device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
-                                               const CUtensorMap& win_map, const AttendArgs& a,
-                                               uint8_t* q_tile, uint8_t* p_tile, uint8_t* wbase,
-                                               int w, uint32_t tmem) {
+__device__ __forceinline__ void engine_warp(const CUtensorMap& kv_map, const CUtensorMap& win_map,
+                                            const AttendArgs& a, const uint8_t* q_tile,
+                                            const uint8_t* p_tile, const cxs::tc::PairSmem ps,
+                                            int e, uint32_t tmem) {
   namespace tc = cxs::tc;
-  const tc::WarpSmem ws{wbase};
-  const int lane = threadIdx.x % 32, half = lane >> 4;
-  const bool leader = lane == 0;
-  const int m = 32 * w + lane;  // this lane's row of the Q / P tiles and of S / O
-  const uint32_t lane_off = (uint32_t)(32 * w) << 16;
-  const uint32_t s_col = tmem, o_col = tmem + 64;  // MMA destinations
-  const uint32_t s_addr = s_col + lane_off, o_addr = o_col + lane_off;
+  const int lane = threadIdx.x % 32;
+  const uint32_t s_col = tmem, o_col = tmem + 64;
   const uint32_t id_s = tc::idesc_bf16(128, 64, 0, 0), id_o = tc::idesc_bf16(128, 64, 0, 1);
   const uint32_t q_addr = cxs::smem_addr(q_tile), p_addr = cxs::smem_addr(p_tile);
-  uint32_t k_phase = 0, v_phase = 0, mma_phase = 0;  // bit b: phase of buffer b
-  const int rows = a.Q * a.H;
-  if (leader) {
+  volatile int* abort = ps.abort_flag();
+  const long long spin = a.spin_limit;
+  if (lane == 0) {
     cxs::tma_prefetch_desc(&kv_map);
     if (a.window) cxs::tma_prefetch_desc(&win_map);
   }
-  auto mma_scores = [&](int b) {  // S = Q . K(b)^T
-    const uint32_t ka = cxs::smem_addr(ws.k(b));
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      tc::mma(s_col, tc::desc_sw128(q_addr + 32 * k, 16, 1024),
-              tc::desc_sw128(ka + 32 * k, 16, 1024), id_s, k);
-  };
-  auto mma_output = [&](int b, bool accumulate) {  // O (+)= P . V(b)
-    const uint32_t va = cxs::smem_addr(ws.v(b));
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      tc::mma(o_col, tc::desc_sw128(p_addr + 32 * k, 16, 1024),
-              tc::desc_sw128(va + 2048 * k, 16, 1024), id_o, accumulate || k > 0);
-  };
-  for (int row = w * gridDim.x + blockIdx.x; row < rows; row += a.consumers) {
-    const int h = row % a.H;
-    const int pos = a.row_positions[row];
-    // Window: positions [w_lo, w_hi], then [o_lo, o_hi] (positions and window
-    // bounds fit int32: host-checked), each in tiles of 64 from its start.
-    // With candidate segments, a row of segment s sees the history below
-    // seg_start, then its own segment, which starts at seg_start + s *
-    // seg_tokens (true position = seg_start + offset into the segment); every
-    // segment row splits its window there, whatever s, so that a candidate's
-    // tiles (and roundings) do not depend on its segment index. Without
-    // segments the window is one contiguous range.
-    int w_lo = 1, w_hi = 0, o_lo = 1, o_hi = 0;
-    if (a.window > 0 && pos >= 0) {
-      const int w_first = (int)a.window_start, w_last = w_first + a.window_len - 1;
-      int own = -1, real = pos;
-      if (a.seg_tokens > 0 && pos >= a.seg_start) {
-        own = a.seg_start + (pos - a.seg_start) / a.seg_tokens * a.seg_tokens;
-        real = a.seg_start + (pos - own);
+  // Running counts over the engine's rows: K / V copies started and landed
+  // (buffer = count mod 3 / mod 2, phase bit per buffer), P.V issued and
+  // seen complete, barrier phases of the softmax warp's arrivals.
+  int k_started = 0, k_landed = 0, v_started = 0, v_landed = 0, pv_issued = 0, pv_seen = 0;
+  uint32_t k_phase = 0, v_phase = 0, sfree_phase = 0, pfull_phase = 0;
+  bool failed = false, first_row = true;
+  const int rows = a.Q * a.H;
+  for (int row = e * gridDim.x + blockIdx.x; row < rows && !failed; row += a.consumers) {
+    const RowTiles rt = row_tiles(a, row);
+    {  // stage the row's selected blocks and their source kinds
+      int block = -1, kind = 0;
+      if (lane < rt.count) {
+        block = a.all_ids[(long long)row * a.W + lane];
+        if (block >= 0 && block < a.P) kind = a.kinds[block];
       }
-      w_lo = max(max(real - a.window + 1, 0), w_first);
-      if (own < 0) {
-        w_hi = min(pos, w_last);
-      } else {
-        w_hi = min(a.seg_start - 1, w_last);
-        o_lo = max(own + max(real - a.window + 1 - a.seg_start, 0), w_first);
-        o_hi = min(pos, w_last);
+      ps.blocks()[lane] = block;
+      ps.kinds()[lane] = kind;
+    }
+    __syncwarp();
+    if (lane == 0 && rt.total > 0) {
+      const int total = rt.total, n_win = rt.n_win, h = rt.h;
+      const int k0 = k_started, v0 = v_started;  // this row's tile j: K copy k0 + j, V copy v0 + j
+      int probe_tile = -1, probe_value = 0;
+      auto block_of = [&](int j) { return ps.blocks()[j - n_win]; };
+      auto copy = [&](int j, bool value) {
+        const int b = value ? (v0 + j) % tc::PairSmem::kVBufs : (k0 + j) % tc::PairSmem::kKBufs;
+        uint64_t* bar = value ? ps.vbar(b) : ps.kbar(b);
+        uint8_t* dst = value ? ps.v(b) : ps.k(b);
+        if (j < n_win) {
+          cxs::mbar_expect_tx(bar, tc::kTileBytes);
+          tc::window_load(dst, &win_map, value ? 64 : 0, h, rt.win_first(j) - (int)a.window_start,
+                          bar);
+        } else {
+          cxs::mbar_expect_tx(bar, BS * 128);
+          cxs::tma_load_2d(dst, &kv_map, value ? 64 : 0, block_of(j) * BS, bar);
+        }
+      };
+      // Start K copies of tiles up to `upto`; tile `need` (and any before it)
+      // must start now, waiting (bounded) for its ready flag.
+      auto start_k = [&](int upto, int need) -> bool {
+        while (k_started - k0 <= upto && k_started - k0 < total) {
+          const int j = k_started - k0;
+          if (j >= n_win) {
+            const int block = block_of(j);
+            if (block < 0 || block >= a.P) {
+              atomicOr(a.error, cxs::kErrBadBlock);
+              return false;
+            }
+            if (ps.kinds()[j - n_win] != 0) {
+              if (probe_tile == j && probe_value) {
+                cxs::fence_acq_rel_gpu();
+              } else if (j <= need) {
+                if (!cxs::wait_ready_bounded(&a.ready[block], spin, a.error)) return false;
+              } else {
+                break;  // not known ready: retry at the next tile
+              }
+              cxs::fence_proxy_async_global();
+            }
+          }
+          copy(j, false);
+          ++k_started;
+        }
+        return true;
+      };
+      // Start V copies of tiles up to `upto` whose K copy has started (its
+      // block is ready); V buffer reuse waits for the P.V two copies back.
+      auto start_v = [&](int upto) -> bool {
+        while (v_started - v0 <= upto && v_started < k_started) {
+          const int need_done = v_started - 1;  // P.V of V copy v_started - 2 complete
+          while (pv_seen < need_done) {
+            if (!tc::pair_wait(ps.obar(), pv_seen & 1, abort, spin, a.error, cxs::kErrCopyTimeout))
+              return false;
+            ++pv_seen;
+          }
+          copy(v_started - v0, true);
+          ++v_started;
+        }
+        return true;
+      };
+      auto land = [&](bool value) -> bool {
+        int& done = value ? v_landed : k_landed;
+        uint32_t& phase = value ? v_phase : k_phase;
+        const int b = value ? done % tc::PairSmem::kVBufs : done % tc::PairSmem::kKBufs;
+        const bool ok = tc::pair_wait(value ? ps.vbar(b) : ps.kbar(b), (phase >> b) & 1u, abort,
+                                      spin, a.error, cxs::kErrCopyTimeout);
+        phase ^= 1u << b;
+        ++done;
+        return ok;
+      };
+      auto softmax_arrival = [&](uint64_t* bar, uint32_t& phase) -> bool {
+        const bool ok = tc::pair_wait(bar, phase, abort, spin, a.error, cxs::kErrReadyTimeout);
+        phase ^= 1u;
+        return ok;
+      };
+      // O (+)= P . V(j). Every earlier P.V is seen complete first (one was
+      // issued a tile ago), so the engine's count of obar phases never lags
+      // two behind, which a parity wait could not tell apart.
+      auto issue_pv = [&](int j) -> bool {
+        while (pv_seen < pv_issued) {
+          if (!tc::pair_wait(ps.obar(), pv_seen & 1, abort, spin, a.error, cxs::kErrCopyTimeout))
+            return false;
+          ++pv_seen;
+        }
+        const uint32_t va = cxs::smem_addr(ps.v((v0 + j) % tc::PairSmem::kVBufs));
+        const bool accumulate = !(j == 0 || j == n_win);
+        tc::fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc::mma(o_col, tc::desc_sw128(p_addr + 32 * k, 16, 1024),
+                  tc::desc_sw128(va + 2048 * k, 16, 1024), id_o, accumulate || k > 0);
+        tc::commit(ps.obar());
+        ++pv_issued;
+        return true;
+      };
+      // Previous rows are complete (the softmax warp has written this row's
+      // Q after its last epilogue), so every buffer is free: P.V seen.
+      bool ok = true;
+      if (!first_row) ok = softmax_arrival(ps.sfree(), sfree_phase);  // this row's Q written
+      pv_seen = pv_issued;
+      ok = ok && start_k(2, 0) && start_v(0);
+      if (ok && first_row) ok = softmax_arrival(ps.sfree(), sfree_phase);
+      first_row = false;
+      for (int t = 0; t < total && ok; ++t) {
+        if (t > 0) ok = softmax_arrival(ps.sfree(), sfree_phase);  // S(t - 1) read
+        ok = ok && start_k(t + 2, t) && land(false);  // K(t)
+        if (!ok) break;
+        {  // S = Q . K(t)^T
+          const uint32_t ka = cxs::smem_addr(ps.k((k0 + t) % tc::PairSmem::kKBufs));
+          tc::fence_after();
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc::mma(s_col, tc::desc_sw128(q_addr + 32 * k, 16, 1024),
+                    tc::desc_sw128(ka + 32 * k, 16, 1024), id_s, k);
+          tc::commit(ps.sbar());
+        }
+        if (t > 0) {
+          ok = softmax_arrival(ps.pfull(), pfull_phase) && land(true)  // P(t-1), V(t-1)
+               && issue_pv(t - 1);
+        }
+        // V(t): its buffer's last P.V (tile t - 2) was issued a tile ago.
+        ok = ok && start_v(t);
+        // Poll the ready flag of the next K copy now; it is read at the next
+        // tile, after its latency has passed.
+        const int next = k_started - k0;
+        if (ok && next < total && next >= n_win && ps.kinds()[next - n_win] != 0) {
+          const int block = block_of(next);
+          if (block >= 0 && block < a.P) {
+            probe_tile = next;
+            probe_value = cxs::ld_relaxed(&a.ready[block]);
+          }
+        }
+      }
+      if (ok) {
+        ok = start_v(total - 1) && softmax_arrival(ps.pfull(), pfull_phase) && land(true) &&
+             issue_pv(total - 1);
+      }
+      if (!ok) {
+        *abort = 1;
+        failed = true;
       }
     }
-    const int n_hist = w_lo <= w_hi ? (w_hi - w_lo) / tc::kTileRows + 1 : 0;
-    const int n_win = n_hist + (o_lo <= o_hi ? (o_hi - o_lo) / tc::kTileRows + 1 : 0);
-    // First position and last position of window tile j.
-    auto win_first = [&](int j) {
-      return j < n_hist ? w_lo + j * tc::kTileRows : o_lo + (j - n_hist) * tc::kTileRows;
-    };
-    auto win_last = [&](int j) { return j < n_hist ? w_hi : o_hi; };
-    const int count = pos >= 0 ? min(a.all_counts[row], a.W) : 0;
-    const int total = n_win + count;
-    // Lane i holds selected occurrence i (block id and first position).
+    __syncwarp();
+    failed = __shfl_sync(0xffffffffu, failed, 0);
+  }
+  if (lane == 0) {
+    // Let every copy this engine started land, and every MMA it issued
+    // complete, before the CTA releases shared memory and TMEM (bounded).
+    while (k_landed < k_started) {
+      const int b = k_landed % tc::PairSmem::kKBufs;
+      tc::bounded_wait(ps.kbar(b), (k_phase >> b) & 1u, spin, a.error, cxs::kErrCopyTimeout);
+      k_phase ^= 1u << b;
+      ++k_landed;
+    }
+    while (v_landed < v_started) {
+      const int b = v_landed % tc::PairSmem::kVBufs;
+      tc::bounded_wait(ps.vbar(b), (v_phase >> b) & 1u, spin, a.error, cxs::kErrCopyTimeout);
+      v_phase ^= 1u << b;
+      ++v_landed;
+    }
+    tc::commit(ps.drain());
+    tc::bounded_wait(ps.drain(), 0, spin, a.error, cxs::kErrCopyTimeout);
+  }
+}
+
+// Softmax warp: S tiles of its engine's rows from TMEM, online softmax, P to
+// shared memory, O rescale, and the epilogue (normalisation, gate mix,
+// output rows; lane writes dims 32 * half .. 32 * half + 31 of head
+// (lane & 15)).
+template <int BS>
+__device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_tile,
+                                             uint8_t* p_tile, const cxs::tc::PairSmem ps, int e,
+                                             uint32_t tmem) {
+  namespace tc = cxs::tc;
+  const int lane = threadIdx.x % 32, half = lane >> 4;
+  const bool leader = lane == 0;
+  const int m = 32 * e + lane;  // this lane's row of the Q / P tiles and of S / O
+  const uint32_t lane_off = (uint32_t)(32 * e) << 16;
+  const uint32_t s_addr = tmem + lane_off, o_addr = tmem + 64 + lane_off;
+  volatile int* abort = ps.abort_flag();
+  const long long spin = a.spin_limit;
+  uint32_t s_phase = 0, o_phase = 0;
+  const int rows = a.Q * a.H;
+  auto agree_wait = [&](uint64_t* bar, uint32_t& phase) -> bool {
+    bool ok = tc::pair_wait(bar, phase, abort, spin, a.error, cxs::kErrCopyTimeout);
+    phase ^= 1u;
+    ok = __all_sync(0xffffffffu, ok);
+    tc::fence_after();
+    return ok;
+  };
+  for (int row = e * gridDim.x + blockIdx.x; row < rows; row += a.consumers) {
+    const RowTiles rt = row_tiles(a, row);
+    const int total = rt.total, n_win = rt.n_win, pos = rt.pos;
+    // Lane i holds selected occurrence i's first position.
     int my_block = -1, my_start = 0;
-    if (lane < count) {
+    if (lane < rt.count) {
       my_block = a.all_ids[(long long)row * a.W + lane];
       if (my_block >= 0 && my_block < a.P) my_start = a.starts[my_block];
     }
-    // Block of tile j (all lanes; -1 for window tiles and past the end).
-    auto block_of = [&](int j) {
-      const int b = __shfl_sync(0xffffffffu, my_block, (j - n_win) & 31);
-      return (j >= n_win && j < total) ? b : -1;
-    };
     tc::write_query_row(q_tile, a.query, row, m, lane);
     cxs::fence_proxy_async_shared();
     __syncwarp();
-    // Lane 0's copy schedule for this row: K / V copies of tiles [0, kn) /
-    // [0, vn) started, [0, kw) / [0, vw) landed.
-    int kn = 0, vn = 0, kw = 0, vw = 0;
-    int pf_tile = -1, pf_ready = 0;  // ready flag of tile pf_tile, acquire-loaded earlier
-    bool failed = false;
-    auto start_copy = [&](int j, int blk, bool value) {
-      const int b = j & 1;
-      uint64_t* bar = value ? ws.vbar(b) : ws.kbar(b);
-      uint8_t* dst = value ? ws.v(b) : ws.k(b);
-      if (j < n_win) {
-        cxs::mbar_expect_tx(bar, tc::kTileBytes);
-        tc::window_load(dst, &win_map, value ? 64 : 0, h, win_first(j) - (int)a.window_start,
-                        bar);
-      } else {
-        cxs::mbar_expect_tx(bar, BS * 128);
-        cxs::tma_load_2d(dst, &kv_map, value ? 64 : 0, blk * BS, bar);
-      }
-    };
-    // Start every copy that is free during step t (K of tiles <= t + 2, V of
-    // tiles <= t + 1 whose K is under way) and whose block is known ready;
-    // with `need_k`, K of tile t + 1 is started even if that means waiting
-    // for its ready flag. b1..b3: blocks of tiles t + 1 .. t + 3.
-    auto pump = [&](int t, int b1, int b2, int b3, bool need_k) {
-      while (!failed && kn < total && kn <= t + 2) {
-        const int j = kn, blk = j == t + 1 ? b1 : b2;
-        if (j >= n_win) {
-          if (j < t + 1 || blk < 0 || blk >= a.P) {
-            atomicOr(a.error, cxs::kErrBadBlock);
-            failed = true;
-            break;
-          }
-          if (!(pf_tile == j && pf_ready)) {
-            if (!(need_k && j == t + 1)) break;
-            if (!cxs::wait_ready_bounded(&a.ready[blk], a.spin_limit, a.error)) {
-              failed = true;
-              break;
-            }
-          }
-          cxs::fence_proxy_async_global();
-        }
-        start_copy(j, blk, false);
-        ++kn;
-      }
-      while (!failed && vn < kn && vn <= t + 1) {
-        const int blk = vn == t + 1 ? b1 : -1;
-        if (vn >= n_win && (blk < 0 || blk >= a.P)) {
-          atomicOr(a.error, cxs::kErrBadBlock);
-          failed = true;
-          break;
-        }
-        start_copy(vn, blk, true);
-        ++vn;
-      }
-      // Acquire-load the ready flag of the next K tile now; it is read at
-      // the next call, after its latency has passed.
-      if (!failed && kn < total && kn >= n_win && !(pf_tile == kn && pf_ready)) {
-        const int blk = kn == t + 1 ? b1 : (kn == t + 2 ? b2 : b3);
-        if (blk >= 0 && blk < a.P) {
-          pf_tile = kn;
-          pf_ready = cxs::ld_acquire(&a.ready[blk]);
-        }
-      }
-    };
-    // Lane 0: let every started copy land (bounded) before giving up the row.
-    auto drain = [&]() {
-      for (; kw < kn; ++kw) {
-        tc::bounded_wait(ws.kbar(kw & 1), (k_phase >> (kw & 1)) & 1u, a.spin_limit, a.error,
-                         cxs::kErrCopyTimeout);
-        k_phase ^= 1u << (kw & 1);
-      }
-      for (; vw < vn; ++vw) {
-        tc::bounded_wait(ws.vbar(vw & 1), (v_phase >> (vw & 1)) & 1u, a.spin_limit, a.error,
-                         cxs::kErrCopyTimeout);
-        v_phase ^= 1u << (vw & 1);
-      }
-    };
-    auto land = [&](bool value) -> bool {  // lane 0: wait for the next K or V copy
-      int& done = value ? vw : kw;
-      uint32_t& phase = value ? v_phase : k_phase;
-      const int b = done & 1;
-      const bool ok = tc::bounded_wait(value ? ws.vbar(b) : ws.kbar(b), (phase >> b) & 1u,
-                                       a.spin_limit, a.error, cxs::kErrCopyTimeout);
-      phase ^= 1u << b;
-      ++done;
-      return ok;
-    };
-    bool alive = true;
+    if (total > 0 && leader) cxs::mbar_arrive(ps.sfree());  // Q written
     float m_run = -INFINITY, l_run = 0.f;
     uint32_t win_packed[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) win_packed[i] = 0;
-    if (total > 0) {
-      {
-        const int b0 = block_of(0), b1 = block_of(1), b2 = block_of(2);
-        if (leader) {
-          pump(-1, b0, b1, b2, true);
-          if (!failed) failed = !land(false);
-          if (!failed) {
-            tc::fence_after();
-            mma_scores(0);
-          }
-          tc::commit(ws.mma_bar());
-        }
+    auto window_output = [&]() {  // normalised bf16 output of the window branch
+      float o[32];
+      tc::combine_o(o_addr, half, o);
+      const float den = l_run > 0.f ? l_run : 1.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) win_packed[i] = cxs::pack_bf16(o[2 * i] / den, o[2 * i + 1] / den);
+    };
+    bool alive = true;
+    for (int t = 0; t < total; ++t) {
+      const bool first_of_branch = t == 0 || t == n_win;
+      if (!agree_wait(ps.sbar(), s_phase)) {  // S(t)
+        alive = false;
+        break;
       }
-      for (int t = 0; t < total; ++t) {
-        const bool first_of_branch = t == 0 || t == n_win;
-        const int b1 = block_of(t + 1), b2 = block_of(t + 2), b3 = block_of(t + 3);
+      float sv[32];
+      tc::load_s(s_addr, half, sv);
+      tc::fence_before();
+      __syncwarp();
+      if (t + 1 < total && leader) cxs::mbar_arrive(ps.sfree());  // S(t) read
+      // P.V(t - 1) must be done before P(t) overwrites the P tile, O is
+      // rescaled or the window branch's O is read.
+      if (t > 0 && !agree_wait(ps.obar(), o_phase)) {
+        alive = false;
+        break;
+      }
+      if (t == n_win && n_win > 0) {  // window branch complete: keep its output, restart
+        window_output();
+        m_run = -INFINITY;
+        l_run = 0.f;
+      }
+      int lo = 0, hi = -1;
+      if (t < n_win) {
+        hi = min(rt.win_last(t) - rt.win_first(t), tc::kTileRows - 1);
+      } else {
         const int cur_block = __shfl_sync(0xffffffffu, my_block, (t - n_win) & 31);
         const int cur_start = __shfl_sync(0xffffffffu, my_start, (t - n_win) & 31);
-        // A
-        const bool waited = tc::bounded_wait(ws.mma_bar(), mma_phase, a.spin_limit, a.error,
-                                             cxs::kErrCopyTimeout);
-        mma_phase ^= 1;
-        tc::fence_after();
-        if (t == n_win && n_win > 0) {
-          // Window branch complete: keep its normalised bf16 output, restart.
-          float o[32];
-          tc::combine_o(o_addr, half, o);
-          const float den = l_run > 0.f ? l_run : 1.f;
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            win_packed[i] = cxs::pack_bf16(o[2 * i] / den, o[2 * i + 1] / den);
-          m_run = -INFINITY;
-          l_run = 0.f;
-        }
-        if (leader) pump(t, b1, b2, b3, false);
-        // B
-        int lo = 0, hi = -1;
-        if (t < n_win) {
-          hi = min(win_last(t) - win_first(t), tc::kTileRows - 1);
-        } else if (cur_block >= 0 && cur_block < a.P) {
-          hi = min(pos - cur_start, BS - 1);
-        }
-        const float m_old = m_run;
-        const float factor = tc::softmax_half(p_tile, s_addr, lo, hi, m_run, l_run, m, half);
-        if (!first_of_branch) tc::rescale_o(o_addr, factor, m_old != -INFINITY && factor != 1.f);
-        cxs::fence_proxy_async_shared();
-        tc::fence_before();
-        // C
-        if (leader) pump(t, b1, b2, b3, true);
-        const bool ok = __all_sync(0xffffffffu, waited) && !__shfl_sync(0xffffffffu, failed, 0);
-        if (!ok) {
-          if (leader) drain();
-          alive = false;
-          break;
-        }
-        // D
-        if (leader) {
-          tc::fence_after();
-          if (land(true)) {
-            mma_output(t & 1, !first_of_branch);
-            if (t + 1 < total) {
-              if (land(false))
-                mma_scores((t + 1) & 1);
-              else
-                failed = true;
-            }
-          } else {
-            failed = true;
-          }
-          tc::commit(ws.mma_bar());
-        }
-        __syncwarp();
+        if (cur_block >= 0 && cur_block < a.P) hi = min(pos - cur_start, BS - 1);
       }
-      if (alive && __shfl_sync(0xffffffffu, failed, 0)) {
-        if (leader) drain();
-        alive = false;
-      }
-      if (!alive) break;
-      // E: the last P.V is complete.
-      tc::bounded_wait(ws.mma_bar(), mma_phase, a.spin_limit, a.error, cxs::kErrCopyTimeout);
-      mma_phase ^= 1;
-      tc::fence_after();
-      if (n_win > 0 && total == n_win) {
-        float o[32];
-        tc::combine_o(o_addr, half, o);
-        const float den = l_run > 0.f ? l_run : 1.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          win_packed[i] = cxs::pack_bf16(o[2 * i] / den, o[2 * i + 1] / den);
+      const float m_old = m_run;
+      const float factor = tc::softmax_regs(sv, lo, hi, m_run, l_run, half);
+      if (!first_of_branch) tc::rescale_o(o_addr, factor, m_old != -INFINITY && factor != 1.f);
+      tc::store_p(p_tile, m, half, sv);
+      cxs::fence_proxy_async_shared();
+      tc::fence_before();
+      __syncwarp();
+      if (leader) cxs::mbar_arrive(ps.pfull());  // P(t) written
+    }
+    if (!alive) break;
+    if (total > 0) {
+      if (!agree_wait(ps.obar(), o_phase)) break;  // the last P.V
+      if (total == n_win && n_win > 0) {
+        window_output();
         l_run = 0.f;
       }
     }
-    // Epilogue: lane writes dims 32 * half .. 32 * half + 31 of head (lane & 15).
     float o[32];
     if (total > n_win) {
       tc::combine_o(o_addr, half, o);
@@ -422,9 +513,9 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
       for (int c = 0; c < 4; ++c) {
         uint32_t r[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          r[e] = cxs::pack_bf16(bf16_round(o[8 * c + 2 * e] / den),
-                                bf16_round(o[8 * c + 2 * e + 1] / den));
+        for (int q = 0; q < 4; ++q)
+          r[q] = cxs::pack_bf16(bf16_round(o[8 * c + 2 * q] / den),
+                                bf16_round(o[8 * c + 2 * q + 1] / den));
         dst[c] = make_uint4(r[0], r[1], r[2], r[3]);
         if (peer) peer[c] = make_uint4(r[0], r[1], r[2], r[3]);
       }
@@ -441,14 +532,14 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
         const uint32_t* cp = reinterpret_cast<const uint32_t*>(&cv);
         uint32_t r[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 c2 = unpack_bf16(cp[e]);
-          const float2 w2 = have_window ? unpack_bf16(win_packed[4 * c + e]) : make_float2(0.f, 0.f);
-          float x0 = bf16_round(bf16_round(o[8 * c + 2 * e] / den) * g1);
-          float x1 = bf16_round(bf16_round(o[8 * c + 2 * e + 1] / den) * g1);
+        for (int q = 0; q < 4; ++q) {
+          const float2 c2 = unpack_bf16(cp[q]);
+          const float2 w2 = have_window ? unpack_bf16(win_packed[4 * c + q]) : make_float2(0.f, 0.f);
+          float x0 = bf16_round(bf16_round(o[8 * c + 2 * q] / den) * g1);
+          float x1 = bf16_round(bf16_round(o[8 * c + 2 * q + 1] / den) * g1);
           x0 = bf16_round(x0 + c2.x * g0);
           x1 = bf16_round(x1 + c2.y * g0);
-          r[e] = cxs::pack_bf16(x0 + w2.x * g2, x1 + w2.y * g2);
+          r[q] = cxs::pack_bf16(x0 + w2.x * g2, x1 + w2.y * g2);
         }
         dst[c] = make_uint4(r[0], r[1], r[2], r[3]);
         if (peer) peer[c] = make_uint4(r[0], r[1], r[2], r[3]);
@@ -457,13 +548,15 @@ __device__ __forceinline__ void attention_warp(const CUtensorMap& kv_map,
     // Peer stores travel over NVLink: make them visible system-wide before
     // the exchange barrier that follows this launch announces them.
     if (peer) __threadfence_system();
-    __syncwarp();  // TMEM reads done before the next row's MMAs
+    tc::fence_before();  // TMEM reads done before the next row's MMAs
+    __syncwarp();
   }
 }
 
 // ------------------------------------------------------ IO + attention ---
-// Warps 0-3: attention warps (tcgen05 engine, tile_tc.cuh), one query row at
-// a time each. Warp 4: the IO warp.
+// Warps 0-3: softmax warps, warps 4-7: engine warps (warp w + 4 serves
+// softmax warp w; tcgen05 engines of tile_tc.cuh, one query row at a time
+// each). Warp 8: the IO warp.
 template <int BS>
 __global__ void __launch_bounds__(kThreads, 1)
     fetch_attend_kernel(const __grid_constant__ CUtensorMap kv_map,
@@ -475,20 +568,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* io_buf = smem;
   uint8_t* q_tile = smem + ((kBlockBytes + 1023) & ~1023);
   uint8_t* p_tile = q_tile + tc::kRowTileBytes;
-  uint8_t* warps_base = p_tile + tc::kRowTileBytes;
-  uint8_t* ctrl = warps_base + kAttnWarps * tc::WarpSmem::kBytes;
+  uint8_t* pairs_base = p_tile + tc::kRowTileBytes;
+  uint8_t* ctrl = pairs_base + kAttnWarps * tc::PairSmem::kBytes;
+  auto pair = [&](int e) { return tc::PairSmem{pairs_base + e * tc::PairSmem::kBytes}; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl);
   uint64_t* io_bar = reinterpret_cast<uint64_t*>(ctrl + 64);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
     cxs::mbar_init(io_bar, 1);
-    for (int w = 0; w < kAttnWarps; ++w) {
-      tc::WarpSmem ws{warps_base + w * tc::WarpSmem::kBytes};
-      for (int b = 0; b < 2; ++b) {
-        cxs::mbar_init(ws.kbar(b), 1);
-        cxs::mbar_init(ws.vbar(b), 1);
-      }
-      cxs::mbar_init(ws.mma_bar(), 1);
+    for (int e = 0; e < kAttnWarps; ++e) {
+      for (int i = 0; i < tc::PairSmem::kNumBars; ++i) cxs::mbar_init(pair(e).bar(i), 1);
+      *pair(e).abort_flag() = 0;
     }
     cxs::fence_mbar_init();
   }
@@ -501,13 +591,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Zero the P tile (each lane only ever writes its own half of its row) and
   // the K/V stages (rows beyond a short block, BS < 64, start at zero and
   // afterwards only hold finite key/value data).
-  if (warp < kAttnWarps) {
-    for (int i = threadIdx.x; i < tc::kRowTileBytes / 16; i += 32 * kAttnWarps)
+  if (warp < kIoWarp) {
+    constexpr int kStaged = tc::PairSmem::kKBufs + tc::PairSmem::kVBufs;
+    for (int i = threadIdx.x; i < tc::kRowTileBytes / 16; i += 32 * kIoWarp)
       reinterpret_cast<uint4*>(p_tile)[i] = make_uint4(0, 0, 0, 0);
-    for (int w = 0; w < kAttnWarps; ++w)
-      for (int i = threadIdx.x; i < 4 * tc::kTileBytes / 16; i += 32 * kAttnWarps)
-        reinterpret_cast<uint4*>(warps_base + w * tc::WarpSmem::kBytes)[i] =
-            make_uint4(0, 0, 0, 0);
+    for (int e = 0; e < kAttnWarps; ++e)
+      for (int i = threadIdx.x; i < kStaged * tc::kTileBytes / 16; i += 32 * kIoWarp)
+        reinterpret_cast<uint4*>(pair(e).base)[i] = make_uint4(0, 0, 0, 0);
   }
   cxs::fence_proxy_async_shared();
   tc::fence_before();
@@ -515,50 +605,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == kAttnWarps) {
-    // ------------------------------------------------------------ IO warp
-    uint64_t* bar = io_bar;
-    uint32_t phase = 0;
-    int missing = a.missing[0];
-    while (true) {
-      int rank = 0;
-      if (lane == 0) rank = atomicAdd(&a.control[0], 1);
-      rank = __shfl_sync(0xffffffffu, rank, 0);
-      if (rank >= missing) break;
-      int block = a.ioids[rank];
-      if (block < 0 || block >= a.P) {
-        if (lane == 0) atomicOr(a.error, cxs::kErrBadBlock);
-        continue;
-      }
-      int kind = a.kinds[block];
-      uint8_t* dst = reinterpret_cast<uint8_t*>(a.kv) + (long long)block * kBlockBytes;
-      if (kind == 1) {
-        if (lane == 0) {
-          const void* src = reinterpret_cast<const void*>(a.sources[block]);
-          cxs::fence_proxy_async_shared();
-          cxs::mbar_expect_tx(bar, kBlockBytes);
-          cxs::bulk_g2s(io_buf, src, kBlockBytes, bar);
-          if (cxs::mbar_wait_bounded(bar, phase, a.spin_limit, a.error)) {
-            cxs::bulk_s2g_and_wait(dst, io_buf, kBlockBytes);
-          } else {
-            cxs::mbar_wait_bounded(bar, phase, a.spin_limit, a.error);
-          }
-          cxs::fence_proxy_async_global();
+  if (warp == kIoWarp) {
+    if (blockIdx.x % a.io_stride == 0) {
+      // ------------------------------------------------------------ IO warp
+      uint64_t* bar = io_bar;
+      uint32_t phase = 0;
+      int missing = a.missing[0];
+      while (true) {
+        int rank = 0;
+        if (lane == 0) rank = atomicAdd(&a.control[0], 1);
+        rank = __shfl_sync(0xffffffffu, rank, 0);
+        if (rank >= missing) break;
+        int block = a.ioids[rank];
+        if (block < 0 || block >= a.P) {
+          if (lane == 0) atomicOr(a.error, cxs::kErrBadBlock);
+          continue;
         }
-        phase ^= 1;
-      } else {
-        // Mixed-tier or tail block: 16-byte vector gathers, tail zero-filled.
-        gather_block<BS>(a.address + (long long)block * BS, a.valid[block],
-                         reinterpret_cast<uint4*>(dst), lane);
-        __threadfence();
-        cxs::fence_proxy_async_global();
-        __syncwarp();
+        int kind = a.kinds[block];
+        uint8_t* dst = reinterpret_cast<uint8_t*>(a.kv) + (long long)block * kBlockBytes;
+        if (kind == 1) {
+          if (lane == 0) {
+            const void* src = reinterpret_cast<const void*>(a.sources[block]);
+            cxs::fence_proxy_async_shared();
+            cxs::mbar_expect_tx(bar, kBlockBytes);
+            cxs::bulk_g2s(io_buf, src, kBlockBytes, bar);
+            if (cxs::mbar_wait_bounded(bar, phase, a.spin_limit, a.error)) {
+              cxs::bulk_s2g_and_wait(dst, io_buf, kBlockBytes);
+            } else {
+              cxs::mbar_wait_bounded(bar, phase, a.spin_limit, a.error);
+            }
+            cxs::fence_proxy_async_global();
+          }
+          phase ^= 1;
+        } else {
+          // Mixed-tier or tail block: 16-byte vector gathers, tail zero-filled.
+          gather_block<BS>(a.address + (long long)block * BS, a.valid[block],
+                           reinterpret_cast<uint4*>(dst), lane);
+          __threadfence();
+          cxs::fence_proxy_async_global();
+          __syncwarp();
+        }
+        if (lane == 0) cxs::st_release(&a.ready[block], 1);
       }
-      if (lane == 0) cxs::st_release(&a.ready[block], 1);
     }
   } else {
-    attention_warp<BS>(kv_map, win_map, a, q_tile, p_tile, warps_base + warp * tc::WarpSmem::kBytes,
-                       warp, tmem_base + warp * tc::kTmemCols);
+    const int e = warp % kAttnWarps;
+    if (warp < kAttnWarps)
+      softmax_warp<BS>(a, q_tile, p_tile, pair(e), e, tmem_base + e * tc::kTmemCols);
+    else
+      engine_warp<BS>(kv_map, win_map, a, q_tile, p_tile, pair(e), e, tmem_base + e * tc::kTmemCols);
   }
   // All warps (IO included) meet before the TMEM columns are released.
   tc::fence_before();
@@ -618,7 +713,7 @@ template <int BS>
 size_t smem_bytes() {
   size_t io = ((size_t)BS * kTokenBytes + 1023) & ~(size_t)1023;
   size_t tiles = 2 * (size_t)cxs::tc::kRowTileBytes;
-  size_t warps = (size_t)kAttnWarps * cxs::tc::WarpSmem::kBytes;
+  size_t warps = (size_t)kAttnWarps * cxs::tc::PairSmem::kBytes;
   return 1024 + io + tiles + warps + 128;
 }
 
@@ -673,6 +768,11 @@ int launch(const cxs_attend_geometry& g, const cxs_attend_buffers& b, cudaStream
   a.seg_tokens = (int)g.segment_tokens;
   a.spin_limit = g.spin_limit > 0 ? g.spin_limit : (1ll << 31);
   a.consumers = grid * kAttnWarps;
+  // IO warps on every io_stride-th CTA, spread over the grid: about
+  // kIoInflightBytes of block copies in flight (IO ranks come from an atomic
+  // cursor, so any number of IO warps fetches every block).
+  const int io_ctas = std::max(1, kIoInflightBytes / (BS * kTokenBytes));
+  a.io_stride = std::max(1, grid / io_ctas);
   a.query = (const __nv_bfloat16*)b.query;
   a.kv = (__nv_bfloat16*)b.kv;
   a.all_ids = b.all_ids;

@@ -61,6 +61,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // Bounded wait on an mbarrier phase. Returns false (and sets *error) on timeout.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase, long long limit,
                                                   int* error) {
@@ -123,6 +127,18 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Relaxed load at GPU scope: a poll of a flag whose value is consumed later;
+// a value seen set becomes an acquire with fence_acq_rel_gpu().
+__device__ __forceinline__ int ld_relaxed(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
 __device__ __forceinline__ void st_release(int* p, int v) {

@@ -1,23 +1,30 @@
-// tcgen05 / TMEM attention engine: one warp per query row (sm_100a).
+// tcgen05 / TMEM attention engine: one warp pair per query row (sm_100a).
 //
-// Each attention warp of a CTA owns one query row (16 GQA heads of one KV
-// head) at a time and issues its own MMAs. Key tiles (64 tokens of K and V,
-// staged in shared memory by TMA with a 128-byte swizzle) go through
-//   S[128 x 64 tok]  = Q[128 x 64 dim] . K^T      tcgen05.mma kind::f16, M=128 N=64
-//   online softmax in registers
-//   O[128 x 64 dim] += P[128 x 64 tok] . V         tcgen05.mma kind::f16, M=128 N=64
-// into the warp's own 128 TMEM columns (S: 64, O: 64). With M = 128, row r
-// of an accumulator is TMEM lane r, and warp w of the CTA can read lanes
-// 32w .. 32w + 31 only, so the warp's rows are 32w .. 32w + 31 of the A
-// tiles (Q and P, shared by the four warps; each MMA reads all 128 rows but
-// only the issuing warp's 32 rows of D are used). Rows 32w + i and
-// 32w + 16 + i both hold head i: lane i handles tokens 0-31 of each tile and
-// lane 16 + i tokens 32-63, with one shuffle to combine maxima and sums. P
-// row 32w + lane carries only the lane's own 32 tokens (the other half stays
-// zero), so the two O rows of a head are partial sums that the epilogue
-// adds. Q (pre-scaled by 0.125, bf16) and P (bf16 probabilities, as the
-// reference rounds them, tma/pipeline.py:250-253) are written in the swizzled
-// K-major layout the MMA descriptors describe; V is read MN-major.
+// Each engine of a CTA is a pair of warps that owns one query row (16 GQA
+// heads of one KV head) at a time:
+//   - the engine warp keeps the row's K/V tiles (64 tokens of K and V,
+//     staged in shared memory by TMA with a 128-byte swizzle) coming and
+//     issues every MMA of the row:
+//       S[128 x 64 tok]  = Q[128 x 64 dim] . K^T   tcgen05.mma kind::f16, M=128 N=64
+//       O[128 x 64 dim] += P[128 x 64 tok] . V      tcgen05.mma kind::f16, M=128 N=64
+//   - the softmax warp reads S from TMEM, runs the online softmax in
+//     registers, writes P to shared memory and rescales O in TMEM.
+// S(t + 1) is computed while the softmax of tile t runs, and neither warp
+// waits for its own MMA issue or copy bookkeeping: the pair hands tiles over
+// through shared-memory mbarriers (S computed, S read, P written, P.V done).
+// Both accumulators live in the pair's 128 TMEM columns (S: 64, O: 64). With
+// M = 128, row r of an accumulator is TMEM lane r, and the softmax warp of
+// engine w can read lanes 32w .. 32w + 31 only, so the engine's rows are
+// 32w .. 32w + 31 of the A tiles (Q and P, shared by the four engines; each
+// MMA reads all 128 rows but only the issuing engine's 32 rows of D are
+// used). Rows 32w + i and 32w + 16 + i both hold head i: lane i handles
+// tokens 0-31 of each tile and lane 16 + i tokens 32-63, with one shuffle to
+// combine maxima and sums. P row 32w + lane carries only the lane's own 32
+// tokens (the other half stays zero), so the two O rows of a head are
+// partial sums that the epilogue adds. Q (pre-scaled by 0.125, bf16) and P
+// (bf16 probabilities, as the reference rounds them, tma/pipeline.py:250-253)
+// are written in the swizzled K-major layout the MMA descriptors describe; V
+// is read MN-major.
 #pragma once
 
 #include "cxs_common.cuh"
@@ -27,11 +34,11 @@ namespace tc {
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLazyRescale = 8.f / kLog2e;  // natural-log units: a factor of 2^8
-constexpr int kEngines = 4;                    // attention warps per CTA (one per TMEM subpartition)
+constexpr int kEngines = 4;                    // warp pairs per CTA (softmax warp w reads TMEM subpartition w)
 constexpr int kTileRows = 64;                  // tokens per key tile (N of S, K of P.V)
 constexpr int kTileBytes = kTileRows * 128;    // one K or V tile
 constexpr int kRowTileBytes = 128 * 128;       // Q or P tile: 128 rows of 64 bf16
-constexpr int kTmemCols = 128;                 // per warp: S (64) + O (64)
+constexpr int kTmemCols = 128;                 // per engine: S (64) + O (64)
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version bits.
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -146,24 +153,54 @@ __device__ __forceinline__ uint32_t sw128_chunk(int row, int chunk) {
   return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-// Per-warp shared memory: two K buffers, two V buffers and the mbarriers
-// (K and V copies of a tile land separately: K is needed one step before V).
-struct WarpSmem {
-  static constexpr int kBars = 4 * kTileBytes;  // kbar[2], vbar[2], mma_bar
-  static constexpr int kBytes = kBars + 1024;   // keeps the next warp 1024-aligned
+// Shared memory of one engine (warp pair): three K buffers, two V buffers,
+// the mbarriers that hand tiles between the two warps, an abort word and the
+// row's selected blocks with their source kinds (staged by the engine warp).
+struct PairSmem {
+  static constexpr int kKBufs = 3, kVBufs = 2;
+  static constexpr int kBars = (kKBufs + kVBufs) * kTileBytes;
+  static constexpr int kBytes = kBars + 1024;  // keeps the next engine 1024-aligned
   uint8_t* base;
   __device__ __forceinline__ uint8_t* k(int b) const { return base + b * kTileBytes; }
-  __device__ __forceinline__ uint8_t* v(int b) const { return base + (2 + b) * kTileBytes; }
-  __device__ __forceinline__ uint64_t* kbar(int b) const {
-    return reinterpret_cast<uint64_t*>(base + kBars) + b;
+  __device__ __forceinline__ uint8_t* v(int b) const { return base + (kKBufs + b) * kTileBytes; }
+  __device__ __forceinline__ uint64_t* bar(int i) const {
+    return reinterpret_cast<uint64_t*>(base + kBars) + i;
   }
-  __device__ __forceinline__ uint64_t* vbar(int b) const {
-    return reinterpret_cast<uint64_t*>(base + kBars) + 2 + b;
+  __device__ __forceinline__ uint64_t* kbar(int b) const { return bar(b); }
+  __device__ __forceinline__ uint64_t* vbar(int b) const { return bar(kKBufs + b); }
+  // S(t) computed (MMA commit) / P.V(t) done (MMA commit) / S read or Q
+  // written (softmax warp) / P(t) written (softmax warp) / final MMA drain.
+  __device__ __forceinline__ uint64_t* sbar() const { return bar(5); }
+  __device__ __forceinline__ uint64_t* obar() const { return bar(6); }
+  __device__ __forceinline__ uint64_t* sfree() const { return bar(7); }
+  __device__ __forceinline__ uint64_t* pfull() const { return bar(8); }
+  __device__ __forceinline__ uint64_t* drain() const { return bar(9); }
+  static constexpr int kNumBars = 10;
+  __device__ __forceinline__ volatile int* abort_flag() const {
+    return reinterpret_cast<volatile int*>(base + kBars + 96);
   }
-  __device__ __forceinline__ uint64_t* mma_bar() const {
-    return reinterpret_cast<uint64_t*>(base + kBars) + 4;
-  }
+  __device__ __forceinline__ int* blocks() const { return reinterpret_cast<int*>(base + kBars + 128); }
+  __device__ __forceinline__ int* kinds() const { return reinterpret_cast<int*>(base + kBars + 256); }
 };
+
+// Bounded wait on an mbarrier phase that the partner warp of an engine
+// completes. Gives up at once when the partner has aborted, or after `limit`
+// cycles: then it records `code` in the device error word and aborts the
+// engine (both warps then leave the launch).
+__device__ __forceinline__ bool pair_wait(uint64_t* bar, uint32_t phase, volatile int* abort,
+                                          long long limit, int* error, int code) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, phase)) {
+    if (*abort) return false;
+    if (clock64() - start > limit) {
+      atomicOr(error, code);
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
 
 // Bounded wait on an mbarrier phase. On a timeout it records `code` in the
 // device error word, drains with a second bounded wait and returns false.
@@ -221,42 +258,43 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Online softmax over one tile for this lane's half (tokens 32 * half ..
-// 32 * half + 31) of its head's row; tokens outside [lo, hi] are masked. The
-// lane and its partner (lane ^ 16) agree on the tile max and sum. Writes the
-// lane's 32 bf16 probabilities into P row `m` and returns the factor the
-// running output must be scaled by (1 unless the reference maximum moved).
-// p = 2^(s log2e - m log2e), the exp2 form of the reference's exp(s - m),
-// with m the running reference maximum.
-__device__ __forceinline__ float softmax_half(uint8_t* p_tile, uint32_t s_addr, int lo, int hi,
-                                              float& m_run, float& l_run, int m, int half) {
-  float sv[32];
-  {
-    uint32_t r0[32], r1[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r0[0]), "=r"(r0[1]), "=r"(r0[2]), "=r"(r0[3]), "=r"(r0[4]), "=r"(r0[5]),
-          "=r"(r0[6]), "=r"(r0[7]), "=r"(r0[8]), "=r"(r0[9]), "=r"(r0[10]), "=r"(r0[11]),
-          "=r"(r0[12]), "=r"(r0[13]), "=r"(r0[14]), "=r"(r0[15]), "=r"(r0[16]), "=r"(r0[17]),
-          "=r"(r0[18]), "=r"(r0[19]), "=r"(r0[20]), "=r"(r0[21]), "=r"(r0[22]), "=r"(r0[23]),
-          "=r"(r0[24]), "=r"(r0[25]), "=r"(r0[26]), "=r"(r0[27]), "=r"(r0[28]), "=r"(r0[29]),
-          "=r"(r0[30]), "=r"(r0[31])
-        : "r"(s_addr));
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r1[0]), "=r"(r1[1]), "=r"(r1[2]), "=r"(r1[3]), "=r"(r1[4]), "=r"(r1[5]),
-          "=r"(r1[6]), "=r"(r1[7]), "=r"(r1[8]), "=r"(r1[9]), "=r"(r1[10]), "=r"(r1[11]),
-          "=r"(r1[12]), "=r"(r1[13]), "=r"(r1[14]), "=r"(r1[15]), "=r"(r1[16]), "=r"(r1[17]),
-          "=r"(r1[18]), "=r"(r1[19]), "=r"(r1[20]), "=r"(r1[21]), "=r"(r1[22]), "=r"(r1[23]),
-          "=r"(r1[24]), "=r"(r1[25]), "=r"(r1[26]), "=r"(r1[27]), "=r"(r1[28]), "=r"(r1[29]),
-          "=r"(r1[30]), "=r"(r1[31])
-        : "r"(s_addr + 32));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+// Scores of this lane's half (tokens 32 * half .. 32 * half + 31) of its
+// head's row of S (warp-collective TMEM reads of both halves).
+__device__ __forceinline__ void load_s(uint32_t s_addr, int half, float (&sv)[32]) {
+  uint32_t r0[32], r1[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r0[0]), "=r"(r0[1]), "=r"(r0[2]), "=r"(r0[3]), "=r"(r0[4]), "=r"(r0[5]),
+        "=r"(r0[6]), "=r"(r0[7]), "=r"(r0[8]), "=r"(r0[9]), "=r"(r0[10]), "=r"(r0[11]),
+        "=r"(r0[12]), "=r"(r0[13]), "=r"(r0[14]), "=r"(r0[15]), "=r"(r0[16]), "=r"(r0[17]),
+        "=r"(r0[18]), "=r"(r0[19]), "=r"(r0[20]), "=r"(r0[21]), "=r"(r0[22]), "=r"(r0[23]),
+        "=r"(r0[24]), "=r"(r0[25]), "=r"(r0[26]), "=r"(r0[27]), "=r"(r0[28]), "=r"(r0[29]),
+        "=r"(r0[30]), "=r"(r0[31])
+      : "r"(s_addr));
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r1[0]), "=r"(r1[1]), "=r"(r1[2]), "=r"(r1[3]), "=r"(r1[4]), "=r"(r1[5]),
+        "=r"(r1[6]), "=r"(r1[7]), "=r"(r1[8]), "=r"(r1[9]), "=r"(r1[10]), "=r"(r1[11]),
+        "=r"(r1[12]), "=r"(r1[13]), "=r"(r1[14]), "=r"(r1[15]), "=r"(r1[16]), "=r"(r1[17]),
+        "=r"(r1[18]), "=r"(r1[19]), "=r"(r1[20]), "=r"(r1[21]), "=r"(r1[22]), "=r"(r1[23]),
+        "=r"(r1[24]), "=r"(r1[25]), "=r"(r1[26]), "=r"(r1[27]), "=r"(r1[28]), "=r"(r1[29]),
+        "=r"(r1[30]), "=r"(r1[31])
+      : "r"(s_addr + 32));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(half ? r1[i] : r0[i]);
-  }
+  for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(half ? r1[i] : r0[i]);
+}
+
+// Online softmax over one tile for this lane's half of its head's row;
+// tokens outside [lo, hi] are masked. The lane and its partner (lane ^ 16)
+// agree on the tile max and sum. Leaves the lane's 32 probabilities in `sv`
+// and returns the factor the running output must be scaled by (1 unless the
+// reference maximum moved). p = 2^(s log2e - m log2e), the exp2 form of the
+// reference's exp(s - m), with m the running reference maximum.
+__device__ __forceinline__ float softmax_regs(float (&sv)[32], int lo, int hi, float& m_run,
+                                              float& l_run, int half) {
   // This lane's valid tokens: [lo_l, hi_l] within its 32.
   const int lo_l = lo - 32 * half, hi_l = hi - 32 * half;
   const bool whole = lo_l <= 0 && hi_l >= 31;
@@ -290,6 +328,11 @@ __device__ __forceinline__ float softmax_half(uint8_t* p_tile, uint32_t s_addr, 
   float sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
   sum += __shfl_xor_sync(0xffffffffu, sum, 16);
   l_run = l_run * factor + sum;
+  return factor;
+}
+
+// The lane's 32 probabilities as bf16 into its half of P row `m`.
+__device__ __forceinline__ void store_p(uint8_t* p_tile, int m, int half, const float (&sv)[32]) {
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     uint4 chunk = make_uint4(pack_bf16(sv[8 * c + 0], sv[8 * c + 1]),
@@ -298,7 +341,6 @@ __device__ __forceinline__ float softmax_half(uint8_t* p_tile, uint32_t s_addr, 
                              pack_bf16(sv[8 * c + 6], sv[8 * c + 7]));
     *reinterpret_cast<uint4*>(p_tile + sw128_chunk(m, 4 * half + c)) = chunk;
   }
-  return factor;
 }
 
 // Scale this warp's O rows by `factor` in TMEM (warp-collective; lanes that
