@@ -806,6 +806,7 @@ constexpr int kFusedMaxPhysical = 8192;
 constexpr int kFusedMaxMap = 65536;
 constexpr int kFusedMaxChain = 8;  // earlier rows per consumer recounted in phase 4
 constexpr int kFusedMaxHeads = 8;
+constexpr int kFusedRegions = 32;  // pool region bases kept in shared memory
 
 // Hardware barrier over the CTAs of the cluster, ordering their memory
 // accesses (shared and global) at cluster scope.
@@ -895,12 +896,35 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   const int words = (g.MAP + 31) / 32;
   uint32_t* claim = reinterpret_cast<uint32_t*>(fused_mem);
   unsigned char* scratch = fused_mem + (((size_t)words * 4 + 15) & ~(size_t)15);
+  // Scratch: the claim bitmaps and word prefix counts of every head (phases
+  // 2-3), the hot hash of this CTA's phase-3 head (built in phase 1) and the
+  // CTA's required lengths and full-history reference counts per physical
+  // block (phase 2); phase 6 reuses it all for the unique keys.
+  const size_t layout_bytes = ((size_t)2 * g.H * words * 4 + 15) & ~(size_t)15;
+  int* hkeys = reinterpret_cast<int*>(scratch + layout_bytes);
+  int* hvals = hkeys + g.HASH;
+  int* cta_required = hvals + g.HASH;  // [P]
+  int* cta_full = cta_required + g.P;  // [P]
+  const int per_head = ctas / g.H;  // phase-3 CTAs per head
+  const bool resolver = (int)blockIdx.x < per_head * g.H;
+  const bool hot_hash = resolver && !b.hbm_locs;
+  // Pool region bases (phase 3 address arithmetic) in shared memory.
+  __shared__ int64_t region_bases[kFusedRegions];
+  const int64_t* bases = g.REGIONS <= kFusedRegions ? region_bases : b.bases;
+  for (int i = threadIdx.x; i < min(g.REGIONS, kFusedRegions); i += kFusedThreads)
+    region_bases[i] = b.bases[i];
 
   // ---- 0: reset
   {
     clear_counters();
     if ((int)blockIdx.x < g.H)
       for (int i = threadIdx.x; i < words; i += kFusedThreads) claim[i] = 0;
+    if (hot_hash)
+      for (int i = threadIdx.x; i < g.HASH; i += kFusedThreads) hkeys[i] = -1;
+    for (int i = threadIdx.x; i < g.P; i += kFusedThreads) {
+      cta_required[i] = 0;
+      cta_full[i] = 0;
+    }
     const long long hc = (long long)g.H * g.CAP, hs = (long long)g.H * g.SORT;
     const long long rw = (long long)g.R * g.W;
     for (long long i = gtid; i < hc; i += gthreads) {
@@ -943,6 +967,29 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     }
     errors = cxs::warp_sum(errors);
     if (lane == 0 && errors) atomicAdd(&cta_stats[h * 7 + 6], errors);
+  }
+  // The hot hash of this CTA's phase-3 head: token -> replica location of
+  // the tags below the cached length (the first location of a duplicate tag).
+  if (hot_hash) {
+    const int h = blockIdx.x % g.H;
+    const int row = (int)b.desc[h * 5];
+    const int old = (int)b.desc[h * 5 + 1];
+    const int32_t* tags = b.tags + (long long)row * (g.HOT + 1);
+    const int32_t* locs = b.locs + (long long)row * (g.HOT + 1);
+    for (int i = threadIdx.x; i < g.HOT; i += kFusedThreads) {
+      const int token = tags[i];
+      if (token < 0 || token >= old) continue;
+      uint32_t s = hash_slot(token, g.HASH - 1);
+      for (int probe = 0; probe < g.HASH; ++probe) {
+        const int prev = atomicCAS(&hkeys[s], -1, token);
+        if (prev == -1) {
+          hvals[s] = locs[i];
+          break;
+        }
+        if (prev == token) break;  // duplicate tag: keep the first location
+        s = (s + 1) & (g.HASH - 1);
+      }
+    }
   }
   __syncthreads();
   flush_counters();
@@ -1008,7 +1055,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       b.active_keys[(long long)h * g.CAP + c] = kInt32Max;
   }
   // References, one occurrence per lane (required = causal prefix maximum,
-  // old / local token counts, one frequency-run count per occurrence).
+  // old / local token counts, one frequency-run count per occurrence). The
+  // required maximum and the counts of full-history occurrences gather in
+  // shared memory and reach global memory once per block and CTA: a block
+  // that every row selects would otherwise queue hundreds of atomics on one
+  // word at L2, and phase 3's reads of that word wait behind them.
   for (int r = gwarp; r < g.R; r += gwarps) {
     const int q = r / g.H, h = r % g.H;
     const int pos = b.positions[q];
@@ -1023,7 +1074,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       if (compact < 0 || compact >= g.CAP) continue;
       const int start = block * g.BS;
       const int req = min(g.BS, min(pos + 1, total) - start);
-      atomicMax(&b.required[(long long)h * g.CAP + compact], req);
+      atomicMax(&cta_required[h * g.CAP + compact], req);
       const int olds = min(max(old - start, 0), req);
       old_refs += olds;
       local_refs += req - olds;
@@ -1032,7 +1083,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       // (token o is counted by every occurrence covering more than o
       // historical tokens: a suffix sum).
       const int historical = min(max(history - start, 0), req);
-      if (historical > 0)
+      if (historical == g.BS)
+        atomicAdd(&cta_full[h * g.CAP + compact], 1);
+      else if (historical > 0)
         atomicAdd(&b.frequencies[(long long)h * g.SORT + (long long)compact * g.BS +
                                  historical - 1], 1);
     }
@@ -1044,167 +1097,170 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     }
   }
   __syncthreads();
+  int* cta_first = cta_required;  // reused in phase 4: the CTA's first consumption depths
+  for (int p = threadIdx.x; p < g.P; p += kFusedThreads) {
+    if (cta_required[p]) atomicMax(&b.required[p], cta_required[p]);
+    if (cta_full[p])
+      atomicAdd(&b.frequencies[(long long)(p / g.CAP) * g.SORT + (long long)(p % g.CAP) * g.BS +
+                               g.BS - 1],
+                cta_full[p]);
+    cta_first[p] = max_depth;
+  }
   flush_counters();
   __syncthreads();
   clear_counters();
   cluster_sync();
 
-  // ---- 3: source resolution; CTAs split by head, each with its hot hash
-  {
-    const int per_head = ctas / g.H;
-    if ((int)blockIdx.x < per_head * g.H) {
-      const int h = blockIdx.x % g.H, k = blockIdx.x / g.H;
-      int* hkeys = reinterpret_cast<int*>(scratch);
-      int* hvals = hkeys + g.HASH;
-      const int row = (int)b.desc[h * 5];
-      const int old = (int)b.desc[h * 5 + 1];
-      const long long pointer = b.desc[h * 5 + 3];
-      const int32_t* table = b.hbm_locs ? b.hbm_locs + (long long)row * g.MAXH : nullptr;
-      for (int i = threadIdx.x; i < g.HASH; i += kFusedThreads) hkeys[i] = -1;
-      __syncthreads();
-      const int32_t* tags = b.tags + (long long)row * (g.HOT + 1);
-      const int32_t* locs = b.locs + (long long)row * (g.HOT + 1);
-      for (int i = threadIdx.x; i < (table ? 0 : g.HOT); i += kFusedThreads) {
-        const int token = tags[i];
-        if (token < 0 || token >= old) continue;
-        uint32_t s = hash_slot(token, g.HASH - 1);
-        for (int probe = 0; probe < g.HASH; ++probe) {
-          const int prev = atomicCAS(&hkeys[s], -1, token);
-          if (prev == -1) {
-            hvals[s] = locs[i];
-            break;
+  // ---- 3: source resolution; CTAs split by head, one compact block per
+  // warp at a time (lane l owns tokens l and l + 32 of the block). The compact
+  // layout of phase 2 (claim bitmaps, word prefix counts) is still in shared
+  // memory and the hot hash was built in phase 1, so a block's id, the head's
+  // block count and hot locations are shared-memory lookups; every global
+  // load of a block (required length, frequency run, pool slots, residency
+  // table) is in flight before the first of them is used. The block loop is
+  // not unrolled: this phase runs once per launch, from a cold instruction
+  // cache, so its code is kept short.
+  if (resolver) {
+    const int h = blockIdx.x % g.H, k = blockIdx.x / g.H;
+    const int row = (int)b.desc[h * 5];
+    const int old = (int)b.desc[h * 5 + 1];
+    const long long pointer = b.desc[h * 5 + 3];
+    const int32_t* table = b.hbm_locs ? b.hbm_locs + (long long)row * g.MAXH : nullptr;
+    const int64_t* row_slots = b.host_locs + (long long)row * g.MAXH;
+    const char* hot_data = static_cast<const char*>(b.hot_data);
+    const uint32_t* hbits = bits + (long long)h * words;
+    const int* hprefix = prefix + (long long)h * words;
+    const int count = hprefix[words - 1] + __popc(hbits[words - 1]);
+    const int regions8 = min(g.REGIONS, 8);
+#pragma unroll 1
+    for (int c = k * kFusedWarps + warp; c < g.CAP; c += per_head * kFusedWarps) {
+      const bool active = c < count;
+      const long long p = (long long)h * g.CAP + c;
+      int32_t* run = b.frequencies + (long long)h * g.SORT + (long long)c * g.BS;
+      // Block id of compact index c: the c-th claimed block of the head.
+      int block = -1;
+      if (active) {
+        int lo = 0, hi = words - 1;  // last word whose prefix count is <= c
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (hprefix[mid] <= c) lo = mid;
+          else hi = mid - 1;
+        }
+        uint32_t word = hbits[lo];
+        for (int skip = c - hprefix[lo]; skip > 0; --skip) word &= word - 1;
+        block = lo * 32 + __ffs(word) - 1;
+      }
+      const int req = active ? b.required[p] : 0;
+      int fv[2];
+      long long slot[2];
+      int table_loc[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int o = lane + 32 * t;
+        const long long token = (long long)block * g.BS + o;
+        const bool history = active && o < g.BS && token < old && token < g.MAXH;
+        fv[t] = o < g.BS ? run[o] : 0;
+        slot[t] = history ? row_slots[token] : -1;
+        table_loc[t] = history && table ? table[token] : -1;
+      }
+      // Hot locations (shared memory) while the loads are in flight.
+      int hot_loc[2] = {-1, -1};
+      if (!table) {
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int o = lane + 32 * t;
+          const long long token = (long long)block * g.BS + o;
+          if (!(active && o < g.BS && token < old)) continue;
+          uint32_t s = hash_slot((int)token, g.HASH - 1);
+          for (int probe = 0; probe < g.HASH; ++probe) {
+            const int key = hkeys[s];
+            if (key == (int)token) {
+              hot_loc[t] = hvals[s];
+              break;
+            }
+            if (key == -1) break;
+            s = (s + 1) & (g.HASH - 1);
           }
-          if (prev == token) break;  // duplicate tag: keep the first location
-          s = (s + 1) & (g.HASH - 1);
         }
       }
-      __syncthreads();
-      const char* hot_data = static_cast<const char*>(b.hot_data);
-      const int count = b.active_counts[h];
-      // Four compact blocks per warp, eight lanes per block; lane `sub` of a
-      // group owns tokens sub, sub + 8, ... and frequency slots
-      // sub * per .. sub * per + per - 1 (per = BS / 8, BS <= 64). Every
-      // load of a block is issued before its first store.
-      const int sub = lane & 7, group = lane >> 3;
-      const int per = g.BS / 8;
-      for (int c0 = (k * kFusedWarps + warp) * 4; c0 < g.CAP;
-           c0 += per_head * kFusedWarps * 4) {
-        const int c = c0 + group;
-        const bool in_range = c < g.CAP;
-        const bool active = in_range && c < count;
-        const long long p = (long long)h * g.CAP + c;
-        int32_t* run = b.frequencies + (long long)h * g.SORT + (long long)c * g.BS;
-        int fv[8];
+      // Frequency run: per-token frequencies are suffix sums of the
+      // per-length counts (token o: counts at slots >= o).
+      {
+        int lo_sum = fv[0], hi_sum = fv[1];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) fv[t] = (in_range && t < per) ? run[sub * per + t] : 0;
-        const int block = active ? b.active_keys[p] : -1;
-        const int req = active ? b.required[p] : 0;
-        // Hot lookups and pool-slot loads for this lane's tokens.
-        long long source[8];
-        int location[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const int o = sub + 8 * t;
-          const long long token = (long long)block * g.BS + o;
-          const bool valid = active && o < req && t < per;
-          const bool previous = valid && token < old;
-          location[t] = -1;
-          source[t] = -1;
-          if (previous && table) {
-            location[t] = token < g.MAXH ? table[token] : -1;
-            if (location[t] < 0 && token < g.MAXH)
-              source[t] = b.host_locs[(long long)row * g.MAXH + token];
-          } else if (previous) {
-            uint32_t s = hash_slot((int)token, g.HASH - 1);
-            for (int probe = 0; probe < g.HASH; ++probe) {
-              const int key = hkeys[s];
-              if (key == (int)token) {
-                location[t] = hvals[s];
-                break;
-              }
-              if (key == -1) break;
-              s = (s + 1) & (g.HASH - 1);
-            }
-            if (location[t] < 0 && token < g.MAXH)
-              source[t] = b.host_locs[(long long)row * g.MAXH + token];
+        for (int d = 1; d < 32; d <<= 1) {
+          const int lo_other = __shfl_down_sync(0xffffffffu, lo_sum, d);
+          const int hi_other = __shfl_down_sync(0xffffffffu, hi_sum, d);
+          if (lane + d < 32) {
+            lo_sum += lo_other;
+            hi_sum += hi_other;
           }
         }
-        // Frequency run: suffix sums of the per-length counts.
-        {
-          int chunk = 0;
+        const int hi_total = __shfl_sync(0xffffffffu, hi_sum, 0);
+        if (lane < g.BS) run[lane] = lo_sum + hi_total;
+        if (lane + 32 < g.BS) run[lane + 32] = hi_sum;
+      }
+      unsigned packed = 0;  // n_valid | n_prev << 8 | n_hot << 16 | n_ext << 24
+      int n_err = 0, region_of[2] = {-1, -1};
 #pragma unroll
-          for (int t = 0; t < 8; ++t) chunk += fv[t];
-          int after = chunk;  // inclusive suffix over this group's lanes >= sub
-#pragma unroll
-          for (int o = 1; o < 8; o <<= 1) {
-            const int other = __shfl_down_sync(0xffffffffu, after, o, 8);
-            if (sub + o < 8) after += other;
-          }
-          after -= chunk;
-#pragma unroll
-          for (int t = 7; t >= 0; --t) {
-            after += fv[t];
-            if (in_range && t < per) run[sub * per + t] = after;
-          }
+      for (int t = 0; t < 2; ++t) {
+        const int o = lane + 32 * t;
+        if (o >= g.BS) continue;
+        const long long token = (long long)block * g.BS + o;
+        const bool valid = active && o < req;
+        const bool previous = valid && token < old;
+        int location = -1;
+        long long source = -1;
+        if (previous) {
+          location = table ? (token < g.MAXH ? table_loc[t] : -1) : hot_loc[t];
+          if (location < 0 && token < g.MAXH) source = slot[t];
         }
-        unsigned packed = 0;  // n_valid | n_prev << 8 | n_hot << 16 | n_ext << 24
-        int n_err = 0;
-        int region_mask_counts[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        const bool external = previous && location < 0;
+        const bool error = external && (source < 0 || source >= g.POOL);
+        const bool safe = external && !error;
+        long long hbm = 0;
+        if (valid && !external)
+          hbm = previous ? (long long)(hot_data + (long long)location * kTokenBytes)
+                         : pointer + (token - old) * kTokenBytes;
+        long long address = hbm;
+        if (safe) {
+          int region;
+          address = pool_address(g, bases, source, &region);
+          if (region < 8) region_of[t] = region;
+          else atomicAdd(&b.region_counts[region], 1);
+        }
+        const long long idx = p * g.BS + o;
+        b.address[idx] = address;
+        b.hbm[idx] = hbm;
+        b.slots[idx] = safe ? source : -1;
+        packed += (unsigned)valid | ((unsigned)previous << 8) |
+                  ((unsigned)(previous && !external) << 16) | ((unsigned)external << 24);
+        n_err += error;
+      }
+      // Block totals over the warp (every count is at most 64).
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const int o = sub + 8 * t;
-          if (!in_range || t >= per) continue;
-          const long long token = (long long)block * g.BS + o;
-          const bool valid = active && o < req;
-          const bool previous = valid && token < old;
-          const bool external = previous && location[t] < 0;
-          const bool error = external && (source[t] < 0 || source[t] >= g.POOL);
-          const bool safe = external && !error;
-          long long hbm = 0;
-          if (valid && !external)
-            hbm = previous ? (long long)(hot_data + (long long)location[t] * kTokenBytes)
-                           : pointer + (token - old) * kTokenBytes;
-          long long address = hbm;
-          if (safe) {
-            int region;
-            address = pool_address(g, b.bases, source[t], &region);
-            if (region < 8) region_mask_counts[region] += 1;
-            else atomicAdd(&b.region_counts[region], 1);
-          }
-          const long long idx = p * g.BS + o;
-          b.address[idx] = address;
-          b.hbm[idx] = hbm;
-          b.slots[idx] = safe ? source[t] : -1;
-          packed += (unsigned)valid | ((unsigned)previous << 8) |
-                    ((unsigned)(previous && !external) << 16) | ((unsigned)external << 24);
-          n_err += error;
-        }
-        // Sums over the 8 lanes of the group (every count is at most 64).
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) {
-          packed += __shfl_xor_sync(0xffffffffu, packed, o, 8);
-          n_err += __shfl_xor_sync(0xffffffffu, n_err, o, 8);
-        }
-        const int regions8 = min(g.REGIONS, 8);
-        for (int r = 0; r < regions8; ++r) {
-          int cnt = region_mask_counts[r];
-#pragma unroll
-          for (int o = 1; o < 8; o <<= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o, 8);
-          if (sub == 0 && cnt) atomicAdd(&cta_regions[r], cnt);
-        }
-        if (sub == 0 && in_range) {
-          const int n_valid = packed & 255u, n_prev = (packed >> 8) & 255u;
-          const int n_hot = (packed >> 16) & 255u, n_ext = packed >> 24;
-          b.valid[p] = (active && n_err == 0) ? req : 0;
-          b.starts[p] = active ? block * g.BS : 0;
-          b.flags[p] = n_ext > 0;
-          if (n_ext > 0) atomicAdd(&cta_missing, 1);
-          if (n_valid) atomicAdd(&cta_stats[h * 7 + 0], n_valid);
-          if (n_prev) atomicAdd(&cta_stats[h * 7 + 1], n_prev);
-          if (n_hot) atomicAdd(&cta_stats[h * 7 + 2], n_hot);
-          if (n_ext) atomicAdd(&cta_stats[h * 7 + 3], n_ext);
-          if (n_err) atomicAdd(&cta_stats[h * 7 + 6], n_err);
-        }
+      for (int d = 16; d; d >>= 1) {
+        packed += __shfl_xor_sync(0xffffffffu, packed, d);
+        n_err += __shfl_xor_sync(0xffffffffu, n_err, d);
+      }
+#pragma unroll 1
+      for (int r = 0; r < regions8; ++r) {
+        const int cnt = __popc(__ballot_sync(0xffffffffu, region_of[0] == r)) +
+                        __popc(__ballot_sync(0xffffffffu, region_of[1] == r));
+        if (lane == 0 && cnt) atomicAdd(&cta_regions[r], cnt);
+      }
+      if (lane == 0) {
+        const int n_valid = packed & 255u, n_prev = (packed >> 8) & 255u;
+        const int n_hot = (packed >> 16) & 255u, n_ext = packed >> 24;
+        b.valid[p] = (active && n_err == 0) ? req : 0;
+        b.starts[p] = active ? block * g.BS : 0;
+        b.flags[p] = n_ext > 0;
+        if (n_ext > 0) atomicAdd(&cta_missing, 1);
+        if (n_valid) atomicAdd(&cta_stats[h * 7 + 0], n_valid);
+        if (n_prev) atomicAdd(&cta_stats[h * 7 + 1], n_prev);
+        if (n_hot) atomicAdd(&cta_stats[h * 7 + 2], n_hot);
+        if (n_ext) atomicAdd(&cta_stats[h * 7 + 3], n_ext);
+        if (n_err) atomicAdd(&cta_stats[h * 7 + 6], n_err);
       }
     }
   }
@@ -1213,7 +1269,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   cluster_sync();
 
   // ---- 4: occurrence rows (+ consumption depth)
-  auto mapped = [&](int h, int block) { return b.mapping[(long long)h * (g.MAP + 1) + block]; };
+  // A block's compact index from the claim bitmaps still in shared memory
+  // (the same value phase 2 wrote into the mapping).
+  auto mapped = [&](int h, int block) { return rank_of(h, block); };
   const bool by_depth = g.ORDER != CXS_ORDER_PHYSICAL;
   for (int r = gwarp; r < g.R; r += gwarps) {
     int32_t* ids = b.all_ids + (long long)r * g.W;
@@ -1232,7 +1290,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     if (pos < 0) continue;
     for (int col = lane; col < min(g.W, count); col += 32) {
       const int block = ids[col];
-      if (block >= 0 && block < g.P && b.flags[block]) atomicMin(&b.first_depth[block], depth + col);
+      if (block >= 0 && block < g.P && b.flags[block]) atomicMin(&cta_first[block], depth + col);
     }
   }
   if (by_depth && !merged_depth) {
@@ -1247,9 +1305,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const int count = min(g.W, b.all_counts[r]);
       for (int col = lane; col < count; col += 32) {
         const int block = b.all_ids[(long long)r * g.W + col];
-        if (block >= 0 && block < g.P && b.flags[block]) atomicMin(&b.first_depth[block], depth + col);
+        if (block >= 0 && block < g.P && b.flags[block]) atomicMin(&cta_first[block], depth + col);
       }
     }
+  }
+  // First depths reach global memory once per block and CTA (as in phase 2).
+  if (by_depth) {
+    __syncthreads();
+    for (int p = threadIdx.x; p < g.P; p += kFusedThreads)
+      if (cta_first[p] < max_depth) atomicMin(&b.first_depth[p], cta_first[p]);
   }
   cluster_sync();
 
@@ -1410,9 +1474,10 @@ int launch_fused(const Geo& g, const cxs_plan_buffers& b, int max_depth, cudaStr
     return CXS_OK;
   if (g.H > kFusedMaxHeads) return CXS_OK;
   const size_t words = (size_t)(g.MAP + 31) / 32;
-  size_t smem = 2 * (size_t)g.H * words * 4;
-  smem = smem > (size_t)g.HASH * 8 ? smem : (size_t)g.HASH * 8;
-  smem = smem > (size_t)g.P * 8 ? smem : (size_t)g.P * 8;
+  // Claim bitmap, then the compact layout of every head, the hot hash and the
+  // per-CTA reference tallies (phases 1-3), or the unique keys (phase 6).
+  size_t smem = (((size_t)2 * g.H * words * 4 + 15) & ~(size_t)15) + (size_t)g.HASH * 8 +
+                (size_t)g.P * 8;
   smem += ((words * 4 + 15) & ~(size_t)15) + 16;  // the claim bitmap in front
   constexpr size_t kMaxFusedSmem = 160 * 1024;
   if (smem > kMaxFusedSmem) return CXS_OK;

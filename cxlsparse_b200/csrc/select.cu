@@ -239,6 +239,53 @@ __device__ __forceinline__ uint32_t topn_key(float v) {
   return v >= 0.f ? (__float_as_uint(v) & 0x7fffffffu) + 1u : 0u;
 }
 
+// Ranked picks k .. width - 1 of one row (warp-collective). Lane l keeps
+// its own candidates l, l + 32, ... below `limit` (visible, not taken) as a
+// list sorted by (key descending, block ascending) in registers, at most L
+// long: no more than width - k <= L picks can come from one lane. Each pick
+// is two warp reductions (the largest head key, then the lowest block id
+// holding it) and a shift of the owner's list, so the cost does not grow
+// with the number of candidates beyond building the lists.
+template <int L>
+__device__ __forceinline__ void ranked_picks(const RowGeo& wr, const float* sc, int limit,
+                                             int32_t* brow, int k, int width, int lane) {
+  uint32_t key[L], idx[L];
+#pragma unroll
+  for (int j = 0; j < L; ++j) {
+    key[j] = 0u;
+    idx[j] = 0xffffffffu;
+  }
+  for (int i = lane; i < limit; i += 32) {
+    uint32_t nk = wr.blocks.hides(i) ? 0u : topn_key(sc[i]), ni = (uint32_t)i;
+    if (nk == 0u) continue;
+    // Candidates arrive in ascending block order, so a strict comparison
+    // keeps equal keys in ascending block order.
+#pragma unroll
+    for (int j = 0; j < L; ++j) {
+      const bool swap = nk > key[j];
+      const uint32_t tk = swap ? key[j] : nk, ti = swap ? idx[j] : ni;
+      key[j] = swap ? nk : key[j];
+      idx[j] = swap ? ni : idx[j];
+      nk = tk;
+      ni = ti;
+    }
+  }
+  for (; k < width; ++k) {
+    const uint32_t top = __reduce_max_sync(0xffffffffu, key[0]);
+    const uint32_t pick = __reduce_min_sync(0xffffffffu, key[0] == top ? idx[0] : 0xffffffffu);
+    if (lane == 0) brow[k] = top ? (int32_t)pick : -1;
+    if (top && idx[0] == pick) {  // the owner drops its head
+#pragma unroll
+      for (int j = 0; j + 1 < L; ++j) {
+        key[j] = key[j + 1];
+        idx[j] = idx[j + 1];
+      }
+      key[L - 1] = 0u;
+      idx[L - 1] = 0xffffffffu;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     compressed_select_tc_kernel(const __grid_constant__ CUtensorMap map, SelectArgs a,
                                 int kres) {
@@ -556,44 +603,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
   }
   // Top-n, warp r for row r: the current block first, then earlier blocks by
-  // (score descending, block ascending). Lane l owns candidates l, l + 32, ...
-  // and keeps its best key; each pick is two warp reductions (max key, then
-  // min block id among the lanes holding it) and one rescan by the owner.
+  // (score descending, block ascending).
   if (warp < kTcRows && q0 + warp < a.Q) {
     const int qq = q0 + warp;
     const RowGeo wr = row_geo(a, a.positions[qq]);
-    const int current = wr.current;
-    const int limit = min(current, ranked_len);
+    const int limit = min(wr.current, ranked_len);
     float* sc = ranked + warp * ranked_len;
     int32_t* brow = a.blocks + ((long long)qq * H + h) * a.width;
-    uint32_t best = 0, best_idx = 0xffffffffu;
-    auto rescan = [&]() {
-      best = 0;
-      best_idx = 0xffffffffu;
-      for (int i = lane; i < limit; i += 32) {
-        const uint32_t key = wr.blocks.hides(i) ? 0u : topn_key(sc[i]);
-        if (key > best) {
-          best = key;
-          best_idx = i;
-        }
-      }
-    };
     int k = 1;
-    if (current < 0) {
+    if (wr.current < 0) {
       if (lane == 0) brow[0] = -1;
     } else {
       k = forced_picks(a, wr, brow, sc, lane);
     }
-    rescan();
-    for (; k < a.width; ++k) {
-      const uint32_t top = __reduce_max_sync(0xffffffffu, best);
-      const uint32_t idx = __reduce_min_sync(0xffffffffu, best == top ? best_idx : 0xffffffffu);
-      if (lane == 0) brow[k] = top ? (int32_t)idx : -1;
-      if (top && (int)(idx & 31) == lane) {
-        sc[idx] = -1.f;  // taken
-        rescan();
-      }
-    }
+    if (a.width <= 16)
+      ranked_picks<16>(wr, sc, limit, brow, k, a.width, lane);
+    else
+      ranked_picks<32>(wr, sc, limit, brow, k, a.width, lane);
   }
   tc::fence_before();
   __syncthreads();
@@ -667,6 +693,7 @@ extern "C" int cxs_compressed_select_nsa(const cxs_select_geometry* geometry, co
     return set_error(CXS_ERR_INVALID, "null compressed-select argument");
   if (((uintptr_t)compressed & 15) || ((uintptr_t)query & 15) || ((uintptr_t)out & 15))
     return set_error(CXS_ERR_INVALID, "query/compressed/out must be 16-byte aligned");
+  if (count > 32) return set_error(CXS_ERR_INVALID, "count (top-n) must be at most 32");
   long long blocks_total = (total + block_size - 1) / block_size;
   int width = (int)(count < blocks_total ? count : blocks_total);
   if (summaries > (1 << 20)) return set_error(CXS_ERR_CAPACITY, "too many summaries");

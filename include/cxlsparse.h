@@ -339,7 +339,8 @@ int cxs_exchange_barrier(int32_t* counter, int32_t* const* peer_flags, int32_t* 
  * selection from the summed GQA probabilities (models/nsa/ops.py:73-123;
  * third_party/nsa_runtime/kernels.py:13-230). Selection order: current block
  * first, then score descending with ties to the lower block id; width =
- * min(count, ceil(total / BS)); entries after the current block are -1.
+ * min(count, ceil(total / BS)) with count <= 32 (the attend launch takes at
+ * most 32 selected blocks per row); entries after the current block are -1.
  */
 int cxs_compressed_select(const void* query,      /* [Q, H, 16, 64] bf16 */
                           const void* compressed, /* [C, H, 128] bf16 (K || V) */
