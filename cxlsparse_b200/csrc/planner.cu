@@ -865,8 +865,6 @@ __device__ __forceinline__ int row_occurrences(const Geo& g, const cxs_plan_buff
 __global__ void __launch_bounds__(kFusedThreads, 1)
     plan_fused_kernel(Geo g, cxs_plan_buffers b, int max_depth, int merged_depth) {
   extern __shared__ __align__(16) unsigned char fused_mem[];
-  typedef cub::BlockScan<int, kFusedThreads> Scan;
-  __shared__ typename Scan::TempStorage scan;
   const int ctas = gridDim.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long long gtid = (long long)blockIdx.x * kFusedThreads + threadIdx.x;
@@ -914,11 +912,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   for (int i = threadIdx.x; i < min(g.REGIONS, kFusedRegions); i += kFusedThreads)
     region_bases[i] = b.bases[i];
 
-  // ---- 0: reset
+  // ---- 0: reset. The claim bitmaps are cleared first and announced with a
+  // split cluster barrier, so the global resets below overlap the barrier's
+  // latency (they are ordered before phase 2 by the barrier after phase 1).
   {
     clear_counters();
     if ((int)blockIdx.x < g.H)
       for (int i = threadIdx.x; i < words; i += kFusedThreads) claim[i] = 0;
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     if (hot_hash)
       for (int i = threadIdx.x; i < g.HASH; i += kFusedThreads) hkeys[i] = -1;
     for (int i = threadIdx.x; i < g.P; i += kFusedThreads) {
@@ -948,7 +949,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     // valid blocks are claimed), so only the sentinel is set here.
     for (long long i = gtid; i < g.H; i += gthreads) b.mapping[i * (g.MAP + 1) + g.MAP] = -2;
   }
-  cluster_sync();
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  __syncthreads();  // this CTA's shared-memory resets (hot hash, tallies) done
 
   // ---- 1: dedup claims: each valid occurrence sets its block's bit in the
   // head's claim bitmap (CTA h's shared memory); duplicates set it again.
@@ -1008,19 +1010,24 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       bits[h * words + i] = cluster_ld(remote + (uint32_t)i * 4);
   }
   __syncthreads();
-  const int per = (words + kFusedThreads - 1) / kFusedThreads;
-  for (int h = 0; h < g.H; ++h) {
-    const int begin = threadIdx.x * per, end = min(words, begin + per);
-    int local = 0;
-    for (int w = begin; w < end; ++w) local += __popc(bits[h * words + w]);
-    int offset;
-    Scan(scan).ExclusiveSum(local, offset);
-    for (int w = begin; w < end; ++w) {
-      prefix[h * words + w] = offset;
-      offset += __popc(bits[h * words + w]);
+  // Word prefix counts of head h: warp h scans the head's words 32 at a time.
+  if (warp < g.H) {
+    const int h = warp;
+    int carry = 0;
+    for (int base = 0; base < words; base += 32) {
+      const int w = base + lane;
+      const int c = w < words ? __popc(bits[h * words + w]) : 0;
+      int incl = c;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int other = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += other;
+      }
+      if (w < words) prefix[h * words + w] = carry + incl - c;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    __syncthreads();
   }
+  __syncthreads();
   auto rank_of = [&](int h, int block) -> int {
     const uint32_t word = bits[h * words + (block >> 5)];
     const uint32_t bit = 1u << (block & 31);
@@ -1034,21 +1041,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       b.active_counts[h] = count;
       if (count > g.CAP) atomicAdd(&b.stats[h * 7 + 6], count - g.CAP);  // no slot left
     }
-    const int begin = threadIdx.x * per, end = min(words, begin + per);
-    for (int w = begin; w < end; ++w) {
-      uint32_t word = bits[h * words + w];
-      int offset = prefix[h * words + w];
-      while (word) {
-        const int block = w * 32 + __ffs(word) - 1;
-        word &= word - 1;
-        if (offset < g.CAP) {
-          b.active_keys[(long long)h * g.CAP + offset] = block;
-          b.insert_keys[(long long)h * g.CAP + offset] = block;
-          b.mapping[(long long)h * (g.MAP + 1) + block] = offset;
-        } else {
-          b.mapping[(long long)h * (g.MAP + 1) + block] = -2;
-        }
-        ++offset;
+    // One thread per block id: claimed blocks write their compact slot.
+    for (int block = threadIdx.x; block < g.MAP; block += kFusedThreads) {
+      const int offset = rank_of(h, block);
+      if (offset < 0) continue;
+      if (offset < g.CAP) {
+        b.active_keys[(long long)h * g.CAP + offset] = block;
+        b.insert_keys[(long long)h * g.CAP + offset] = block;
+        b.mapping[(long long)h * (g.MAP + 1) + block] = offset;
+      } else {
+        b.mapping[(long long)h * (g.MAP + 1) + block] = -2;
       }
     }
     for (int c = min(count, g.CAP) + threadIdx.x; c < g.CAP; c += kFusedThreads)
