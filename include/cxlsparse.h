@@ -45,7 +45,7 @@ enum cxs_status {
 };
 
 /* Bits of the device error word written by cxs_fetch_attend. */
-#define CXS_DEVICE_ERR_READY_TIMEOUT 1 /* an attention warp gave up waiting on ready[b] */
+#define CXS_DEVICE_ERR_READY_TIMEOUT 1 /* an attention engine gave up waiting on ready[b] */
 #define CXS_DEVICE_ERR_COPY_TIMEOUT 2  /* a bulk copy did not complete within the limit */
 #define CXS_DEVICE_ERR_BAD_BLOCK 4     /* a plan entry was out of range */
 
@@ -201,11 +201,13 @@ int cxs_plan_commit_hot(const cxs_plan_geometry* geometry, const cxs_plan_buffer
  *    contiguous 16-byte aligned external blocks move host -> shared -> HBM
  *    with 1-D bulk TMA copies, mixed/tail blocks move with 16-byte vector
  *    gathers; each then publishes ready[b] with st.release.gpu.
- *  - attention warps own query rows; they first run the sliding-window
- *    branch (HBM resident), then acquire ready[b] for each selected
- *    occurrence in the original order, stage K and V through shared memory
- *    with 2-D tensor TMA, and run online-softmax attention with tensor-core
- *    MMAs; the epilogue optionally applies the sigmoid-gate mix
+ *  - attention engines (warp pairs) own query rows; they first run the
+ *    sliding-window branch (HBM resident), then acquire ready[b] for each
+ *    selected occurrence in the original order (not needed for blocks that
+ *    were resident before the launch), stage K and V through shared memory
+ *    with 2-D tensor TMA, and run online-softmax attention with tcgen05 MMAs
+ *    that the engine warp issues while its softmax warp works on the
+ *    previous tile; the epilogue optionally applies the sigmoid-gate mix
  *    (models/nsa/model.py:470-473).
  * A preceding prepare kernel (same call) classifies block sources, gathers
  * resident blocks into the staging buffer and initialises ready flags.
@@ -279,10 +281,11 @@ typedef struct cxs_attend_buffers {
 int cxs_fetch_attend(const cxs_attend_geometry* geometry, const cxs_attend_buffers* buffers,
                      void* stream);
 
-/* Number of attention warps one cxs_fetch_attend launch runs on the current
- * device for `block_size` (grid = resident CTAs x 8 warps). A plan's
- * consumer_ctas should be min(rows, this) so that its consumption-depth order
- * models the real consumers (tma/transport.py:63 uses min(rows, 256)). */
+/* Number of attention engines (consumers) one cxs_fetch_attend launch runs on
+ * the current device for `block_size` (grid = resident CTAs x 4 warp-pair
+ * engines). A plan's consumer_ctas should be min(rows, this) so that its
+ * consumption-depth order models the real consumers (tma/transport.py:63
+ * uses min(rows, 256)). */
 int cxs_attend_capacity(int32_t block_size, int32_t* attention_warps);
 
 /* Allocation-free variant of cxs_fetch_attend. No counterpart in the
