@@ -424,6 +424,9 @@ __device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_til
     return ok;
   };
   for (int row = e * gridDim.x + blockIdx.x; row < rows; row += a.consumers) {
+    // The query row first (its loads do not depend on the plan's tables), so
+    // the engine can start S(0) as soon as its first K tile lands.
+    tc::write_query_row(q_tile, a.query, row, m, lane);
     const RowTiles rt = row_tiles(a, row);
     const int total = rt.total, n_win = rt.n_win, pos = rt.pos;
     // Lane i holds selected occurrence i's first position.
@@ -432,7 +435,6 @@ __device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_til
       my_block = a.all_ids[(long long)row * a.W + lane];
       if (my_block >= 0 && my_block < a.P) my_start = a.starts[my_block];
     }
-    tc::write_query_row(q_tile, a.query, row, m, lane);
     cxs::fence_proxy_async_shared();
     __syncwarp();
     if (total > 0 && leader) cxs::mbar_arrive(ps.sfree());  // Q written
@@ -588,16 +590,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                  "r"(kTmemAlloc));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  // Zero the P tile (each lane only ever writes its own half of its row) and
-  // the K/V stages (rows beyond a short block, BS < 64, start at zero and
-  // afterwards only hold finite key/value data).
+  // Zero the P tile (each lane only ever writes its own half of its row) and,
+  // for blocks shorter than a tile (BS < 64), the K/V stages: the rows beyond
+  // such a block start at zero and afterwards only hold finite key/value data.
   if (warp < kIoWarp) {
     constexpr int kStaged = tc::PairSmem::kKBufs + tc::PairSmem::kVBufs;
     for (int i = threadIdx.x; i < tc::kRowTileBytes / 16; i += 32 * kIoWarp)
       reinterpret_cast<uint4*>(p_tile)[i] = make_uint4(0, 0, 0, 0);
-    for (int e = 0; e < kAttnWarps; ++e)
-      for (int i = threadIdx.x; i < kStaged * tc::kTileBytes / 16; i += 32 * kIoWarp)
-        reinterpret_cast<uint4*>(pair(e).base)[i] = make_uint4(0, 0, 0, 0);
+    if (BS < tc::kTileRows)
+      for (int e = 0; e < kAttnWarps; ++e)
+        for (int i = threadIdx.x; i < kStaged * tc::kTileBytes / 16; i += 32 * kIoWarp)
+          reinterpret_cast<uint4*>(pair(e).base)[i] = make_uint4(0, 0, 0, 0);
   }
   cxs::fence_proxy_async_shared();
   tc::fence_before();
