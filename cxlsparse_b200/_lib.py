@@ -141,6 +141,8 @@ def lib():
             "cxs_block_summaries_segments": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_i32,
                                                      c_i64, c_i64, c_vp]),
             "cxs_rms_norm": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, ctypes.c_float, c_vp]),
+            "cxs_residual_rms_norm": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, ctypes.c_float,
+                                              c_vp]),
             "cxs_qkv_rope": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp,
                                      c_i32, c_vp, c_i32, c_vp, c_vp]),
             "cxs_qkv_rope_segments": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_i32, c_i32, c_i32,
@@ -193,6 +195,7 @@ def exported_symbols():
             "cxs_compressed_select", "cxs_compressed_select_segments",
             "cxs_compressed_select_nsa", "cxs_select_score_columns",
             "cxs_block_summaries", "cxs_block_summaries_segments", "cxs_rms_norm",
+            "cxs_residual_rms_norm",
             "cxs_qkv_rope", "cxs_qkv_rope_segments", "cxs_silu_mul", "cxs_compress_windows",
             "cxs_device_alloc",
             "cxs_device_free", "cxs_ipc_get_handle", "cxs_ipc_open_handle", "cxs_ipc_close",

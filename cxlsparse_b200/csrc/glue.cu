@@ -92,6 +92,52 @@ __global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x,
   }
 }
 
+// One CTA per row: the residual add of the preceding projection and the
+// RMSNorm that follows it, in the reference's bf16 sequence
+// (models/nsa/model.py: hidden = hidden + F.linear(...), then rms_norm):
+//   h = bf16(hidden + delta), written back to `hidden`;
+//   out = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * w).
+// The row is read as 16-byte vectors and kept in registers (dim % 8 == 0,
+// aligned rows, at most kMaxChunks vectors per thread; checked by the host).
+__global__ void residual_rms_norm_kernel(__nv_bfloat16* hidden, const __nv_bfloat16* delta,
+                                         const __nv_bfloat16* __restrict__ w,
+                                         __nv_bfloat16* __restrict__ out, int dim, float eps) {
+  __shared__ float partial[32];
+  uint4* row = reinterpret_cast<uint4*>(hidden + (long long)blockIdx.x * dim);
+  const uint4* drow = reinterpret_cast<const uint4*>(delta + (long long)blockIdx.x * dim);
+  uint4* orow = reinterpret_cast<uint4*>(out + (long long)blockIdx.x * dim);
+  const int chunks = dim / 8;
+  float v[kMaxChunks][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < chunks) {
+      float d[8];
+      unpack8(row[c], v[k]);
+      unpack8(drow[c], d);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[k][i] = rbf(v[k][i] + d[i]);
+        sum += v[k][i] * v[k][i];
+      }
+      row[c] = pack8(v[k]);
+    }
+  }
+  const float scale = rsqrtf(block_sum(sum, partial) / (float)dim + eps);
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < chunks) {
+      float wv[8], o[8];
+      unpack8(reinterpret_cast<const uint4*>(w)[c], wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = rbf(v[k][i] * scale) * wv[i];
+      orow[c] = pack8(o);
+    }
+  }
+}
+
 // RoPE (rotate-half, bf16 rounding per op) + sigmoid gates + output packing
 // from the fused projection [E, Hq*64 | Hkv*64 | Hkv*64 | Hq*3]. One CTA per
 // token; the token's 32 (cos, sin) pairs are computed once and shared by all heads.
@@ -364,6 +410,25 @@ extern "C" int cxs_rms_norm(const void* x, const void* weight, void* out, int32_
     rms_norm_kernel<false><<<rows, 256, 0, (cudaStream_t)stream>>>(
         (const __nv_bfloat16*)x, (const __nv_bfloat16*)weight, (__nv_bfloat16*)out, dim, eps);
   CXS_LAUNCH_CHECK("rms_norm_kernel");
+  return CXS_OK;
+}
+
+extern "C" int cxs_residual_rms_norm(void* hidden, const void* delta, const void* weight,
+                                     void* out, int32_t rows, int32_t dim, float eps,
+                                     void* stream) {
+  if (rows < 0 || dim < 1) return set_error(CXS_ERR_INVALID, "invalid rms_norm geometry");
+  if (!hidden || !delta || !weight || !out)
+    return set_error(CXS_ERR_INVALID, "null residual rms_norm argument");
+  if (dim % 8 || dim / 8 > 256 * kMaxChunks ||
+      (((uintptr_t)hidden | (uintptr_t)delta | (uintptr_t)weight | (uintptr_t)out) & 15))
+    return set_error(CXS_ERR_INVALID,
+                     "residual rms_norm needs 16-byte aligned rows of at most %d (dim % 8 == 0)",
+                     8 * 256 * kMaxChunks);
+  if (!rows) return CXS_OK;
+  residual_rms_norm_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(
+      (__nv_bfloat16*)hidden, (const __nv_bfloat16*)delta, (const __nv_bfloat16*)weight,
+      (__nv_bfloat16*)out, dim, eps);
+  CXS_LAUNCH_CHECK("residual_rms_norm_kernel");
   return CXS_OK;
 }
 

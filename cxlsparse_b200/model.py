@@ -419,6 +419,10 @@ class NSAExtendModel:
                                        w["g"][h0 * cfg.groups * 3:(h0 + kl) * cfg.groups * 3]]
                                       ).contiguous()
                 w["gate_up"] = torch.cat([w["gate"], w["up"]]).contiguous()
+                # o_proj and down as [K, N] (NN GEMMs, faster at these row
+                # counts); their residual adds run in the RMSNorm that follows.
+                w["o_t"] = w["o"].t().contiguous()
+                w["down_t"] = w["down"].t().contiguous()
         old = st.length
         layout = SegmentLayout(old, E, n_cand, bs)
         tail_len, start, seg_tokens = layout.tail, layout.start, layout.tokens
@@ -532,15 +536,31 @@ class NSAExtendModel:
             mlp=torch.empty((rows, cfg.ffn), dtype=torch.bfloat16, device=d))
         return self.fast
 
-    def _layer_fast(self, index, hidden):
+    def _norm(self, hidden, delta, weight, out):
+        """out = rms_norm(hidden) after ``hidden += delta`` (in place, the
+        residual add of the preceding projection), in one launch; plain
+        rms_norm without a delta."""
+        cfg, lib = self.cfg, _lib.lib()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        if delta is None:
+            _lib.check(lib.cxs_rms_norm(hidden.data_ptr(), weight.data_ptr(), out.data_ptr(),
+                                        len(hidden), cfg.hidden, cfg.rms_eps, stream))
+        else:
+            _lib.check(lib.cxs_residual_rms_norm(
+                hidden.data_ptr(), delta.data_ptr(), weight.data_ptr(), out.data_ptr(),
+                len(hidden), cfg.hidden, cfg.rms_eps, stream))
+
+    def _layer_fast(self, index, hidden, pending=None):
+        """One layer on the fused path. ``hidden`` still lacks the previous
+        layer's down projection ``pending`` (added in place by this layer's
+        first RMSNorm); returns (hidden, this layer's down projection)."""
         cfg, w, f = self.cfg, self.layers[index], self.fast
         L = f["layers"][index]
         E = f["E"]
         lib = _lib.lib()
         stream = torch.cuda.current_stream(self.device).cuda_stream
         x, query, gates, positions = f["x"], f["query"], f["gates"], f["positions"]
-        _lib.check(lib.cxs_rms_norm(hidden.data_ptr(), w["in_norm"].data_ptr(), x.data_ptr(), E,
-                                    cfg.hidden, cfg.rms_eps, stream))
+        self._norm(hidden, pending, w["in_norm"], x)
         proj = F.linear(x, w["qkvg"])
         kl = self.kv_local
         segments = f["segments"]
@@ -595,12 +615,12 @@ class NSAExtendModel:
             self.exchange.barrier(stream)
         if self.attention_outputs is not None:  # the transport's output is a borrowed view
             self.attention_outputs.append(mixed[:E].clone())
-        hidden = torch.addmm(hidden, mixed.reshape(E, -1), w["o"].t())
-        _lib.check(lib.cxs_rms_norm(hidden.data_ptr(), w["post_norm"].data_ptr(), x.data_ptr(),
-                                    E, cfg.hidden, cfg.rms_eps, stream))
+        # hidden = hidden + o_proj(mixed) (each rounded to bf16, as the
+        # reference's bf16 tensors are), fused with the post-attention norm.
+        self._norm(hidden, torch.mm(mixed.reshape(E, -1), w["o_t"]), w["post_norm"], x)
         gate_up = F.linear(x, w["gate_up"])
         _lib.check(lib.cxs_silu_mul(gate_up.data_ptr(), E, cfg.ffn, f["mlp"].data_ptr(), stream))
-        return torch.addmm(hidden, f["mlp"], w["down"].t())
+        return hidden, torch.mm(f["mlp"], w["down_t"])
 
     def extend_fast(self, token_ids, hidden=None, user=None):
         """Extend step through the fused glue (after ``prepare_fast``).
@@ -614,18 +634,18 @@ class NSAExtendModel:
             self.fast = self.fast_states[user]
         if self.fast is None or len(token_ids) != self.fast["E"]:
             raise ValueError("prepare_fast(len(token_ids)) first")
-        if hidden is None:
-            hidden = F.embedding(token_ids, self.embed)
+        # The layers update `hidden` in place; the caller's tensor stays as given.
+        hidden = F.embedding(token_ids, self.embed) if hidden is None else hidden.clone()
+        pending = None  # the last down projection, added by the next norm
         for index in range(self.cfg.layers):
-            hidden = self._layer_fast(index, hidden)
-            if self.layer_outputs is not None:
-                self.layer_outputs.append(hidden)
+            hidden, pending = self._layer_fast(index, hidden, pending)
+            if self.layer_outputs is not None:  # materialise the layer's output
+                hidden, pending = hidden + pending, None
+                self.layer_outputs.append(hidden.clone())  # the next layer adds in place
         self.transport.join()
         self._check_exchange()
         out = torch.empty_like(hidden)
-        _lib.check(_lib.lib().cxs_rms_norm(
-            hidden.data_ptr(), self.final_norm.data_ptr(), out.data_ptr(), len(hidden),
-            self.cfg.hidden, self.cfg.rms_eps, torch.cuda.current_stream(self.device).cuda_stream))
+        self._norm(hidden, pending, self.final_norm, out)
         return out
 
     def capture_extend(self, extend_tokens, user="user", warmup=2, candidates=1):

@@ -422,6 +422,14 @@ int cxs_block_summaries_segments(const void* tokens, int64_t count, int32_t head
 /* out[r] = bf16(bf16(x[r] * rsqrt(mean(x[r]^2) + eps)) * weight), bf16 rows. */
 int cxs_rms_norm(const void* x, const void* weight, void* out, int32_t rows, int32_t dim,
                  float eps, void* stream);
+
+/* The residual add of a projection and the RMSNorm that follows it, in one
+ * launch and in the reference's bf16 sequence (hidden = hidden + F.linear(..),
+ * then rms_norm; models/nsa/model.py:440-492): hidden[r] = bf16(hidden[r] +
+ * delta[r]) in place, out[r] = bf16(bf16(hidden[r] * rsqrt(mean(hidden[r]^2) +
+ * eps)) * weight). Rows are 16-byte aligned, dim a multiple of 8. */
+int cxs_residual_rms_norm(void* hidden, const void* delta, const void* weight, void* out,
+                          int32_t rows, int32_t dim, float eps, void* stream);
 /* From the fused projection [tokens, q_heads*64 | kv*64 (k) | kv*64 (v) | q_heads*3 (g)]
  * (row stride proj_stride elements): rotary q/k (rotate-half, inv_freq [32]),
  * write query [tokens, q_heads, 64], records [tokens, kv, 128] (K || V, row
