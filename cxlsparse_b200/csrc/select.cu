@@ -298,6 +298,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int m = 32 * lg + lane;             // A row / TMEM lane of this thread
   const int h = blockIdx.x % H;
   const int q0 = (blockIdx.x / H) * kTcRows;
+  // Position of the row this warp ranks (warps 0 .. kTcRows - 1), read once
+  // here so the load overlaps the score pass.
+  const bool ranks_row = warp < kTcRows && q0 + warp < a.Q;
+  const int rank_pos = ranks_row ? a.positions[q0 + warp] : 0;
   uint8_t* q_tile = smem;
   uint8_t* k_base = q_tile + kTcQBytes;
   uint8_t* v_base = k_base + kres * kTcChunkBytes;
@@ -420,8 +424,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc::fence_after();
   };
 
-  // Pass 1: per-row max and normaliser over every chunk.
+  // Pass 1: per-row max and normaliser over every chunk. With a single chunk
+  // (the common case) the probabilities computed for the normaliser stay in
+  // registers for pass 2 (same values: the chunk's max is the final max).
   float m_run = -INFINITY, l_run = 0.f;
+  const bool single = chunks == 1;
+  float v0[32], v1[32];
   for (int j = 0; j < chunks && ok; ++j) {
     if (j > 0 && !resident) {
       if (tid == 0) {
@@ -435,7 +443,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // This warp's column groups (32 columns each) of the chunk: 2 cq, 2 cq + 1.
     const bool mine = cq < tiles_of(j);
     const int col0 = kTcChunk * j + 64 * cq;
-    float v0[32], v1[32];
     if (mine) {  // warp-uniform
       tc::ld32(s_addr + 64 * cq, v0);
       tc::ld32(s_addr + 64 * cq + 32, v1);
@@ -458,8 +465,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (mine) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        if ((vis0 >> i) & 1u) sum += tc::ex2(fmaf(v0[i], tc::kLog2e, -off));
-        if ((vis1 >> i) & 1u) sum += tc::ex2(fmaf(v1[i], tc::kLog2e, -off));
+        const float p0 = (vis0 >> i) & 1u ? tc::ex2(fmaf(v0[i], tc::kLog2e, -off)) : 0.f;
+        const float p1 = (vis1 >> i) & 1u ? tc::ex2(fmaf(v1[i], tc::kLog2e, -off)) : 0.f;
+        sum += p0;
+        sum += p1;
+        if (single) {
+          v0[i] = p0;
+          v1[i] = p1;
+        }
       }
     }
     red_sum[cq * 128 + m] = sum;
@@ -495,11 +508,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int half = 0; half < 2; ++half) {
         const int col0 = kTcChunk * j + 64 * cq + 32 * half;
         float v[32];
-        tc::ld32(s_addr + 64 * cq + 32 * half, v);
-        const uint32_t vis = rg.visible_bits(col0);
+        if (single) {  // pass 1's probabilities (offset = its maximum)
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          v[i] = (vis >> i) & 1u ? tc::ex2(fmaf(v[i], tc::kLog2e, -offset)) : 0.f;
+          for (int i = 0; i < 32; ++i) v[i] = half ? v1[i] : v0[i];
+        } else {
+          tc::ld32(s_addr + 64 * cq + 32 * half, v);
+          const uint32_t vis = rg.visible_bits(col0);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            v[i] = (vis >> i) & 1u ? tc::ex2(fmaf(v[i], tc::kLog2e, -offset)) : 0.f;
+        }
         // P (bf16): 16-byte chunks 4 half .. 4 half + 3 of row m of sub-tile cq.
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -585,8 +603,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // aggregated by warp r for row r.
   const bool rank_keys = a.identity;
   if (!rank_keys) {
-    if (warp < kTcRows && q0 + warp < a.Q) {
-      const RowGeo wr = row_geo(a, a.positions[q0 + warp]);
+    if (ranks_row) {
+      const RowGeo wr = row_geo(a, rank_pos);
       aggregate_blocks(a, wr, scores + warp * score_len, bscores + warp * a.nb_len, lane);
     }
     __syncthreads();
@@ -604,9 +622,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   // Top-n, warp r for row r: the current block first, then earlier blocks by
   // (score descending, block ascending).
-  if (warp < kTcRows && q0 + warp < a.Q) {
+  if (ranks_row) {
     const int qq = q0 + warp;
-    const RowGeo wr = row_geo(a, a.positions[qq]);
+    const RowGeo wr = row_geo(a, rank_pos);
     const int limit = min(wr.current, ranked_len);
     float* sc = ranked + warp * ranked_len;
     int32_t* brow = a.blocks + ((long long)qq * H + h) * a.width;
