@@ -23,7 +23,7 @@ READ_ORDERS = {
 }
 
 c_i32, c_i64, c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
-ABI_VERSION = 3  # CXS_ABI_VERSION
+ABI_VERSION = 4  # CXS_ABI_VERSION
 # CXS_NOALLOC_MAX_PHYSICAL: most physical blocks cxs_fetch_attend_noalloc
 # takes; its static scratch is 16 bytes per block + 256 (checked against the
 # header by tests/test_abi.py and at compile time in attend.cu).
@@ -81,7 +81,8 @@ class SelectGeometry(ctypes.Structure):
 ATTEND_BUFFER_FIELDS = (
     "query", "kv", "all_ids", "all_counts", "row_positions", "starts", "valid", "flags",
     "ioids", "missing", "address", "sources", "kinds", "ready", "control", "error",
-    "window_kv", "compressed", "gates", "out", "out_peer",
+    "window_kv", "compressed", "gates", "out", "out_peer", "first_depth",
+    "near_consumers",
 )
 
 

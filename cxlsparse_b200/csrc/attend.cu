@@ -54,6 +54,8 @@ struct AttendArgs {
   const int64_t* address;
   const int64_t* sources;
   const int32_t* kinds;
+  const int32_t* first_depth;  // read-order key of every block, or NULL (list order)
+  const int32_t* near;
   int32_t* ready;
   int32_t* control;
   int32_t* error;
@@ -138,6 +140,47 @@ __global__ void prepare_kernel(int P, int BS, const int64_t* __restrict__ addres
 // softmax warp writes the (gate-mixed) output.
 
 // Tiles of one query row, computed alike by both warps of an engine.
+// Position of this lane's selected occurrence in its row's processing order:
+// by the plan's read-order key (first consumption depth, more near consumers
+// first, block), the key the IO warps fetch missing blocks by, so that an
+// engine takes its blocks in the order they arrive; equal keys keep list
+// order. The plan gives every block this key whatever its residency, so the
+// order (and the result) does not depend on which blocks are resident or on
+// arrival times. Without the key (NULL) the order is the list order. Lanes at
+// or beyond `count` keep their own slot. The key packs depth (24 bits),
+// near consumers (16 bits, inverted) and block (24 bits); a field beyond its
+// width saturates, which still gives one fixed order.
+struct SlotFields {
+  int depth = -1, near = 0, block = 0;  // depth -1: no key (list order)
+};
+
+__device__ __forceinline__ SlotFields slot_fields(const AttendArgs& a, int block) {
+  SlotFields f;
+  if (a.first_depth && block >= 0 && block < a.P) {
+    f.depth = a.first_depth[block];
+    f.near = a.near ? a.near[block] : 0;
+    f.block = block;
+  }
+  return f;
+}
+
+__device__ __forceinline__ unsigned long long slot_key(SlotFields f) {
+  if (f.depth < 0) return 0ull;
+  const unsigned long long depth = (unsigned)min(f.depth, 0xffffff);
+  const unsigned long long near = (unsigned)min(max(f.near, 0), 0xffff);
+  return depth << 40 | (0xffffull - near) << 24 | (unsigned)min(f.block, 0xffffff);
+}
+
+__device__ __forceinline__ int process_slot(unsigned long long key, int count, int lane) {
+  int slot = 0;
+#pragma unroll 4
+  for (int j = 0; j < count; ++j) {
+    const unsigned long long kj = __shfl_sync(0xffffffffu, key, j);
+    slot += kj < key || (kj == key && j < lane);
+  }
+  return lane < count ? slot : lane;
+}
+
 struct RowTiles {
   int h, pos, count, n_hist, n_win, total;
   int w_lo, w_hi, o_lo, o_hi;
@@ -223,21 +266,63 @@ __device__ __forceinline__ void engine_warp(const CUtensorMap& kv_map, const CUt
   const int rows = a.Q * a.H;
   for (int row = e * gridDim.x + blockIdx.x; row < rows && !failed; row += a.consumers) {
     const RowTiles rt = row_tiles(a, row);
-    {  // stage the row's selected blocks and their source kinds
+    {  // stage the row's selected blocks and their source kinds, in processing order
       int block = -1, kind = 0;
       if (lane < rt.count) {
         block = a.all_ids[(long long)row * a.W + lane];
         if (block >= 0 && block < a.P) kind = a.kinds[block];
       }
-      ps.blocks()[lane] = block;
-      ps.kinds()[lane] = kind;
+      const int slot = process_slot(slot_key(slot_fields(a, block)), rt.count, lane);
+      ps.blocks()[slot] = block;
+      ps.kinds()[slot] = kind;
     }
     __syncwarp();
     if (lane == 0 && rt.total > 0) {
       const int total = rt.total, n_win = rt.n_win, h = rt.h;
       const int k0 = k_started, v0 = v_started;  // this row's tile j: K copy k0 + j, V copy v0 + j
-      int probe_tile = -1, probe_value = 0;
+      const int count = rt.count;
       auto block_of = [&](int j) { return ps.blocks()[j - n_win]; };
+      // Selected occurrences [0, acq) are acquired (or resident). The ready
+      // flags of the next kProbe are read with relaxed loads a tile before
+      // they are needed (probe_base: first of them, -1: none pending); a
+      // run of them seen set becomes an acquire with one fence.
+      constexpr int kProbe = 4;
+      int acq = 0, probe_base = -1;
+      int probe[kProbe];
+      auto take_probe = [&]() {
+        if (probe_base < 0) return;
+        bool cold = false;
+        while (acq < count) {
+          const int i = acq - probe_base;
+          if (ps.kinds()[acq] == 0) {
+            ++acq;
+            continue;
+          }
+          bool seen = false;
+#pragma unroll
+          for (int q = 0; q < kProbe; ++q) seen |= q == i && probe[q] != 0;
+          if (!seen) break;
+          ++acq;
+          cold = true;
+        }
+        probe_base = -1;
+        if (cold) {
+          cxs::fence_acq_rel_gpu();
+          cxs::fence_proxy_async_global();
+        }
+      };
+      auto issue_probe = [&]() {
+        if (probe_base >= 0 || acq >= count) return;
+        probe_base = acq;
+#pragma unroll
+        for (int q = 0; q < kProbe; ++q) {
+          const int o = acq + q;
+          const int block = o < count ? ps.blocks()[o] : -1;
+          probe[q] = 0;
+          if (block >= 0 && block < a.P && ps.kinds()[o] != 0)
+            probe[q] = cxs::ld_relaxed(&a.ready[block]);
+        }
+      };
       auto copy = [&](int j, bool value) {
         const int b = value ? (v0 + j) % tc::PairSmem::kVBufs : (k0 + j) % tc::PairSmem::kKBufs;
         uint64_t* bar = value ? ps.vbar(b) : ps.kbar(b);
@@ -257,20 +342,19 @@ __device__ __forceinline__ void engine_warp(const CUtensorMap& kv_map, const CUt
         while (k_started - k0 <= upto && k_started - k0 < total) {
           const int j = k_started - k0;
           if (j >= n_win) {
-            const int block = block_of(j);
+            const int o = j - n_win, block = block_of(j);
             if (block < 0 || block >= a.P) {
               atomicOr(a.error, cxs::kErrBadBlock);
               return false;
             }
-            if (ps.kinds()[j - n_win] != 0) {
-              if (probe_tile == j && probe_value) {
-                cxs::fence_acq_rel_gpu();
-              } else if (j <= need) {
-                if (!cxs::wait_ready_bounded(&a.ready[block], spin, a.error)) return false;
-              } else {
-                break;  // not known ready: retry at the next tile
-              }
+            // Every earlier occurrence has started, so acq >= o here.
+            if (o >= acq) take_probe();
+            while (acq < count && acq <= o && ps.kinds()[acq] == 0) ++acq;
+            if (o >= acq) {
+              if (j > need) break;  // not known ready: retry at the next tile
+              if (!cxs::wait_ready_bounded(&a.ready[block], spin, a.error)) return false;
               cxs::fence_proxy_async_global();
+              acq = o + 1;
             }
           }
           copy(j, false);
@@ -355,16 +439,9 @@ __device__ __forceinline__ void engine_warp(const CUtensorMap& kv_map, const CUt
         }
         // V(t): its buffer's last P.V (tile t - 2) was issued a tile ago.
         ok = ok && start_v(t);
-        // Poll the ready flag of the next K copy now; it is read at the next
-        // tile, after its latency has passed.
-        const int next = k_started - k0;
-        if (ok && next < total && next >= n_win && ps.kinds()[next - n_win] != 0) {
-          const int block = block_of(next);
-          if (block >= 0 && block < a.P) {
-            probe_tile = next;
-            probe_value = cxs::ld_relaxed(&a.ready[block]);
-          }
-        }
+        // Poll the next ready flags now; they are read at the next tile,
+        // after their latency has passed.
+        if (ok) issue_probe();
       }
       if (ok) {
         ok = start_v(total - 1) && softmax_arrival(ps.pfull(), pfull_phase) && land(true) &&
@@ -429,7 +506,8 @@ __device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_til
     tc::write_query_row(q_tile, a.query, row, m, lane);
     const RowTiles rt = row_tiles(a, row);
     const int total = rt.total, n_win = rt.n_win, pos = rt.pos;
-    // Lane i holds selected occurrence i's first position.
+    // Lane i holds selected occurrence i's block, first position and slot in
+    // the processing order (the engine warp computes the same slots).
     int my_block = -1, my_start = 0;
     if (lane < rt.count) {
       my_block = a.all_ids[(long long)row * a.W + lane];
@@ -438,14 +516,16 @@ __device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_til
     cxs::fence_proxy_async_shared();
     __syncwarp();
     if (total > 0 && leader) cxs::mbar_arrive(ps.sfree());  // Q written
+    // The order is first needed at the first selected tile, after the window.
+    const int my_slot = process_slot(slot_key(slot_fields(a, my_block)), rt.count, lane);
     float m_run = -INFINITY, l_run = 0.f;
     uint32_t win_packed[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) win_packed[i] = 0;
-    auto window_output = [&]() {  // normalised bf16 output of the window branch
+    auto window_output = [&](float l_win) {  // normalised bf16 output of the window branch
       float o[32];
       tc::combine_o(o_addr, half, o);
-      const float den = l_run > 0.f ? l_run : 1.f;
+      const float den = l_win > 0.f ? l_win : 1.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) win_packed[i] = cxs::pack_bf16(o[2 * i] / den, o[2 * i + 1] / den);
     };
@@ -461,14 +541,8 @@ __device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_til
       tc::fence_before();
       __syncwarp();
       if (t + 1 < total && leader) cxs::mbar_arrive(ps.sfree());  // S(t) read
-      // P.V(t - 1) must be done before P(t) overwrites the P tile, O is
-      // rescaled or the window branch's O is read.
-      if (t > 0 && !agree_wait(ps.obar(), o_phase)) {
-        alive = false;
-        break;
-      }
-      if (t == n_win && n_win > 0) {  // window branch complete: keep its output, restart
-        window_output();
+      const float l_prev = l_run;
+      if (t == n_win && n_win > 0) {  // window branch complete: the selected branch restarts
         m_run = -INFINITY;
         l_run = 0.f;
       }
@@ -476,12 +550,21 @@ __device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_til
       if (t < n_win) {
         hi = min(rt.win_last(t) - rt.win_first(t), tc::kTileRows - 1);
       } else {
-        const int cur_block = __shfl_sync(0xffffffffu, my_block, (t - n_win) & 31);
-        const int cur_start = __shfl_sync(0xffffffffu, my_start, (t - n_win) & 31);
-        if (cur_block >= 0 && cur_block < a.P) hi = min(pos - cur_start, BS - 1);
+        const uint32_t holder = __ballot_sync(0xffffffffu, my_slot == t - n_win);
+        const int src = holder ? __ffs(holder) - 1 : 0;
+        const int cur_block = __shfl_sync(0xffffffffu, my_block, src);
+        const int cur_start = __shfl_sync(0xffffffffu, my_start, src);
+        if (holder && cur_block >= 0 && cur_block < a.P) hi = min(pos - cur_start, BS - 1);
       }
       const float m_old = m_run;
       const float factor = tc::softmax_regs(sv, lo, hi, m_run, l_run, half);
+      // P.V(t - 1) runs under the softmax above; it must be done before P(t)
+      // overwrites the P tile, O is rescaled or the window branch's O is read.
+      if (t > 0 && !agree_wait(ps.obar(), o_phase)) {
+        alive = false;
+        break;
+      }
+      if (t == n_win && n_win > 0) window_output(l_prev);  // keep the window branch's output
       if (!first_of_branch) tc::rescale_o(o_addr, factor, m_old != -INFINITY && factor != 1.f);
       tc::store_p(p_tile, m, half, sv);
       cxs::fence_proxy_async_shared();
@@ -493,7 +576,7 @@ __device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_til
     if (total > 0) {
       if (!agree_wait(ps.obar(), o_phase)) break;  // the last P.V
       if (total == n_win && n_win > 0) {
-        window_output();
+        window_output(l_run);
         l_run = 0.f;
       }
     }
@@ -788,6 +871,8 @@ int launch(const cxs_attend_geometry& g, const cxs_attend_buffers& b, cudaStream
   a.address = b.address;
   a.sources = b.sources;
   a.kinds = b.kinds;
+  a.first_depth = b.first_depth;
+  a.near = b.near_consumers;
   a.ready = b.ready;
   a.control = b.control;
   a.error = b.error;

@@ -422,7 +422,7 @@ extern "C" int cxs_residual_rms_norm(void* hidden, const void* delta, const void
   if (dim % 8 || dim / 8 > 256 * kMaxChunks ||
       (((uintptr_t)hidden | (uintptr_t)delta | (uintptr_t)weight | (uintptr_t)out) & 15))
     return set_error(CXS_ERR_INVALID,
-                     "residual rms_norm needs 16-byte aligned rows of at most %d (dim % 8 == 0)",
+                     "residual rms_norm needs 16-byte aligned rows of at most %d, dim a multiple of 8",
                      8 * 256 * kMaxChunks);
   if (!rows) return CXS_OK;
   residual_rms_norm_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(

@@ -372,8 +372,10 @@ __global__ void occurrences_kernel(Geo g, cxs_plan_buffers b) {
 
 // ------------------------------------------------------ consumption depth ---
 // Depth of each row along its consumer's serial row stream, counting resident
-// steps; first depth at which each missing block is consumed
-// (dependencies.py:47-75).
+// steps; first depth at which each block is consumed (dependencies.py:47-75,
+// which keeps it for missing blocks; resident blocks get it too, so that the
+// attention launch can order every row's blocks by the read-order key
+// whatever their residency).
 __global__ void depth_kernel(Geo g, cxs_plan_buffers b) {
   int r = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   int lane = threadIdx.x % 32;
@@ -388,12 +390,12 @@ __global__ void depth_kernel(Geo g, cxs_plan_buffers b) {
   int count = min(g.W, b.all_counts[r]);
   for (int col = lane; col < count; col += 32) {
     int block = b.all_ids[(long long)r * g.W + col];
-    if (block >= 0 && block < g.P && b.flags[block]) atomicMin(&b.first_depth[block], depth + col);
+    if (block >= 0 && block < g.P) atomicMin(&b.first_depth[block], depth + col);
   }
 }
 
 // Distinct rows consuming a block within NEAR_WINDOW steps of its first depth
-// (dependencies.py:78-112).
+// (dependencies.py:78-112; every block, as for the first depth).
 __global__ void near_kernel(Geo g, cxs_plan_buffers b) {
   int r = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   int lane = threadIdx.x % 32;
@@ -403,7 +405,7 @@ __global__ void near_kernel(Geo g, cxs_plan_buffers b) {
   const int32_t* ids = b.all_ids + (long long)r * g.W;
   for (int col = lane; col < count; col += 32) {
     int block = ids[col];
-    if (block < 0 || block >= g.P || !b.flags[block]) continue;
+    if (block < 0 || block >= g.P) continue;
     int first = b.first_depth[block];
     int depth = depth0 + col;
     if (depth < first || depth >= first + kNearWindow) continue;
@@ -1292,7 +1294,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     if (pos < 0) continue;
     for (int col = lane; col < min(g.W, count); col += 32) {
       const int block = ids[col];
-      if (block >= 0 && block < g.P && b.flags[block]) atomicMin(&cta_first[block], depth + col);
+      if (block >= 0 && block < g.P) atomicMin(&cta_first[block], depth + col);
     }
   }
   if (by_depth && !merged_depth) {
@@ -1307,7 +1309,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const int count = min(g.W, b.all_counts[r]);
       for (int col = lane; col < count; col += 32) {
         const int block = b.all_ids[(long long)r * g.W + col];
-        if (block >= 0 && block < g.P && b.flags[block]) atomicMin(&cta_first[block], depth + col);
+        if (block >= 0 && block < g.P) atomicMin(&cta_first[block], depth + col);
       }
     }
   }
@@ -1328,7 +1330,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const int32_t* ids = b.all_ids + (long long)r * g.W;
       for (int col = lane; col < count; col += 32) {
         const int block = ids[col];
-        if (block < 0 || block >= g.P || !b.flags[block]) continue;
+        if (block < 0 || block >= g.P) continue;
         const int first = b.first_depth[block];
         const int depth = depth0 + col;
         if (depth < first || depth >= first + kNearWindow) continue;

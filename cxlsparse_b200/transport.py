@@ -251,7 +251,9 @@ class GRSelectedTransport:
             kinds=w["kinds"].data_ptr(), ready=w["ready"].data_ptr(),
             control=w["control"].data_ptr(), error=w["error"].data_ptr(),
             window_kv=_lib.ptr(w.get("window_kv")), compressed=_lib.ptr(w.get("compressed")),
-            gates=_lib.ptr(w.get("gates")), out=w["output"].data_ptr())
+            gates=_lib.ptr(w.get("gates")), out=w["output"].data_ptr(),
+            first_depth=w["first_depth"].data_ptr(),
+            near_consumers=w["near_consumers"].data_ptr())
         w["allocated_bytes"] = sum(v.numel() * v.element_size() for v in w.values()
                                    if isinstance(v, torch.Tensor))
         self.workspaces[key] = w

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define CXS_ABI_VERSION 3
+#define CXS_ABI_VERSION 4
 
 enum cxs_status {
   CXS_OK = 0,
@@ -149,8 +149,8 @@ typedef struct cxs_plan_buffers {
   int32_t* row_positions;   /* [R] */
   int32_t* region_counts;   /* [regions] */
   int32_t* row_depth;       /* [R] */
-  int32_t* first_depth;     /* [P] */
-  int32_t* near_consumers;  /* [P] */
+  int32_t* first_depth;     /* [P] first consumption depth of every referenced block */
+  int32_t* near_consumers;  /* [P] near consumers of every referenced block */
   int32_t* chosen;          /* [H, hot] chosen hot indices */
   /* query-private plan only (may be NULL otherwise) */
   int32_t* private_required;    /* [H, CAP] */
@@ -276,6 +276,18 @@ typedef struct cxs_attend_buffers {
   void* out_peer;            /* NULL, or a peer GPU's buffer of the same layout: every
                                 output row is also stored there over NVLink (KV-head
                                 split exchange; see cxs_exchange_barrier) */
+  const int32_t* first_depth;    /* [P] the plan's first consumption depth of every
+                                    block (cxs_plan_buffers.first_depth), or NULL */
+  const int32_t* near_consumers; /* [P] the plan's near-consumer counts, or NULL.
+                                    With first_depth, every row takes its selected
+                                    blocks by the read-order key (first depth, more
+                                    near consumers first, block; ties in list order),
+                                    the key the IO warps fetch missing blocks by, so
+                                    an engine follows the order in which blocks
+                                    arrive. The plan keys every block whatever its
+                                    residency, so the result does not depend on
+                                    residency; it differs from list order (NULL) by
+                                    fp32 summation rounding. */
 } cxs_attend_buffers;
 
 int cxs_fetch_attend(const cxs_attend_geometry* geometry, const cxs_attend_buffers* buffers,

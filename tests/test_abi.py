@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
     assert set(names) == set(_lib.exported_symbols())
     for name in names:
         assert hasattr(lib, name), name
-    assert lib.cxs_abi_version() == _lib.ABI_VERSION == 3
+    assert lib.cxs_abi_version() == _lib.ABI_VERSION == 4
 
 
 def _c_layout(struct, fields):

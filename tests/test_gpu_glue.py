@@ -24,6 +24,27 @@ def test_rms_norm_matches_torch_sequence(cuda, dim):
     torch.testing.assert_close(out.float(), rms_norm(x, w, 1e-6).float(), rtol=0.01, atol=0.01)
 
 
+def test_residual_rms_norm_matches_add_then_norm(cuda):
+    """hidden += delta in bf16 (kept as the new residual), then RMSNorm of the
+    sum: the reference's residual add followed by the next norm."""
+    torch.manual_seed(3)
+    rows, dim = 256, 2048
+    hidden = torch.randn(rows, dim, device=cuda).bfloat16()
+    delta = (0.1 * torch.randn(rows, dim, device=cuda)).bfloat16()
+    w = (torch.rand(dim, device=cuda) + 0.5).bfloat16()
+    expect_h = hidden + delta
+    expect = rms_norm(expect_h, w, 1e-6)
+    out = torch.empty_like(hidden)
+    _lib.check(_lib.lib().cxs_residual_rms_norm(hidden.data_ptr(), delta.data_ptr(), w.data_ptr(),
+                                                out.data_ptr(), rows, dim, 1e-6, _stream()))
+    assert torch.equal(hidden, expect_h)  # the bf16 sum, bit for bit
+    torch.testing.assert_close(out.float(), expect.float(), rtol=0.01, atol=0.01)
+    with pytest.raises(ValueError, match="multiple of 8"):
+        _lib.check(_lib.lib().cxs_residual_rms_norm(hidden.data_ptr(), delta.data_ptr(),
+                                                    w.data_ptr(), out.data_ptr(), rows, 1000 + 4,
+                                                    1e-6, _stream()))
+
+
 def test_qkv_rope_gates_and_packing(cuda):
     torch.manual_seed(1)
     E, qh, kvh = 40, 32, 2

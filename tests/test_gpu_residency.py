@@ -143,8 +143,10 @@ def test_transport_over_partly_resident_blocks(cuda, read_order):
 def test_model_with_replica_matches_frequency_policy(cuda):
     """The same model with a static replica (recent blocks + half-resident
     straddling blocks) instead of the frequency hot set reads the same KV
-    values from other tiers: its extend is bit-identical, and its pool
-    reads are exactly the selected non-resident history tokens."""
+    values from other tiers: its extend is bit-identical (each row takes its
+    selected blocks by the plan's read-order key, which does not depend on
+    residency), and its pool reads are exactly the selected non-resident
+    history tokens."""
     from cxlsparse_b200.model import NSAConfig, NSAExtendModel, residency_pattern
 
     cfg = NSAConfig(layers=2, hot=64)

@@ -7,7 +7,8 @@ own suffix) and the gate mix. Checked against the CPU oracle run per
 candidate in true positions (rtol = atol = 0.03, the reference's tolerance,
 tests/test_nsa_tma_transport.py:39-41), selections bit-exactly against the
 ordering rule applied to the kernel's own scores, rotations of the
-candidates over the segments bit-exactly at the transport level, and, end
+candidates over the segments at the transport level (bit-exactly for the
+window branch, to summation rounding where selected blocks enter), and, end
 to end, a segmented extend of the model against separate single-candidate
 extends (statistically: the batch shapes differ, see that test).
 """
@@ -156,8 +157,9 @@ def test_transport_segments_match_each_candidate(cuda, history, extend, candidat
     """Each candidate's selected / window / mixed output against the FP64 /
     fp32 oracle in its true positions; cold history fetched once for all
     candidates; and rotating the candidates over the segments rotates the
-    outputs bit for bit (a candidate's result does not depend on its
-    segment index)."""
+    outputs (a candidate's result does not depend on its segment index: bit
+    for bit for the window branch, to summation rounding where selected
+    blocks enter)."""
     case = _segment_case(history=history, extend=extend, candidates=candidates, bs=bs,
                          window=window, width=width)
     layout, extend = case["layout"], case["extend"]
@@ -207,7 +209,14 @@ def test_transport_segments_match_each_candidate(cuda, history, extend, candidat
             rot_gates = gates.view(n, extend, *gates.shape[1:]).roll(-1, 0).flatten(0, 1)
             out_rot, _ = run(rotated, rot_gates.contiguous())
             expected_rot = out.view(n, extend, *out.shape[1:]).roll(-1, 0).flatten(0, 1)
-            assert torch.equal(out_rot, expected_rot)
+            if mode == "window":  # no selected block enters: bit for bit
+                assert torch.equal(out_rot, expected_rot)
+            else:
+                # Each row takes its selected blocks in the plan's IO-rank
+                # order; with more rows than attention engines that order
+                # follows the rows' placement, so the rotated outputs agree
+                # to fp32 summation rounding (a bf16 ulp or two).
+                torch.testing.assert_close(out_rot, expected_rot, rtol=0.01, atol=2e-3)
     finally:
         transport.close()
         case["pool"].close()
