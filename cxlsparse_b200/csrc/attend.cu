@@ -136,8 +136,8 @@ __global__ void prepare_kernel(int P, int BS, const int64_t* __restrict__ addres
 // One engine (a warp pair, tile_tc.cuh) per query row at a time: rows
 // e * gridDim.x + blockIdx.x + k * consumers for engine e of the CTA. Per row
 // the sliding-window tiles come first, then the row's selected occurrences
-// in list order (duplicates attended again, as the reference does); the
-// softmax warp writes the (gate-mixed) output.
+// by the plan's read-order key (duplicates attended again, as the reference
+// does); the softmax warp writes the (gate-mixed) output.
 
 // Tiles of one query row, computed alike by both warps of an engine.
 // Position of this lane's selected occurrence in its row's processing order:
@@ -573,6 +573,19 @@ __device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_til
       if (leader) cxs::mbar_arrive(ps.pfull());  // P(t) written
     }
     if (!alive) break;
+    // The gate-mix inputs load while the last P.V completes.
+    const long long off = ((long long)row * 16 + (lane & 15)) * 64 + 32 * half;
+    float g0 = 0.f, g1 = 0.f, g2 = 0.f;
+    uint4 cmp[4];
+    if (a.gate) {
+      const __nv_bfloat16* gp = a.gates + ((long long)row * 16 + (lane & 15)) * 3;
+      g0 = __bfloat162float(gp[0]);
+      g1 = __bfloat162float(gp[1]);
+      g2 = __bfloat162float(gp[2]);
+      const uint4* src = reinterpret_cast<const uint4*>(a.compressed + off);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) cmp[c] = src[c];
+    }
     if (total > 0) {
       if (!agree_wait(ps.obar(), o_phase)) break;  // the last P.V
       if (total == n_win && n_win > 0) {
@@ -587,7 +600,6 @@ __device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_til
 #pragma unroll
       for (int i = 0; i < 32; ++i) o[i] = 0.f;
     }
-    const long long off = ((long long)row * 16 + (lane & 15)) * 64 + 32 * half;
     const float den = l_run > 0.f ? l_run : 1.f;
     const long long out_row = (long long)(row / a.H) * a.out_heads + a.out_head0 + row % a.H;
     const long long ooff = (out_row * 16 + (lane & 15)) * 64 + 32 * half;
@@ -606,10 +618,6 @@ __device__ __forceinline__ void softmax_warp(const AttendArgs& a, uint8_t* q_til
       }
     } else {
       // Gate mix in the reference's bf16 rounding sequence (model.py:470-473).
-      const __nv_bfloat16* gp = a.gates + ((long long)row * 16 + (lane & 15)) * 3;
-      const float g0 = __bfloat162float(gp[0]), g1 = __bfloat162float(gp[1]),
-                  g2 = __bfloat162float(gp[2]);
-      const uint4* cmp = reinterpret_cast<const uint4*>(a.compressed + off);
       const bool have_window = a.window > 0 && pos >= 0;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
