@@ -37,7 +37,7 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # ncu --set full capture (NVTX range profile_step). The staged and window KV
 # stay in L2, so DRAM sees far less than the algorithmic bytes. A recorded
 # figure, not measured by this run: NCU_TRAFFIC_SOURCE names the capture.
-NCU_DRAM_BYTES_PER_LAUNCH = 2.94e6
+NCU_DRAM_BYTES_PER_LAUNCH = 3.74e6  # mean of the two captured launches
 NCU_TRAFFIC_SOURCE = ("recorded, not measured by this run: ncu capture summarised in "
                       "profiles/fetch_attend_h16k_e256_ncu.md")
 
