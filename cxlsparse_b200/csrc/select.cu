@@ -228,8 +228,15 @@ constexpr int kTcTmemCols = 512;                    // S (256) + O (64), power o
 constexpr int kTcMaxScores = 2048;                  // per-row score slots in shared memory
 constexpr int kTcReduceBytes = 2 * 4 * 128 * 4;     // per-quarter row max / sum
 
-size_t tc_smem_bytes(int kres, int score_len, int nb_len) {
-  return 1024 + (size_t)kTcQBytes + 2 * (size_t)kres * kTcChunkBytes + kTcPBytes +
+// Bytes of the K (or V) staging region: one chunk buffer, or with several
+// chunks resident (kres > 1) the tiles of every summary, chunk j at
+// j * kTcChunkBytes (only the last chunk is partial).
+__host__ __device__ __forceinline__ size_t tc_kv_region(int kres, int summaries) {
+  return kres > 1 ? (size_t)((summaries + 63) / 64) * kTcTileBytes : (size_t)kTcChunkBytes;
+}
+
+size_t tc_smem_bytes(int kres, int summaries, int score_len, int nb_len) {
+  return 1024 + (size_t)kTcQBytes + 2 * tc_kv_region(kres, summaries) + kTcPBytes +
          kTcReduceBytes + (size_t)kTcRows * (score_len + nb_len) * 4 + 64;
 }
 
@@ -304,8 +311,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int rank_pos = ranks_row ? a.positions[q0 + warp] : 0;
   uint8_t* q_tile = smem;
   uint8_t* k_base = q_tile + kTcQBytes;
-  uint8_t* v_base = k_base + kres * kTcChunkBytes;
-  uint8_t* p_tile = v_base + kres * kTcChunkBytes;
+  uint8_t* v_base = k_base + tc_kv_region(kres, C);
+  uint8_t* p_tile = v_base + tc_kv_region(kres, C);
   float* red_max = reinterpret_cast<float*>(p_tile + kTcPBytes);  // [4][128]
   float* red_sum = red_max + 4 * 128;                               // [4][128]
   // Per-row key scores [kTcRows][score_len] and block scores
@@ -325,6 +332,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // their own complete-block count), so the copies can start at once.
   const int chunks = (C + kTcChunk - 1) / kTcChunk;
   const bool resident = chunks <= kres;  // K and V of every chunk stay in shared memory
+  // Two chunks whose second holds at most 192 summaries (H = 16384 with the
+  // extend's new blocks gives 260): both S chunks stay in TMEM (columns
+  // [0, 256) and [256, 448), O in [448, 512)), computed once for both passes.
+  const bool s_resident = resident && chunks == 2 && C <= kTcChunk + 192;
+  auto s_of = [&](int j) { return s_resident ? (uint32_t)(kTcChunk * j) : 0u; };
   auto tiles_of = [&](int j) { return min(4, (C - kTcChunk * j + 63) / 64); };
   auto load_half = [&](int j, uint8_t* dst, int channel) {
     for (int t = 0; t < tiles_of(j); ++t)
@@ -384,7 +396,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_off = (uint32_t)(32 * lg) << 16;
-  const uint32_t s_col = tmem, o_col = tmem + kTcChunk;
+  const uint32_t s_col = tmem, o_col = tmem + (s_resident ? 448 : kTcChunk);
   const uint32_t s_addr = s_col + lane_off, o_addr = o_col + lane_off;
   const uint32_t q_addr = cxs::smem_addr(q_tile), p_addr = cxs::smem_addr(p_tile);
   const long long spin = 1ll << 31;
@@ -405,15 +417,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     ok = __syncthreads_and(done);
     tc::fence_after();
   };
-  auto mma_scores = [&](int j) {  // S = Q . K_j^T, N = 64 x tiles
+  auto mma_scores = [&](int j) {  // S = Q . K_j^T, N = 64 x tiles (both chunks if TMEM-resident)
     if (tid == 0) {
       tc::fence_after();
-      const uint32_t ka = cxs::smem_addr(k_of(j));
-      const uint32_t id = tc::idesc_bf16(128, 64 * tiles_of(j), 0, 0);
+      for (int c = j; c < (s_resident ? chunks : j + 1); ++c) {
+        const uint32_t ka = cxs::smem_addr(k_of(c));
+        const uint32_t id = tc::idesc_bf16(128, 64 * tiles_of(c), 0, 0);
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        tc::mma(s_col, tc::desc_sw128(q_addr + 32 * k, 16, 1024),
-                tc::desc_sw128(ka + 32 * k, 16, 1024), id, k);
+        for (int k = 0; k < 4; ++k)
+          tc::mma(s_col + s_of(c), tc::desc_sw128(q_addr + 32 * k, 16, 1024),
+                  tc::desc_sw128(ka + 32 * k, 16, 1024), id, k);
+      }
       tc::commit(mma_bar);
     }
     wait_mma();
@@ -439,13 +453,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (j == 0 || !resident) wait_tma();
     if (!ok) break;
-    mma_scores(j);
+    if (!s_resident || j == 0) mma_scores(j);
     // This warp's column groups (32 columns each) of the chunk: 2 cq, 2 cq + 1.
     const bool mine = cq < tiles_of(j);
     const int col0 = kTcChunk * j + 64 * cq;
     if (mine) {  // warp-uniform
-      tc::ld32(s_addr + 64 * cq, v0);
-      tc::ld32(s_addr + 64 * cq + 32, v1);
+      tc::ld32(s_addr + s_of(j) + 64 * cq, v0);
+      tc::ld32(s_addr + s_of(j) + 64 * cq + 32, v1);
     }
     float mt = -INFINITY;
     const uint32_t vis0 = rg.visible_bits(col0), vis1 = rg.visible_bits(col0 + 32);
@@ -490,7 +504,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
   float* my_scores = scores + ql * score_len;
   for (int j = 0; j < chunks && ok; ++j) {
-    if (chunks > 1) {
+    if (chunks > 1 && !s_resident) {
       if (!resident) {
         if (tid == 0) {
           cxs::mbar_expect_tx(tma_bar, 2 * tiles_of(j) * kTcTileBytes);
@@ -512,7 +526,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = half ? v1[i] : v0[i];
         } else {
-          tc::ld32(s_addr + 64 * cq + 32 * half, v);
+          tc::ld32(s_addr + s_of(j) + 64 * cq + 32 * half, v);
           const uint32_t vis = rg.visible_bits(col0);
 #pragma unroll
           for (int i = 0; i < 32; ++i)
@@ -778,16 +792,16 @@ extern "C" int cxs_compressed_select_nsa(const cxs_select_geometry* geometry, co
   const int grid = ((queries + kTcRows - 1) / kTcRows) * heads;
   int chunks = (summaries + kTcChunk - 1) / kTcChunk;
   int kres = chunks <= kTcMaxResident ? (chunks > 0 ? chunks : 1) : 1;
-  if (kres > 1 && tc_smem_bytes(kres, score_len, a.nb_len) > (size_t)kMaxSmem) kres = 1;
-  size_t tc_smem = tc_smem_bytes(kres, score_len, a.nb_len);
+  if (kres > 1 && tc_smem_bytes(kres, summaries, score_len, a.nb_len) > (size_t)kMaxSmem) kres = 1;
+  size_t tc_smem = tc_smem_bytes(kres, summaries, score_len, a.nb_len);
   if (score_len > kTcMaxScores || tc_smem > (size_t)kMaxSmem) {
     // Long key lists: the score rows go to the device's global scratch.
     const size_t need = (size_t)grid * kTcRows * (score_len + a.nb_len) * sizeof(float);
     int status = score_scratch(device, need, (cudaStream_t)stream, &a.row_scores);
     if (status != CXS_OK) return status;
-    kres = chunks <= kTcMaxResident && tc_smem_bytes(chunks, 0, 0) <= (size_t)kMaxSmem
+    kres = chunks <= kTcMaxResident && tc_smem_bytes(chunks, summaries, 0, 0) <= (size_t)kMaxSmem
                ? (chunks > 0 ? chunks : 1) : 1;
-    tc_smem = tc_smem_bytes(kres, 0, 0);
+    tc_smem = tc_smem_bytes(kres, summaries, 0, 0);
   }
   compressed_select_tc_kernel<<<grid, kTcThreads, tc_smem, (cudaStream_t)stream>>>(map, a, kres);
   CXS_LAUNCH_CHECK("compressed_select_tc_kernel");
