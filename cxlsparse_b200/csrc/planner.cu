@@ -519,9 +519,12 @@ __global__ void __launch_bounds__(kChunk) chunk_compact_kernel(Geo g, cxs_plan_b
 // maximum, keep every larger frequency and the lowest-index ties (an ordered
 // warp-segmented gather), then sort the `hot` winners (rank counting up to
 // 1024 of them, a block radix sort above). Histograms use warp-aggregated
-// shared atomics because most frequencies share a few small values.
+// shared atomics because most frequencies share a few small values. When the
+// table fits (`staged`), one pass with eight loads in flight per thread copies
+// it into shared memory (after the sort storage) and every later pass reads
+// it there instead of making a round of dependent global loads per stride.
 template <int ITEMS>
-__global__ void __launch_bounds__(1024) hot_select_kernel(Geo g, cxs_plan_buffers b) {
+__global__ void __launch_bounds__(1024) hot_select_kernel(Geo g, cxs_plan_buffers b, int staged) {
   typedef cub::BlockRadixSort<unsigned long long, 1024, ITEMS> Sort;
   typedef cub::BlockReduce<unsigned int, 1024> Reduce;
   extern __shared__ __align__(16) unsigned char sort_mem[];
@@ -536,7 +539,27 @@ __global__ void __launch_bounds__(1024) hot_select_kernel(Geo g, cxs_plan_buffer
   const int32_t* freq = b.frequencies + (long long)h * g.SORT;
   int n = g.SORT;
   unsigned int local_max = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) local_max = max(local_max, (unsigned)freq[i]);
+  if (staged) {
+    constexpr size_t kTemp = (sizeof(typename Sort::TempStorage) + 15) & ~size_t(15);
+    int32_t* stage = reinterpret_cast<int32_t*>(sort_mem + kTemp);
+    for (int base = 0; base < n; base += 8 * 1024) {
+      int v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = base + k * 1024 + threadIdx.x;
+        v[k] = i < n ? freq[i] : 0;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = base + k * 1024 + threadIdx.x;
+        if (i < n) stage[i] = v[k];
+        local_max = max(local_max, (unsigned)v[k]);
+      }
+    }
+    freq = stage;
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) local_max = max(local_max, (unsigned)freq[i]);
+  }
   unsigned int fmax = Reduce(reduce).Reduce(local_max, cub::Max());
   if (threadIdx.x == 0) {
     max_s = fmax;
@@ -1459,10 +1482,17 @@ int launch_publish(const Geo& g, const cxs_plan_buffers& b, unsigned long long b
 
 template <int ITEMS>
 int launch_hot(const Geo& g, const cxs_plan_buffers& b, cudaStream_t stream) {
-  size_t smem = sizeof(typename cub::BlockRadixSort<unsigned long long, 1024, ITEMS>::TempStorage);
+  const size_t temp =
+      (sizeof(typename cub::BlockRadixSort<unsigned long long, 1024, ITEMS>::TempStorage) + 15) &
+      ~size_t(15);
+  // Stage the frequency table in shared memory when it fits beside the sort
+  // storage and the kernel's static arrays (kMaxHot candidates, histograms).
+  const size_t table = (size_t)g.SORT * sizeof(int32_t);
+  const bool staged = temp + table + kMaxHot * sizeof(unsigned long long) + 8192 <= 200 * 1024;
+  const size_t smem = staged ? temp + table : temp;
   CXS_CUDA(cudaFuncSetAttribute(hot_select_kernel<ITEMS>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  hot_select_kernel<ITEMS><<<g.H, 1024, smem, stream>>>(g, b);
+  hot_select_kernel<ITEMS><<<g.H, 1024, smem, stream>>>(g, b, staged ? 1 : 0);
   CXS_LAUNCH_CHECK("hot_select_kernel");
   return CXS_OK;
 }
